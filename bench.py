@@ -1,0 +1,437 @@
+#!/usr/bin/env python
+"""Benchmark of the Mantle graph hot path on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W] [--impl ours|reference]
+
+A step is one replay (`run`) of the recorded graph of the workload over its
+synthetic inputs. The default workload is the two-scatters-plus-three-updates
+graph: two scatter-adds of 2^24 Float32 values by uniform Int32 index into
+2^16 bins (an Int32 histogram fused into the first), then three in-place
+updates with read-after-write hazards on a Float32[2^20] buffer. `value` is
+whole-job algorithmic GB/s: (16 B per scattered element + 36 B per updated
+element) x ranks / max-over-ranks time per step. The inputs (256 MiB per
+replay) are larger than the 126 MB L2, so no flush is needed between steps;
+the bins and the update buffers are L2-resident by design.
+
+`--workload chain` runs the eight-kernel elementwise chain (N=2^22) instead.
+
+Multi-GPU (torchrun, one process per GPU): every rank replays its own
+independent graph on its own seeded data ("scaling": "weak"); no collective
+touches the data path. The barrier and the max-over-ranks reduction of the
+device-timed step go through torch.distributed (NCCL).
+
+`--impl reference` times the CPU restatement of the same workload (the oracle,
+C + OpenMP on all host cores) — the reference itself is Julia on Vulkan and
+cannot run here. Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mantle.jl_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+BASELINE_METRIC = "replayed-graph GB/s & TFLOP/s vs roofline; DNN images/sec at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ── clocks during the timed region (NVML, read only) ────────────────────────
+class ClockSampler:
+    """Samples SM clock and throttle reasons every few ms while running."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: clocks are reported as unavailable
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(0.005)
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+        return False
+
+    def summary(self) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ── distributed plumbing ────────────────────────────────────────────────────
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, x: float) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def finish(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ── timing helpers ──────────────────────────────────────────────────────────
+def device_time_ms(stream_ptr: int, fn, steps: int) -> float:
+    """CUDA events on the stream the work is launched on; sync on both sides."""
+    import torch
+    s = torch.cuda.ExternalStream(stream_ptr)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(s)
+    for _ in range(steps):
+        fn()
+    b.record(s)
+    b.synchronize()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+_PINNED: list = []
+
+
+def pinned_like(a: np.ndarray) -> np.ndarray:
+    """A copy of `a` in page-locked host memory (kept alive for the process)."""
+    import torch
+    t = torch.empty(a.shape, dtype=getattr(torch, str(a.dtype)), pin_memory=True)
+    _PINNED.append(t)
+    out = t.numpy()
+    out[...] = a
+    return out
+
+
+# ── CPU baseline (oracle) ───────────────────────────────────────────────────
+def cpu_scatter_step(inp: dict, nbins: int, threads: int, frac: float = 1.0):
+    """One step of the workload on the CPU: two scatters + histogram + three
+    updates, float32 with private per-thread bins (oracle/mantle_oracle.c)."""
+    import ctypes as C
+
+    from oracle import oracle as O
+    lib = O.lib()
+    n = int(inp["ia"].size * frac)
+    nu = int(inp["b"].size * frac)
+    st = cpu_scatter_step.__dict__.setdefault("scratch", {})
+    key = (threads, nbins)
+    if key not in st:
+        st[key] = (np.empty(threads * nbins, np.float32), np.empty(threads * nbins, np.uint32),
+                   np.empty(nbins, np.float32), np.empty(nbins, np.float32), np.empty(nbins, np.uint32))
+    sf, su, acc_a, acc_b, hist = st[key]
+    f32p, i32p, u32p = C.POINTER(C.c_float), C.POINTER(C.c_int32), C.POINTER(C.c_uint32)
+    P = lambda a, t: a.ctypes.data_as(t)  # noqa: E731
+    lib.oracle_scatter_f32(P(inp["va"], f32p), P(inp["ia"], i32p), n, nbins, P(acc_a, f32p), P(hist, u32p),
+                           P(sf, f32p), P(su, u32p), threads)
+    lib.oracle_scatter_f32(P(inp["vb"], f32p), P(inp["ib"], i32p), n, nbins, P(acc_b, f32p), None,
+                           P(sf, f32p), P(su, u32p), threads)
+    b = inp["b_work"]
+    lib.oracle_touch3(P(b, f32p), P(inp["c"], f32p), P(inp["d"], f32p), nu, threads)
+    return 16 * n + 36 * nu
+
+
+def cpu_baseline_scatter(inp: dict, nbins: int, budget_s: float = 10.0) -> dict:
+    from oracle import oracle as O
+    threads = O.max_threads()
+    inp = dict(inp)
+    inp["b_work"] = inp["b"].copy()
+    cpu_scatter_step(inp, nbins, threads)  # warm
+    t0 = time.perf_counter()
+    nbytes = steps = 0
+    while time.perf_counter() - t0 < budget_s:
+        nbytes += cpu_scatter_step(inp, nbins, threads)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} full steps (2x 2^{int(np.log2(inp['ia'].size))} scatter + histogram + "
+                      f"3 updates on 2^{int(np.log2(inp['b'].size))}) in {dt:.1f} s"}
+
+
+# ── workloads ───────────────────────────────────────────────────────────────
+def bench_scatter(args, ws, rank, local, peaks, peak_kind):
+    import torch
+
+    import mantle_cuda as M
+    from mantle_cuda.workloads import build_scatter
+
+    dev = M.Device(local)
+    w = build_scatter(dev, rank=rank)
+    plan = w.plan
+    stream = dev.stream
+
+    for _ in range(args.warmup):
+        M.run(plan)
+    dev.synchronize()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = device_time_ms(stream, lambda: M.run(plan), args.steps)
+    ms_step = max_over_ranks(ws, ms / args.steps)
+    value = ws * w.bytes_step / (ms_step * 1e-3) / 1e9
+
+    # The dominant kernel, timed alone on the same stream: scatter a (value +
+    # index per element; histogram fused).
+    B = w.bufs
+    kargs = (B["acc_a"], B["hist"], B["va"], B["ia"], w.nbins, 0)
+    wsb = M.workspace_bytes(M.kernels.scatter_add, kargs, w.n)
+    scratch = torch.empty(max(wsb, 16), dtype=torch.uint8, device=f"cuda:{local}")
+    launch = lambda: M.launch(M.kernels.scatter_add, kargs, w.n, stream=stream, workspace=scratch)  # noqa: E731
+    for _ in range(3):
+        launch()
+    kreps = max(10, min(args.steps, 200))
+    k_ms = device_time_ms(stream, launch, kreps) / kreps
+    algo_bytes = 8 * w.n
+    achieved = algo_bytes / (k_ms * 1e-3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "scatter_add_traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    roofline = {"bound": "hbm", "kernel": "scatter_add (scatter a: 2^24 values -> 2^16 bins + histogram)",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "algorithmic_bytes": algo_bytes, "peak_kind": f"{peak_kind} (burst copy)",
+                "kernel_ms": round(k_ms, 4)}
+
+    # End to end through the public API: each step the four input arrays go
+    # from pinned host memory through Update, the graph replays, and the bins
+    # come back to the host.
+    w2 = build_scatter(dev, rank=rank, with_updates_from_host=True)
+    host = {k: pinned_like(w2.inputs[k]) for k in ("va", "ia", "vb", "ib")}
+    h2d = sum(v.nbytes for v in host.values())
+    outs = {k: np.empty(w2.nbins, np.float32 if k != "hist" else np.int32) for k in ("acc_a", "acc_b", "hist")}
+    d2h = sum(v.nbytes for v in outs.values())
+
+    def e2e_step():
+        for k, v in host.items():
+            w2.refs[k](v)
+        M.run(w2.plan)
+        for k, o in outs.items():
+            M.lib().mtl_buffer_download(w2.bufs[k].handle, o.ctypes.data, 0, o.nbytes)
+
+    for _ in range(2):
+        e2e_step()
+    dev.synchronize()
+    barrier(ws)
+    e2e_steps = max(3, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    dev.synchronize()
+    e2e_s = max_over_ranks(ws, (time.perf_counter() - t0) / e2e_steps)
+    e2e = {"value": round(ws * w2.bytes_step / e2e_s / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_s * 1e3, 3)}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_baseline_scatter(w.inputs, w.nbins, budget_s=args.cpu_seconds)
+
+    nk = plan.nkernels()
+    line = {
+        "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
+        "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
+        "config": {"workload": "two scatters + int32 histogram + three RAW updates (bench/two_scatters.jl, "
+                               "bench/three_updates.jl shape)",
+                   "scatter_elements": w.n, "bins": w.nbins, "update_elements": w.nupd,
+                   "graph": "5 passes, replayed as one CUDA graph", "parallelism": f"{ws} independent graphs",
+                   "l2": "inputs (256 MiB/step) exceed the 126 MB L2; no flush"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": nk * args.steps, "kernels_per_step": nk, "clocks": clk.summary(),
+    }
+    return line
+
+
+def bench_chain(args, ws, rank, local, peaks, peak_kind):
+    import mantle_cuda as M
+    from mantle_cuda.workloads import build_chain
+
+    dev = M.Device(local)
+    # The unfused eight-kernel graph, and the same graph compiled with fusion.
+    w = build_chain(dev, seed=rank, fuse=not args.unfused)
+    for _ in range(args.warmup):
+        M.run(w.plan)
+    dev.synchronize()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = device_time_ms(dev.stream, lambda: M.run(w.plan), args.steps)
+    ms_step = max_over_ranks(ws, ms / args.steps)
+    nbytes = w.bytes_unfused if args.unfused else w.bytes_compulsory
+    value = ws * nbytes / (ms_step * 1e-3) / 1e9
+    nk = w.plan.nkernels()
+    line = {
+        "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded PCG64, x,y,z U[-1,1]",
+        "config": {"workload": "elementwise chain, 8 dependent kernels" + (" (unfused)" if args.unfused else " (fused)"),
+                   "n": w.n, "bytes_per_step": nbytes, "l2": "inputs 48 MiB + output 16 MiB per step"},
+        "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None},
+        "gpu_launches": nk * args.steps, "clocks": clk.summary(),
+    }
+    return line
+
+
+def reference_arm(args, ws, rank):
+    """The CPU restatement of the same workload on all host cores."""
+    if rank != 0:
+        return None
+    from mantle_cuda.workloads import seeded_integers, seeded_uniform
+    n, nbins, nupd = 1 << 24, 1 << 16, 1 << 20
+    inp = {"va": seeded_uniform(0, n, 0, 1, 0), "ia": seeded_integers(0, n, nbins, 1),
+           "vb": seeded_uniform(0, n, 0, 1, 2), "ib": seeded_integers(0, n, nbins, 3),
+           "b": seeded_uniform(0, nupd, -1, 1, 4), "c": seeded_uniform(0, nupd, -1, 1, 5),
+           "d": seeded_uniform(0, nupd, -1, 1, 6)}
+    from oracle import oracle as O
+    threads = O.max_threads()
+    inp["b_work"] = inp["b"].copy()
+    # Size each step so the whole run stays within about a minute.
+    t0 = time.perf_counter()
+    cpu_scatter_step(inp, nbins, threads)
+    t1 = time.perf_counter() - t0
+    total = args.steps + args.warmup
+    frac = min(1.0, 60.0 / max(total * t1, 1e-9))
+    for _ in range(args.warmup):
+        cpu_scatter_step(inp, nbins, threads, frac)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += cpu_scatter_step(inp, nbins, threads, frac)
+    dt = time.perf_counter() - t0
+    v = nbytes / dt / 1e9
+    return {
+        "metric": BASELINE_METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32", "impl": "reference",
+        "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
+        "config": {"workload": "two scatters + int32 histogram + three RAW updates", "scatter_elements": n,
+                   "bins": nbins, "update_elements": nupd, "fraction_per_step": round(frac, 4)},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps of {frac:.3f} x the workload (oracle/mantle_oracle.c, "
+                                   "float32 private bins, OpenMP)"},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["scatter", "chain"], default="scatter")
+    ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = reference_arm(args, ws, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    ws, rank, local = dist_init()
+    peaks, peak_kind = load_peaks()
+    try:
+        if args.workload == "chain":
+            line = bench_chain(args, ws, rank, local, peaks, peak_kind)
+        else:
+            line = bench_scatter(args, ws, rank, local, peaks, peak_kind)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        finish(ws)
+
+
+if __name__ == "__main__":
+    main()

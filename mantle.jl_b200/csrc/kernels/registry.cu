@@ -1,0 +1,197 @@
+// The table of built-in kernel families a dispatch can name, with their
+// argument signatures, the bounds checks run before any launch, and the
+// launchers.
+
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "../mtl_internal.hpp"
+
+namespace mtl {
+
+int (*ew_emit_fn(const char* name))(const LaunchArgs&, std::vector<EwOp>&, int*, int*, int*);
+mtl_status scatter_check(const LaunchArgs& la, const uint64_t* bytes);
+uint64_t scatter_workspace(const LaunchArgs& la);
+mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+
+// ── checks ──────────────────────────────────────────────────────────────────
+static int64_t nd_total(const LaunchArgs& la) {
+  int64_t t = 1;
+  for (int i = 0; i < la.ndim; ++i) t *= la.nd[i];
+  return t;
+}
+
+// Every buffer argument of an elementwise kernel is indexed 0..n-1.
+static mtl_status check_elementwise(const LaunchArgs& la, const uint64_t* bytes) {
+  const int64_t n = nd_total(la);
+  for (size_t i = 0; i < la.a.size(); ++i) {
+    if (la.a[i].kind != MTL_ARG_PTR) continue;
+    if (bytes[i] && bytes[i] < (uint64_t)n * 4)
+      return fail(MTL_ERR_ARGUMENT,
+                  "elementwise kernel: buffer argument %zu has %llu bytes but the ndrange covers "
+                  "%lld Float32 elements",
+                  i + 1, (unsigned long long)bytes[i], (long long)n);
+  }
+  return MTL_OK;
+}
+
+// ── fill_span!(dst, base, v): dst[base + i] = v   test/test_window.jl:386-389 ─
+__global__ void fill_span_kernel(float* dst, int64_t base, float v, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) dst[base + i] = v;
+}
+static mtl_status check_fill_span(const LaunchArgs& la, const uint64_t* bytes) {
+  const int64_t n = nd_total(la);
+  const int64_t base = la.a[1].i32;
+  if (base < 0) return fail(MTL_ERR_ARGUMENT, "fill_span: negative base");
+  if (bytes[0] && bytes[0] < (uint64_t)(base + n) * 4)
+    return fail(MTL_ERR_ARGUMENT, "fill_span: writes elements %lld..%lld of a %llu-element buffer",
+                (long long)base + 1, (long long)(base + n), (unsigned long long)(bytes[0] / 4));
+  return MTL_OK;
+}
+static mtl_status run_fill_span(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  const int64_t n = nd_total(la);
+  if (n <= 0) return MTL_OK;
+  int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)la.sm_count * 8);
+  fill_span_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<float*>(la.a[0].ptr), la.a[1].i32, la.a[2].f32, n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "fill_span: %s", cudaGetErrorString(e));
+}
+
+// ── counters: bump_counter!(c) and clear_and_tally!(c, tally) ───────────────
+// test/test_window.jl:334-341: every work item adds one to c[1] atomically;
+// the clear writes 0 to c[1] and adds one to tally[1]. Warp-aggregated: one
+// atomic per warp, with the warp's active count.
+__global__ void bump_counter_kernel(uint32_t* c, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    unsigned mask = __activemask();
+    int leader = __ffs(mask) - 1;
+    if ((threadIdx.x & 31) == (unsigned)leader) atomicAdd(c, (uint32_t)__popc(mask));
+  }
+}
+__global__ void clear_and_tally_kernel(uint32_t* c, uint32_t* tally) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    c[0] = 0;
+    atomicAdd(tally, 1u);
+  }
+}
+static mtl_status check_counter(const LaunchArgs& la, const uint64_t* bytes) {
+  for (size_t i = 0; i < la.a.size(); ++i)
+    if (la.a[i].kind == MTL_ARG_PTR && bytes[i] && bytes[i] < 4)
+      return fail(MTL_ERR_ARGUMENT, "counter argument %zu is smaller than one UInt32", i + 1);
+  return MTL_OK;
+}
+static mtl_status run_bump_counter(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  const int64_t n = nd_total(la);
+  if (n <= 0) return MTL_OK;
+  int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)la.sm_count * 8);
+  bump_counter_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<uint32_t*>(la.a[0].ptr), n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "bump_counter: %s", cudaGetErrorString(e));
+}
+static mtl_status run_clear_and_tally(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  clear_and_tally_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(reinterpret_cast<uint32_t*>(la.a[0].ptr),
+                                                              reinterpret_cast<uint32_t*>(la.a[1].ptr));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "clear_and_tally: %s", cudaGetErrorString(e));
+}
+
+// ── the table ───────────────────────────────────────────────────────────────
+#define EW(name, sig, rd, wr) \
+  { name, sig, true, rd, wr, check_elementwise, nullptr, nullptr, nullptr }
+
+static KernelDesc g_kernels[] = {
+    // reference kernels (bench/, test/)
+    EW("stir", "BBf", 0b010, 0b001),
+    EW("mix", "BBBf", 0b0110, 0b0001),
+    EW("keep", "BB", 0b10, 0b01),
+    EW("touch1", "B", 0b1, 0b1),
+    EW("touch2", "BB", 0b11, 0b01),
+    EW("touch3", "BBB", 0b111, 0b001),
+    EW("touch4", "BBBB", 0b1111, 0b0001),
+    EW("bump", "BBf", 0b010, 0b001),
+    EW("scaleby", "BBf", 0b010, 0b001),
+    EW("sched_write", "Bf", 0b00, 0b01),
+    EW("sched_accum", "BB", 0b11, 0b01),
+    // the elementwise chain workload, one op per kernel, and all eight at once
+    EW("axpy", "BBBf", 0b0110, 0b0001),
+    EW("mul", "BBB", 0b110, 0b001),
+    EW("add", "BBB", 0b110, 0b001),
+    EW("sub", "BBB", 0b110, 0b001),
+    EW("fma", "BBBB", 0b1110, 0b0001),
+    EW("abs", "BB", 0b10, 0b01),
+    EW("sqrt_abs", "BB", 0b10, 0b01),
+    EW("scale", "BBf", 0b010, 0b001),
+    EW("chain8", "BBBB", 0b1110, 0b0001),
+    {"fill_span", "Bif", false, 0b000, 0b001, check_fill_span, nullptr, run_fill_span, nullptr},
+    {"bump_counter", "B", false, 0b1, 0b1, check_counter, nullptr, run_bump_counter, nullptr},
+    {"clear_and_tally", "BB", false, 0b10, 0b11, check_counter, nullptr, run_clear_and_tally, nullptr},
+    {"scatter_add", "bbbBii", false, 0b001100, 0b000011, scatter_check, scatter_workspace, scatter_run,
+     nullptr},
+};
+#undef EW
+
+static bool g_init = false;
+static void init_table() {
+  if (g_init) return;
+  for (KernelDesc& k : g_kernels)
+    if (k.elementwise) k.ew_emit = ew_emit_fn(k.name);
+  g_init = true;
+}
+
+const KernelDesc* kernel_desc(int id) {
+  init_table();
+  if (id < 0 || id >= (int)(sizeof g_kernels / sizeof g_kernels[0])) return nullptr;
+  return &g_kernels[id];
+}
+int kernel_count() { return (int)(sizeof g_kernels / sizeof g_kernels[0]); }
+int kernel_find(const char* name) {
+  init_table();
+  for (int i = 0; i < kernel_count(); ++i)
+    if (!strcmp(g_kernels[i].name, name)) return i;
+  return -1;
+}
+
+mtl_status launch_kernel(int kernel, const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream) {
+  const KernelDesc* kd = kernel_desc(kernel);
+  if (!kd) return fail(MTL_ERR_ARGUMENT, "unknown kernel %d", kernel);
+  std::vector<uint64_t> bytes(la.a.size(), 0);
+  for (size_t i = 0; i < la.a.size(); ++i) {
+    bytes[i] = la.a[i].bytes;
+    char c = kd->sig[i];
+    if ((c == 'B') && (la.a[i].kind != MTL_ARG_PTR || la.a[i].ptr == 0))
+      return fail(MTL_ERR_ARGUMENT, "%s: argument %zu must be a device buffer", kd->name, i + 1);
+  }
+  if (kd->check)
+    if (mtl_status s = kd->check(la, bytes.data())) return s;
+  if (kd->elementwise) return ew_launch_single(kd, la, stream);
+  return kd->launch(la, ws, ws_bytes, stream);
+}
+
+}  // namespace mtl
+
+extern "C" {
+
+mtl_status mtl_kernel_lookup(const char* name, int32_t* kernel) {
+  if (!name || !kernel) return mtl::fail(MTL_ERR_ARGUMENT, "mtl_kernel_lookup: NULL argument");
+  int k = mtl::kernel_find(name);
+  if (k < 0) return mtl::fail(MTL_ERR_ARGUMENT, "no built-in kernel named \"%s\"", name);
+  *kernel = k;
+  return MTL_OK;
+}
+
+mtl_status mtl_kernel_info(int32_t kernel, const char** name, const char** signature) {
+  const mtl::KernelDesc* kd = mtl::kernel_desc(kernel);
+  if (!kd) return mtl::fail(MTL_ERR_ARGUMENT, "unknown kernel %d", kernel);
+  if (name) *name = kd->name;
+  if (signature) *signature = kd->sig;
+  return MTL_OK;
+}
+
+int32_t mtl_kernel_count(void) { return mtl::kernel_count(); }
+
+}  // extern "C"

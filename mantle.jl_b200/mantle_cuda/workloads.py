@@ -1,0 +1,148 @@
+"""The graphs of the benchmark workloads, recorded through the public API the
+way the reference's bench/*.jl scripts record theirs.
+
+* elementwise chain: three Float32 vectors, eight dependent kernels
+  (axpy a=0.5, mul, add, fma, abs, sqrt(abs), scale 2, sub) over transients —
+  the multi-pass shape of bench/chain.jl with the op list of the workload.
+* two scatters + three updates: two scatter-adds of Float32 values by Int32
+  index into separate accumulators, one Int32 histogram fused into the first,
+  and three in-place updates (touch1!/touch2!/touch3!, bench/stress.jl:30-45)
+  on one buffer, ordered read-after-write by the derived hazards — the shape of
+  bench/two_scatters.jl and bench/three_updates.jl.
+
+Inputs are synthetic and seeded (numpy PCG64); nothing is read from disk.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import Buffer, Graph, Plan, Transient, Update, compute, dispatch, kernels, use
+
+
+def seeded_uniform(seed: int, n: int, lo: float, hi: float, stream: int = 0) -> np.ndarray:
+    rng = np.random.Generator(np.random.PCG64([seed, stream]))
+    return rng.uniform(lo, hi, n).astype(np.float32)
+
+
+def seeded_integers(seed: int, n: int, hi: int, stream: int = 0) -> np.ndarray:
+    rng = np.random.Generator(np.random.PCG64([seed, stream]))
+    return rng.integers(0, hi, n, dtype=np.int32)
+
+
+# ── elementwise chain ───────────────────────────────────────────────────────
+@dataclass
+class ChainWorkload:
+    n: int
+    x: Buffer
+    y: Buffer
+    z: Buffer
+    out: Buffer
+    graph: Graph
+    plan: Plan
+    inputs: dict = field(default_factory=dict)
+
+    # compulsory bytes of one replay: read x, y, z, write out
+    @property
+    def bytes_compulsory(self) -> int:
+        return 16 * self.n
+
+    # bytes the eight unfused passes move: 12+12+12+16+8+8+8+12 per element
+    @property
+    def bytes_unfused(self) -> int:
+        return 88 * self.n
+
+
+def build_chain(dev, n: int = 1 << 22, seed: int = 0, fuse: bool = False, single_kernel: bool = False,
+                **plan_kw) -> ChainWorkload:
+    x_h = seeded_uniform(seed, n, -1, 1, 0)
+    y_h = seeded_uniform(seed, n, -1, 1, 1)
+    z_h = seeded_uniform(seed, n, -1, 1, 2)
+    x, y, z = Buffer(dev, x_h), Buffer(dev, y_h), Buffer(dev, z_h)
+    out = Buffer(dev, np.float32, n)
+    g = Graph(dev)
+    if single_kernel:
+        compute(g, "chain8", lambda p: dispatch(p, kernels.chain8, (
+            use(p, out, write=True), use(p, x, read=True), use(p, y, read=True), use(p, z, read=True)), n))
+    else:
+        t = [Transient.Buffer(g, np.float32, n) for _ in range(7)]
+        W = lambda p, b: use(p, b, write=True)  # noqa: E731
+        R = lambda p, b: use(p, b, read=True)  # noqa: E731
+        compute(g, "axpy", lambda p: dispatch(p, kernels.axpy, (W(p, t[0]), R(p, x), R(p, y), 0.5), n))
+        compute(g, "mul", lambda p: dispatch(p, kernels.mul, (W(p, t[1]), R(p, t[0]), R(p, z)), n))
+        compute(g, "add", lambda p: dispatch(p, kernels.add, (W(p, t[2]), R(p, t[1]), R(p, y)), n))
+        compute(g, "fma", lambda p: dispatch(p, kernels.fma, (W(p, t[3]), R(p, t[2]), R(p, x), R(p, z)), n))
+        compute(g, "abs", lambda p: dispatch(p, kernels.abs, (W(p, t[4]), R(p, t[3])), n))
+        compute(g, "sqrt", lambda p: dispatch(p, kernels.sqrt_abs, (W(p, t[5]), R(p, t[4])), n))
+        compute(g, "scale", lambda p: dispatch(p, kernels.scale, (W(p, t[6]), R(p, t[5]), 2.0), n))
+        compute(g, "sub", lambda p: dispatch(p, kernels.sub, (W(p, out), R(p, t[6]), R(p, x)), n))
+    plan = Plan(g, fuse=fuse, **plan_kw)
+    return ChainWorkload(n, x, y, z, out, g, plan, {"x": x_h, "y": y_h, "z": z_h})
+
+
+# ── two scatters + histogram + three updates ────────────────────────────────
+@dataclass
+class ScatterWorkload:
+    n: int
+    nbins: int
+    nupd: int
+    bufs: dict
+    graph: Graph
+    plan: Plan
+    inputs: dict
+    refs: dict
+
+    @property
+    def bytes_scatter(self) -> int:
+        """Algorithmic bytes of the two scatters: value + index per element each."""
+        return 16 * self.n
+
+    @property
+    def bytes_updates(self) -> int:
+        """The three updates: 8 + 12 + 16 bytes per element."""
+        return 36 * self.nupd
+
+    @property
+    def bytes_step(self) -> int:
+        return self.bytes_scatter + self.bytes_updates
+
+
+def build_scatter(dev, n: int = 1 << 24, nbins: int = 1 << 16, nupd: int = 1 << 20, seed: int = 0,
+                  rank: int = 0, with_updates_from_host: bool = False, **plan_kw) -> ScatterWorkload:
+    """`rank` offsets the seed streams so every GPU of a multi-GPU run has its
+    own independent graph and data."""
+    s = 10 * rank
+    inputs = {
+        "va": seeded_uniform(seed, n, 0, 1, s + 0),
+        "ia": seeded_integers(seed, n, nbins, s + 1),
+        "vb": seeded_uniform(seed, n, 0, 1, s + 2),
+        "ib": seeded_integers(seed, n, nbins, s + 3),
+        "b": seeded_uniform(seed, nupd, -1, 1, s + 4),
+        "c": seeded_uniform(seed, nupd, -1, 1, s + 5),
+        "d": seeded_uniform(seed, nupd, -1, 1, s + 6),
+    }
+    bufs = {k: Buffer(dev, v) for k, v in inputs.items()}
+    bufs["acc_a"] = Buffer(dev, np.float32, nbins)
+    bufs["acc_b"] = Buffer(dev, np.float32, nbins)
+    bufs["hist"] = Buffer(dev, np.int32, nbins)
+    B = bufs
+    g = Graph(dev)
+    refs = {}
+    if with_updates_from_host:
+        for k in ("va", "ia", "vb", "ib"):
+            refs[k] = Update(g, B[k])
+
+    compute(g, "scatter a", lambda p: dispatch(p, kernels.scatter_add, (
+        use(p, B["acc_a"], write=True), use(p, B["hist"], write=True),
+        use(p, B["va"], read=True), use(p, B["ia"], read=True), nbins, 0), n))
+    compute(g, "scatter b", lambda p: dispatch(p, kernels.scatter_add, (
+        use(p, B["acc_b"], write=True), None,
+        use(p, B["vb"], read=True), use(p, B["ib"], read=True), nbins, 0), n))
+    compute(g, "update 1", lambda p: dispatch(p, kernels.touch1, (use(p, B["b"], read=True, write=True),), nupd))
+    compute(g, "update 2", lambda p: dispatch(p, kernels.touch2, (
+        use(p, B["b"], read=True, write=True), use(p, B["c"], read=True)), nupd))
+    compute(g, "update 3", lambda p: dispatch(p, kernels.touch3, (
+        use(p, B["b"], read=True, write=True), use(p, B["c"], read=True), use(p, B["d"], read=True)), nupd))
+    plan = Plan(g, **plan_kw)
+    return ScatterWorkload(n, nbins, nupd, bufs, g, plan, inputs, refs)

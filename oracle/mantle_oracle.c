@@ -1,0 +1,182 @@
+/*
+ * mantle_oracle.c — CPU restatement of the data-parallel work the Mantle
+ * graphs of this backend carry. TEST INFRASTRUCTURE ONLY: the parity tests,
+ * the smoke check and bench.py's CPU-baseline / reference arm call it as the
+ * checker or as the CPU timing. The product never links or calls it.
+ *
+ * Built with -ffp-contract=off so every expression rounds exactly as written,
+ * in the order written (the GPU kernels use explicit round-to-nearest
+ * intrinsics for the same reason).
+ *
+ * Sources restated:
+ *   touch1!..touch3!   bench/stress.jl:30-45   a = a*1.0001 + b (+ c)
+ *   mix!               bench/fuzz.jl:19-22     dst = a*0.5 + b*0.25 + k
+ *   stir!              bench/independent.jl:37-40
+ *   the eight-op chain and the scatter-add/histogram are stated by the
+ *   workload definitions (no reference kernel exists for them: parity with
+ *   the reference is unpinned there, and this file is the definition).
+ */
+#include <math.h>
+#include <omp.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+static int nthreads(int t) { return t > 0 ? t : omp_get_max_threads(); }
+
+/* out = 2*sqrt(|fma(((0.5x+y)*z)+y, x, z)|) - x, one rounding per op. */
+void oracle_chain8(const float* x, const float* y, const float* z, float* out, int64_t n, int threads) {
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    float t1 = 0.5f * x[i];
+    t1 = t1 + y[i];
+    float t2 = t1 * z[i];
+    float t3 = t2 + y[i];
+    float t4 = fmaf(t3, x[i], z[i]);
+    float t5 = fabsf(t4);
+    float t6 = sqrtf(fabsf(t5));
+    float t7 = 2.0f * t6;
+    out[i] = t7 - x[i];
+  }
+}
+
+/* The chain as eight separate passes over memory, as the unfused graph runs it
+ * (axpy, mul, add, fma, abs, sqrt(abs), scale, sub), with intermediates in
+ * `tmp` (n floats each, 7 of them). Same values as oracle_chain8. */
+void oracle_chain8_passes(const float* x, const float* y, const float* z, float* out, float* tmp,
+                          int64_t n, int threads) {
+  float *t1 = tmp, *t2 = tmp + n, *t3 = tmp + 2 * n, *t4 = tmp + 3 * n, *t5 = tmp + 4 * n,
+        *t6 = tmp + 5 * n, *t7 = tmp + 6 * n;
+  int nt = nthreads(threads);
+#pragma omp parallel num_threads(nt)
+  {
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t1[i] = 0.5f * x[i] + y[i];
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t2[i] = t1[i] * z[i];
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t3[i] = t2[i] + y[i];
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t4[i] = fmaf(t3[i], x[i], z[i]);
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t5[i] = fabsf(t4[i]);
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t6[i] = sqrtf(fabsf(t5[i]));
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) t7[i] = 2.0f * t6[i];
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = t7[i] - x[i];
+  }
+}
+
+/* Three in-place updates with read-after-write order (touch1!, touch2!,
+ * touch3!): b = b*1.0001 + 1; b = b*1.0001 + c; b = b*1.0001 + c + d. */
+void oracle_touch3(float* b, const float* c, const float* d, int64_t n, int threads) {
+  int nt = nthreads(threads);
+#pragma omp parallel num_threads(nt)
+  {
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      float t = b[i] * 1.0001f;
+      b[i] = t + 1.0f;
+    }
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      float t = b[i] * 1.0001f;
+      b[i] = t + c[i];
+    }
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      float t = b[i] * 1.0001f;
+      t = t + c[i];
+      b[i] = t + d[i];
+    }
+  }
+}
+
+/* Scatter-add checker: acc[b] = sum of v[i] with idx[i] == b, in double, and
+ * the exact count per bin. Indices outside [0, nbins) are skipped. Per-thread
+ * private bins, reduced in thread order. acc may be NULL (histogram only),
+ * hist may be NULL. */
+void oracle_scatter_f64(const float* v, const int32_t* idx, int64_t n, int32_t nbins, double* acc,
+                        uint32_t* hist, int threads) {
+  int nt = nthreads(threads);
+  double* pa = acc ? (double*)calloc((size_t)nt * nbins, sizeof(double)) : NULL;
+  uint32_t* ph = hist ? (uint32_t*)calloc((size_t)nt * nbins, sizeof(uint32_t)) : NULL;
+#pragma omp parallel num_threads(nt)
+  {
+    int t = omp_get_thread_num();
+    double* a = pa ? pa + (size_t)t * nbins : NULL;
+    uint32_t* h = ph ? ph + (size_t)t * nbins : NULL;
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      int32_t b = idx[i];
+      if ((uint32_t)b >= (uint32_t)nbins) continue;
+      if (a) a[b] += (double)v[i];
+      if (h) h[b] += 1u;
+    }
+  }
+  for (int32_t b = 0; b < nbins; ++b) {
+    if (acc) {
+      double s = 0;
+      for (int t = 0; t < nt; ++t) s += pa[(size_t)t * nbins + b];
+      acc[b] = s;
+    }
+    if (hist) {
+      uint32_t s = 0;
+      for (int t = 0; t < nt; ++t) s += ph[(size_t)t * nbins + b];
+      hist[b] = s;
+    }
+  }
+  free(pa);
+  free(ph);
+}
+
+/* The same scatter in float, as a CPU implementation of the workload would run
+ * it (private float bins per thread, reduced in thread order). `scratch` holds
+ * threads*nbins floats and threads*nbins uint32 (caller-allocated, so the timed
+ * region allocates nothing). */
+void oracle_scatter_f32(const float* v, const int32_t* idx, int64_t n, int32_t nbins, float* acc,
+                        uint32_t* hist, float* scratch_f, uint32_t* scratch_u, int threads) {
+  int nt = nthreads(threads);
+#pragma omp parallel num_threads(nt)
+  {
+    int t = omp_get_thread_num();
+    float* a = acc ? scratch_f + (size_t)t * nbins : NULL;
+    uint32_t* h = hist ? scratch_u + (size_t)t * nbins : NULL;
+    if (a) memset(a, 0, sizeof(float) * (size_t)nbins);
+    if (h) memset(h, 0, sizeof(uint32_t) * (size_t)nbins);
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      int32_t b = idx[i];
+      if ((uint32_t)b >= (uint32_t)nbins) continue;
+      if (a) a[b] += v[i];
+      if (h) h[b] += 1u;
+    }
+#pragma omp barrier
+#pragma omp for schedule(static)
+    for (int32_t b = 0; b < nbins; ++b) {
+      if (acc) {
+        float s = 0;
+        for (int k = 0; k < nt; ++k) s += scratch_f[(size_t)k * nbins + b];
+        acc[b] = s;
+      }
+      if (hist) {
+        uint32_t s = 0;
+        for (int k = 0; k < nt; ++k) s += scratch_u[(size_t)k * nbins + b];
+        hist[b] = s;
+      }
+    }
+  }
+}
+
+/* mix!(dst, a, b, k) over n elements (bench/fuzz.jl:19-22). */
+void oracle_mix(float* dst, const float* a, const float* b, float k, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float t = a[i] * 0.5f;
+    float u = b[i] * 0.25f;
+    dst[i] = (t + u) + k;
+  }
+}
+
+int oracle_max_threads(void) { return omp_get_max_threads(); }
