@@ -6,16 +6,19 @@
 // written. `accumulate` = 0 overwrites the outputs with the sums of this call,
 // 1 adds them to what is there.
 //
-// Layout of the work on B200: a thread-block cluster of c CTAs (c <= 8, one
-// portable cluster) privatises the whole bin range in distributed shared
-// memory — CTA r owns bins [r*per, (r+1)*per) of every table — so each element
-// costs one `red.shared::cluster` into the owning CTA instead of a global atomic
-// that would serialise in L2. The input is streamed once with 128-bit loads.
-// Each cluster then writes its private bins to scratch, and a second kernel
-// sums the clusters' partials per bin in a fixed order, so the float sums do
-// not depend on which cluster finished first and the integer counts are exact.
+// Layout of the work on B200 (measured there: shared-memory atomics run at
+// 8.5 u32 / 2.5 f32 per clock per SM, remote distributed-shared-memory atomics
+// 10-40x slower, L2 atomics ~190 G/s for the whole GPU): a thread-block
+// cluster of c co-scheduled CTAs splits the bin range, CTA r keeping bins
+// [r*per, (r+1)*per) of every table in its own shared memory. All c CTAs
+// stream the cluster's contiguous chunk of the input — one of the c reads comes
+// from HBM, the others hit L2 — and each applies only the elements whose bin it
+// owns, with local shared-memory atomics. No atomic leaves the SM.
+// Each CTA then writes its private bins to scratch, and a second kernel sums the
+// clusters' partials per bin in a fixed order, so the float sums do not depend
+// on which cluster finished first and the integer counts are exact.
 //
-// Bins larger than the cluster's shared memory fall back to global atomics
+// Bins larger than a cluster's shared memory fall back to global atomics
 // (L2-resident tables), which needs no scratch.
 
 #include <cooperative_groups.h>
@@ -23,6 +26,9 @@
 
 #include <algorithm>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "../mtl_internal.hpp"
 
@@ -30,17 +36,26 @@ namespace cg = cooperative_groups;
 
 namespace mtl {
 
-// Shared-memory bytes of bins per CTA that still leave room for two CTAs per SM.
-static constexpr uint32_t kBinsSmemPerCta = 96 * 1024;
-static constexpr int kThreads = 512;
-static constexpr int kCtasPerSm = 2;
+// Shared-memory bytes of bins per CTA (one CTA per SM) and threads per CTA.
+#ifndef MTL_SCATTER_SMEM_KB
+#define MTL_SCATTER_SMEM_KB 128
+#endif
+#ifndef MTL_SCATTER_THREADS
+#define MTL_SCATTER_THREADS 1024
+#endif
+#ifndef MTL_SCATTER_CTAS_PER_SM
+#define MTL_SCATTER_CTAS_PER_SM 1
+#endif
+static constexpr uint32_t kBinsSmemPerCta = MTL_SCATTER_SMEM_KB * 1024;
+static constexpr int kThreads = MTL_SCATTER_THREADS;
+static constexpr int kCtasPerSm = MTL_SCATTER_CTAS_PER_SM;
 
 struct ScatterShape {
   bool cluster;     // false: global-atomic fallback
-  int c;            // cluster size
+  int c;            // cluster size: CTAs sharing one chunk, each owning 1/c of the bins
   int shift;        // per = 1 << shift bins per CTA
   int tables;       // 1 or 2
-  int nclusters;    // grid = nclusters * c
+  int nclusters;    // grid = nclusters * c, one CTA per SM
   uint32_t smem;    // dynamic shared bytes per CTA
 };
 
@@ -50,7 +65,50 @@ static int ceil_log2(uint64_t x) {
   return s;
 }
 
-static ScatterShape scatter_shape(int nbins, int tables, int sm_count) {
+template <bool ACC, bool HIST>
+__global__ void scatter_cluster_kernel(const float* __restrict__, const int* __restrict__, int64_t,
+                                       uint32_t, int, float* __restrict__, uint32_t* __restrict__);
+
+// How many clusters of this shape the device runs at once: a grid larger than
+// that would run in a second, mostly idle wave (clusters must fit inside one
+// GPC, so the answer is not simply SMs / c). Cached per device and shape.
+static int max_active_clusters(int device, int tables, int c, uint32_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, uint32_t>, int> cache;
+  auto key = std::make_tuple(device, tables, c, smem);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  const void* k = tables == 2 ? (const void*)scatter_cluster_kernel<true, true>
+                              : (const void*)scatter_cluster_kernel<true, false>;
+  int n = 0;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = c;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
+static ScatterShape scatter_shape(int nbins, int tables, int sm_count, int device) {
   ScatterShape sh{};
   sh.tables = tables;
   int lg = ceil_log2((uint64_t)std::max(nbins, 1));
@@ -61,8 +119,12 @@ static ScatterShape scatter_shape(int nbins, int tables, int sm_count) {
       sh.cluster = true;
       sh.c = c;
       sh.shift = shift;
-      sh.smem = (uint32_t)smem;
+      sh.smem = (uint32_t)std::max<uint64_t>(smem, 16);
       sh.nclusters = std::max(1, sm_count * kCtasPerSm / c);
+      if (device >= 0) {
+        int fit = max_active_clusters(device, tables, c, sh.smem);
+        if (fit > 0) sh.nclusters = std::min(sh.nclusters, fit);
+      }
       return sh;
     }
   }
@@ -70,45 +132,44 @@ static ScatterShape scatter_shape(int nbins, int tables, int sm_count) {
   return sh;
 }
 
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void red_cluster_f32(uint32_t addr, float v) {
-  asm volatile("red.shared::cluster.add.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void red_cluster_u32(uint32_t addr, uint32_t v) {
-  asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
 __device__ __forceinline__ int4 ld_nc_v4(const int* p) {
   int4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.v4.s32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
 }
 __device__ __forceinline__ float4 ld_nc_v4f(const float* p) {
   float4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
                : "l"(p));
   return r;
 }
 
+// One element: applied by the CTA that owns its bin, skipped by the others.
+// Branch-free: the owner test is a predicate on the shared-memory reductions.
+// Bins outside [0, nbins) have an owner >= c (negative indices wrap to a huge
+// unsigned value), so no CTA applies them.
 template <bool ACC, bool HIST>
-__device__ __forceinline__ void scatter_one(int b, float v, uint32_t nbins, int shift,
-                                            uint32_t acc_base, uint32_t hist_base) {
-  if ((uint32_t)b >= nbins) return;
+__device__ __forceinline__ void scatter_one(int b, float v, uint32_t rank, int shift, uint32_t acc_base,
+                                            uint32_t hist_base) {
   const uint32_t owner = (uint32_t)b >> shift;
-  const uint32_t local = (uint32_t)b & ((1u << shift) - 1);
-  if (ACC) red_cluster_f32(mapa_shared(acc_base + local * 4, owner), v);
-  if (HIST) red_cluster_u32(mapa_shared(hist_base + local * 4, owner), 1u);
+  const uint32_t off = ((uint32_t)b & ((1u << shift) - 1)) * 4;
+  if (ACC)
+    asm volatile("{ .reg .pred p; setp.eq.u32 p, %0, %1; @p red.shared.add.f32 [%2], %3; }" ::"r"(owner),
+                 "r"(rank), "r"(acc_base + off), "f"(v)
+                 : "memory");
+  if (HIST)
+    asm volatile("{ .reg .pred p; setp.eq.u32 p, %0, %1; @p red.shared.add.u32 [%2], 1; }" ::"r"(owner),
+                 "r"(rank), "r"(hist_base + off)
+                 : "memory");
 }
 
-// One cluster privatises all bins; partials go to ws[cluster][table][nbins].
+// CTA `rank` of cluster `cl` applies the elements of chunk `cl` that fall in its
+// bin range; partials go to ws[cl][nbins] per table.
 template <bool ACC, bool HIST>
-__global__ void __launch_bounds__(kThreads) scatter_cluster_kernel(
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) scatter_cluster_kernel(
     const float* __restrict__ v, const int* __restrict__ idx, int64_t n, uint32_t nbins, int shift,
     float* __restrict__ ws_acc, uint32_t* __restrict__ ws_hist) {
   extern __shared__ __align__(16) uint32_t smem[];
@@ -116,59 +177,66 @@ __global__ void __launch_bounds__(kThreads) scatter_cluster_kernel(
   const uint32_t per = 1u << shift;
   const uint32_t tables = (ACC ? 1 : 0) + (HIST ? 1 : 0);
   for (uint32_t i = threadIdx.x; i < tables * per; i += blockDim.x) smem[i] = 0;
-  // Every CTA's bins are zero before any CTA of the cluster adds into them.
-  cluster.sync();
+  __syncthreads();
+  float* sacc = reinterpret_cast<float*>(smem);
+  uint32_t* shist = smem + (ACC ? per : 0);
+  const uint32_t acc_base = (uint32_t)__cvta_generic_to_shared(sacc);
+  const uint32_t hist_base = (uint32_t)__cvta_generic_to_shared(shist);
 
-  const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
-  const uint32_t acc_base = base;
-  const uint32_t hist_base = base + (ACC ? per * 4 : 0);
-  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t rank = cluster.block_rank();
+  const uint32_t c = cluster.num_blocks();
+  const int64_t cl = blockIdx.x / c;
+  const int64_t ncl = gridDim.x / c;
+  // This cluster's chunk, in groups of four elements.
+  const int64_t n4 = n / 4;
+  const int64_t per_cl = (n4 + ncl - 1) / ncl;
+  const int64_t g0 = cl * per_cl;
+  const int64_t g1 = min(n4, g0 + per_cl);
   const bool vec = ((reinterpret_cast<uintptr_t>(idx) | (ACC ? reinterpret_cast<uintptr_t>(v) : 0)) & 15) == 0;
-  int64_t done = 0;
   if (vec) {
-    const int64_t n4 = n / 4;
-    int64_t q = tid;
+    int64_t q = g0 + threadIdx.x;
+    const int64_t stride = blockDim.x;
     // Two groups of four per iteration keep 64 bytes per thread in flight.
-    for (; q + nthreads < n4; q += 2 * nthreads) {
+    for (; q + stride < g1; q += 2 * stride) {
       int4 b0 = ld_nc_v4(idx + 4 * q);
-      int4 b1 = ld_nc_v4(idx + 4 * (q + nthreads));
+      int4 b1 = ld_nc_v4(idx + 4 * (q + stride));
       float4 v0 = make_float4(0, 0, 0, 0), v1 = v0;
       if (ACC) {
         v0 = ld_nc_v4f(v + 4 * q);
-        v1 = ld_nc_v4f(v + 4 * (q + nthreads));
+        v1 = ld_nc_v4f(v + 4 * (q + stride));
       }
-      scatter_one<ACC, HIST>(b0.x, v0.x, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.y, v0.y, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.z, v0.z, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.w, v0.w, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.x, v1.x, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.y, v1.y, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.z, v1.z, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.w, v1.w, nbins, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.x, v0.x, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.y, v0.y, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.z, v0.z, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.w, v0.w, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b1.x, v1.x, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b1.y, v1.y, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b1.z, v1.z, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b1.w, v1.w, rank, shift, acc_base, hist_base);
     }
-    for (; q < n4; q += nthreads) {
+    for (; q < g1; q += stride) {
       int4 b0 = ld_nc_v4(idx + 4 * q);
       float4 v0 = make_float4(0, 0, 0, 0);
       if (ACC) v0 = ld_nc_v4f(v + 4 * q);
-      scatter_one<ACC, HIST>(b0.x, v0.x, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.y, v0.y, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.z, v0.z, nbins, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.w, v0.w, nbins, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.x, v0.x, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.y, v0.y, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.z, v0.z, rank, shift, acc_base, hist_base);
+      scatter_one<ACC, HIST>(b0.w, v0.w, rank, shift, acc_base, hist_base);
     }
-    done = n4 * 4;
+    // The ragged tail (n not a multiple of four) belongs to the last cluster.
+    if (cl == ncl - 1)
+      for (int64_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x)
+        scatter_one<ACC, HIST>(idx[i], ACC ? v[i] : 0.f, rank, shift, acc_base, hist_base);
+  } else {
+    const int64_t e0 = g0 * 4, e1 = cl == ncl - 1 ? n : g1 * 4;
+    for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x)
+      scatter_one<ACC, HIST>(idx[i], ACC ? v[i] : 0.f, rank, shift, acc_base, hist_base);
   }
-  for (int64_t i = done + tid; i < n; i += nthreads)
-    scatter_one<ACC, HIST>(idx[i], ACC ? v[i] : 0.f, nbins, shift, acc_base, hist_base);
-
-  // All adds into this CTA's bins have landed before it reads them.
-  cluster.sync();
-  const uint32_t rank = cluster.block_rank();
-  const int64_t cl = blockIdx.x / cluster.num_blocks();
+  __syncthreads();
   const uint32_t lo = rank * per;
   for (uint32_t i = threadIdx.x; i < per && lo + i < nbins; i += blockDim.x) {
-    if (ACC) ws_acc[cl * nbins + lo + i] = __uint_as_float(smem[i]);
-    if (HIST) ws_hist[cl * nbins + lo + i] = smem[(ACC ? per : 0) + i];
+    if (ACC) ws_acc[cl * nbins + lo + i] = sacc[i];
+    if (HIST) ws_hist[cl * nbins + lo + i] = shist[i];
   }
 }
 
@@ -242,7 +310,7 @@ mtl_status scatter_check(const LaunchArgs& la, const uint64_t* bytes) {
 
 uint64_t scatter_workspace(const LaunchArgs& la) {
   int tables = (la.a[0].kind != MTL_ARG_NULL) + (la.a[1].kind != MTL_ARG_NULL);
-  ScatterShape sh = scatter_shape(la.a[4].i32, tables, la.sm_count);
+  ScatterShape sh = scatter_shape(la.a[4].i32, tables, la.sm_count, la.device);
   if (!sh.cluster) return 0;
   return (uint64_t)sh.nclusters * tables * (uint64_t)la.a[4].i32 * 4;
 }
@@ -280,7 +348,7 @@ mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* 
   scatter_unpack(la, acc, hist, v, idx, nbins, accumulate, n);
   cudaStream_t s = (cudaStream_t)stream;
   const int tables = (acc != nullptr) + (hist != nullptr);
-  ScatterShape sh = scatter_shape(nbins, tables, la.sm_count);
+  ScatterShape sh = scatter_shape(nbins, tables, la.sm_count, la.device);
   cudaError_t e = cudaSuccess;
   if (sh.cluster) {
     uint64_t need = (uint64_t)sh.nclusters * tables * (uint64_t)nbins * 4;

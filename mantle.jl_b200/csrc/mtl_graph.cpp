@@ -939,6 +939,7 @@ mtl_status mtl_graph_dispatch(mtl_graph* g, int32_t pass, int32_t kernel, const 
       la.a.push_back(a);
     }
     la.sm_count = device_sm_count(g->dev);
+    la.device = device_ordinal(g->dev);
     uint64_t bytes = kd->workspace(la);
     if (bytes > 0) {
       d.workspace_rid = new_transient(g, (bytes + 255) / 256, 256, true);

@@ -92,6 +92,7 @@ struct LaunchArgs {
   int ndim = 1;
   int group[3] = {0, 0, 0};
   int sm_count = 148;
+  int device = -1;  // CUDA ordinal the launch is for (-1: none, shapes use sm_count)
 };
 
 // Description of one elementwise micro-op program (fused chains). Defined in
@@ -231,6 +232,7 @@ struct CompileOpts {
 // Runs Dag, Schedule, Liveness, Place, Aliasing, Barriers and the edge lowering.
 mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a);
 bool overlapping(const mtl_graph* g, int a, int b);
-// SM count of a device (148 when there is none: analysis-only graphs).
+// SM count and ordinal of a device (148 / -1 when there is none: analysis-only graphs).
 int device_sm_count(mtl_device* d);
+int device_ordinal(mtl_device* d);
 }  // namespace mtl

@@ -48,6 +48,7 @@ struct mtl_buffer {
 
 namespace mtl {
 int device_sm_count(mtl_device* d) { return d ? d->sm_count : 148; }
+int device_ordinal(mtl_device* d) { return d ? d->ordinal : -1; }
 }
 
 #define CUDA_TRY(expr)                                                                       \
@@ -137,6 +138,7 @@ static mtl_status resolve(const mtl_plan* pl, const Dispatch& d, LaunchArgs& la,
     la.group[i] = d.group[i];
   }
   la.sm_count = device_sm_count(pl->g->dev);
+  la.device = device_ordinal(pl->g->dev);
   for (const mtl_arg& m : d.args) {
     Arg x;
     switch (m.kind) {
@@ -918,6 +920,7 @@ static mtl_status direct_args(int32_t kernel, const mtl_arg* args, int32_t nargs
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaGetLastError();
   la.sm_count = sms;
+  la.device = dev;
   for (int i = 0; i < nargs; ++i) {
     Arg x;
     const mtl_arg& m = args[i];

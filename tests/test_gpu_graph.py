@@ -147,7 +147,9 @@ def test_scatter_workload_graph_replays(dev):
     w2 = build_scatter(dev, n=n, nbins=nbins, nupd=nupd, seed=5, alias=False)
     pos = {p.name: k for k, p in enumerate(w2.plan.passes)}
     assert w2.plan.edges(pos["scatter b"]) == []
-    assert M.peakbytes(w2.plan) == 2 * M.peakbytes(w.plan)
+    # aliased: the two scratch buffers share bytes; not aliased: both are held
+    assert M.peakbytes(w2.plan) == M.naivebytes(w2.plan)
+    assert M.peakbytes(w.plan) < M.naivebytes(w.plan)
 
 
 def test_backend_and_both_modes_agree(dev):
