@@ -307,6 +307,20 @@ mtl_status mtl_kernel_workspace(int32_t kernel, const mtl_arg* args, int32_t nar
 mtl_status mtl_launch(int32_t kernel, const mtl_arg* args, int32_t nargs, const int64_t* ndrange,
                       int32_t ndim, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Scatter-add / histogram that allocates nothing (no counterpart in the
+ * reference). For callers that cannot call cudaMalloc on this path: scratch
+ * comes from a fixed MTL_NOALLOC_SCRATCH_BYTES array compiled into the library,
+ * held by every GPU that loads it until the process exits. Same arguments and
+ * results as the `scatter_add` kernel (acc or hist may be NULL), launched on
+ * `stream` for the current device. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) — make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race, so
+ * order them. A call whose bins need more scratch than the array holds fails
+ * with MTL_ERR_ARGUMENT. */
+#define MTL_NOALLOC_SCRATCH_BYTES (20u << 20)
+mtl_status mtl_scatter_add_noalloc(float* acc, uint32_t* hist, const float* values, const int32_t* idx,
+                                   int64_t n, int32_t nbins, int32_t accumulate, void* stream);
+
 /* ── collectives (NCCL over NVLink) ──────────────────────────────────────── */
 /* One communicator per process/GPU; `unique_id` is NCCL's 128-byte id, shared
  * by the caller over any host channel (torch.distributed's store). */
