@@ -265,6 +265,51 @@ def fragmentation(items: list[Item], height: int):
     return (1.0, 0.0) if L == 0 else (height / L, max((i.size for i in items), default=0) / L)
 
 
+def parsegap(s: str, addend: int):
+    """csv.jl:10-22: `lo-hi` or `lo-hi@wlo:whi`; `end`-style files add 1 to hi."""
+    at = s.split("@")
+    span = at[0].split("-")
+    if len(span) != 2:
+        raise ValueError(f"improperly formed gap: {s}")
+    during = (int(span[0]), int(span[1]) + addend)
+    window = None
+    if len(at) > 1:
+        w = at[1].split(":")
+        if len(w) != 2:
+            raise ValueError(f"improperly formed gap: {s}")
+        window = (int(w[0]), int(w[1]))
+    return (during, window)
+
+
+def readproblem(text: str, capacity: int):
+    """csv.jl:24-56 over the file's text: a column named `end` is an inclusive last
+    time and adds 1 to every upper bound, gaps included; `upper` is exclusive."""
+    lines = [ln for ln in text.splitlines() if ln.strip()]
+    addend = 0
+    cols = {}
+    for i, raw in enumerate(x.strip() for x in lines[0].split(",")):
+        key = {"buffer": "id", "buffer_id": "id", "begin": "lower", "start": "lower"}.get(raw, raw)
+        if key == "end":
+            key, addend = "upper", 1
+        if key in cols:
+            raise ValueError(f"duplicate column: {key}")
+        cols[key] = i
+    for req in ("id", "lower", "upper", "size"):
+        if req not in cols:
+            raise ValueError(f"missing required column: {req}")
+    items = []
+    for line in lines[1:]:
+        f = line.split(",")
+        if len(f) != len(cols):
+            raise ValueError(f"row has {len(f)} fields, header has {len(cols)}")
+        at = lambda k: f[cols[k]]  # noqa: E731
+        gaps = [parsegap(g, addend) for g in at("gaps").split(" ") if g] if "gaps" in cols else []
+        items.append(Item(at("id"), (int(at("lower")), int(at("upper")) + addend), int(at("size")),
+                          int(at("alignment")) if "alignment" in cols else 1, gaps,
+                          int(at("offset")) if "offset" in cols else None))
+    return items, capacity
+
+
 # ── graph model and compile phases (ext/MantleLavaExt.jl) ──────────────────
 @dataclass
 class Res:
