@@ -147,10 +147,23 @@ __global__ void __launch_bounds__(256, 2) ew_vec_kernel(const __grid_constant__ 
     for (int j = 0; j < p.nout; ++j)
       reinterpret_cast<float4*>(p.out[j])[g] = get(r, p.out_reg[j]).x[0];
   }
+  // The ragged tail (at most three elements) is done by the first threads of
+  // block 0, one element each, so a launch is always a single kernel.
+  const int64_t t = groups * 4 + threadIdx.x;
+  if (blockIdx.x == 0 && t < p.n) {
+    Vec<1> r[EW_MAX_REGS];
+    for (int k = 0; k < p.nin; ++k) {
+      Vec<1> v;
+      v.x[0].x = v.x[0].y = v.x[0].z = v.x[0].w = p.in[k][t];
+      set(r, k, v);
+    }
+    run_program(p, r);
+    for (int j = 0; j < p.nout; ++j) p.out[j][t] = get(r, p.out_reg[j]).x[0].x;
+  }
 }
 
-// Scalar body for the ragged tail (or everything, when a pointer is not
-// 16-byte aligned). Uses lane 0 of a width-1 vector.
+// Scalar body, for programs where some pointer is not 16-byte aligned. Uses
+// lane 0 of a width-1 vector.
 __global__ void __launch_bounds__(256) ew_scalar_kernel(const __grid_constant__ EwParams p,
                                                         int64_t begin) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -179,6 +192,11 @@ static int sm_count_of_current() {
   return cached[dev];
 }
 
+bool ew_program_fits(const EwProgram& p) {
+  return (int)p.inputs.size() <= EW_MAX_IN && (int)p.outputs.size() <= EW_MAX_OUT &&
+         (int)p.ops.size() <= EW_MAX_OPS && p.nregs <= EW_MAX_REGS;
+}
+
 mtl_status ew_launch_program(const EwProgram& prog, void* stream) {
   if ((int)prog.inputs.size() > EW_MAX_IN || (int)prog.outputs.size() > EW_MAX_OUT ||
       (int)prog.ops.size() > EW_MAX_OPS || prog.nregs > EW_MAX_REGS)
@@ -205,20 +223,14 @@ mtl_status ew_launch_program(const EwProgram& prog, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   const int block = 256;
   const int sms = sm_count_of_current();
-  int64_t done = 0;
   if (aligned) {
-    int64_t groups = p.n / 4;
-    if (groups > 0) {
-      // Two resident blocks per SM; a grid-stride loop covers the rest.
-      int64_t blocks = std::min<int64_t>((groups + block - 1) / block, (int64_t)sms * 2);
-      ew_vec_kernel<<<(unsigned)blocks, block, 0, s>>>(p);
-      done = groups * 4;
-    }
-  }
-  if (done < p.n) {
-    int64_t rest = p.n - done;
-    int64_t blocks = std::min<int64_t>((rest + block - 1) / block, (int64_t)sms * 8);
-    ew_scalar_kernel<<<(unsigned)blocks, block, 0, s>>>(p, done);
+    // Two resident blocks per SM; a grid-stride loop covers the rest.
+    const int64_t groups = p.n / 4;
+    int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((groups + block - 1) / block, (int64_t)sms * 2));
+    ew_vec_kernel<<<(unsigned)blocks, block, 0, s>>>(p);
+  } else {
+    int64_t blocks = std::min<int64_t>((p.n + block - 1) / block, (int64_t)sms * 8);
+    ew_scalar_kernel<<<(unsigned)blocks, block, 0, s>>>(p, 0);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "elementwise launch: %s", cudaGetErrorString(e));

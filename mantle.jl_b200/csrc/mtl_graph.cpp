@@ -339,6 +339,135 @@ static void add_unique(std::vector<int>& v, int x) {
   if (std::find(v.begin(), v.end(), x) == v.end()) v.push_back(x);
 }
 
+// ── elementwise fusion ──────────────────────────────────────────────────────
+struct Step {
+  std::vector<int> members;  // pass ids, in execution order
+  std::vector<std::pair<int, uint32_t>> usages;
+};
+
+// A pass that can join a fused run: one elementwise dispatch over a 1-D range,
+// every argument a whole declared resource of the graph, no scratch.
+static bool fusable(const mtl_graph* g, const Pass& p) {
+  if (p.kind != MTL_PASS_COMPUTE || p.dispatches.size() != 1) return false;
+  const Dispatch& d = p.dispatches[0];
+  const KernelDesc* kd = kernel_desc(d.kernel);
+  if (!kd || !kd->elementwise || !kd->ew_emit || d.ndim != 1 || d.workspace_rid) return false;
+  for (const mtl_arg& a : d.args)
+    if (a.kind == MTL_ARG_PTR) return false;
+  for (auto& u : p.usages) {
+    const Resource* r = res_of(g, u.first);
+    if (!r || r->kind == RES_VIEW || base_of(u.second) != MTL_U_STORAGE) return false;
+  }
+  return true;
+}
+
+// The micro-op program of a run, with resource ids standing in for pointers:
+// it fails when the run exceeds what one fused kernel can hold.
+static bool program_fits(const mtl_graph* g, const std::vector<int>& run) {
+  std::vector<EwMember> ms;
+  for (int pid : run) {
+    const Dispatch& d = g->passes[pid].dispatches[0];
+    EwMember m;
+    m.kd = kernel_desc(d.kernel);
+    m.la.nd[0] = d.nd[0];
+    for (const mtl_arg& x : d.args) {
+      Arg a;
+      a.kind = x.kind == MTL_ARG_RESOURCE ? MTL_ARG_PTR : x.kind;
+      a.ptr = x.kind == MTL_ARG_RESOURCE ? (uint64_t)x.rid : 0;
+      a.rid = x.kind == MTL_ARG_RESOURCE ? x.rid : 0;
+      a.f32 = x.v.f32;
+      a.i32 = x.v.i32;
+      a.i64 = x.v.i64;
+      a.f64 = x.v.f64;
+      m.la.a.push_back(a);
+    }
+    ms.push_back(m);
+  }
+  EwProgram prog;
+  std::string saved = mtl_last_error();
+  bool ok = ew_build_program(ms, {}, prog) == MTL_OK && ew_program_fits(prog);
+  set_error("%s", saved.c_str());
+  return ok;
+}
+
+void fuse_steps(mtl_graph* g, const std::vector<int>& decl, const std::vector<int>& order, bool fuse,
+                std::vector<Step>& steps, std::vector<int64_t>& elided_at) {
+  steps.clear();
+  const int n = (int)order.size();
+  std::vector<std::vector<int>> runs;
+  for (int p = 0; p < n; ++p) {
+    int pid = decl[order[p]];
+    const Pass& ps = g->passes[pid];
+    bool joined = false;
+    if (fuse && fusable(g, ps) && !runs.empty() && runs.back().size() >= 1) {
+      std::vector<int>& r = runs.back();
+      const Pass& head = g->passes[r[0]];
+      if (fusable(g, head) && head.dispatches[0].nd[0] == ps.dispatches[0].nd[0]) {
+        r.push_back(pid);
+        if (program_fits(g, r))
+          joined = true;
+        else
+          r.pop_back();
+      }
+    }
+    if (!joined) runs.push_back({pid});
+  }
+  // A transient is elided when every pass that touches it is in one fused run
+  // and the first of them writes it without reading it: its value then lives in
+  // registers only.
+  auto& ts = g->transients;
+  std::vector<int> step_of(g->passes.size(), -1);
+  for (int k = 0; k < (int)runs.size(); ++k)
+    for (int pid : runs[k]) step_of[pid] = k;
+  std::vector<int> owner(ts.size(), -2);  // -2 untouched, -1 not elidable, else the run
+  for (int k = 0; k < (int)runs.size(); ++k)
+    for (int pid : runs[k])
+      for (auto& u : g->passes[pid].usages) {
+        int ti = transient_of(g, u.first);
+        if (ti < 0) continue;
+        const Resource* r = res_of(g, u.first);
+        if (runs[k].size() < 2 || r->kind == RES_VIEW || g->res[ts[ti].rid - 1].internal) {
+          owner[ti] = -1;
+        } else if (owner[ti] == -2) {
+          owner[ti] = usage_writes(u.second) && !usage_reads(u.second) ? k : -1;
+        } else if (owner[ti] != k) {
+          owner[ti] = -1;
+        }
+      }
+  elided_at.assign(ts.size(), 0);
+  for (int k = 0; k < (int)runs.size(); ++k) {
+    Step st;
+    st.members = runs[k];
+    if (runs[k].size() == 1) {
+      st.usages = g->passes[runs[k][0]].usages;
+    } else {
+      // Merged usages: read if the run reads the value from before it, write if
+      // the run writes it.
+      std::vector<int> rids;
+      std::map<int, uint32_t> flags;
+      std::set<int> written;
+      for (int pid : runs[k])
+        for (auto& u : g->passes[pid].usages) {
+          int ti = transient_of(g, u.first);
+          if (ti >= 0 && owner[ti] == k) continue;
+          if (!flags.count(u.first)) rids.push_back(u.first);
+          uint32_t& f = flags[u.first];
+          f |= MTL_U_STORAGE;
+          if (usage_reads(u.second) && !written.count(u.first)) f |= MTL_U_READ;
+          if (usage_writes(u.second)) {
+            f |= MTL_U_WRITE;
+            written.insert(u.first);
+          }
+        }
+      for (int rid : rids) st.usages.push_back({rid, flags[rid]});
+    }
+    steps.push_back(st);
+  }
+  for (size_t ti = 0; ti < ts.size(); ++ti)
+    if (owner[ti] >= 0) elided_at[ti] = owner[ti] + 1;
+  (void)step_of;
+}
+
 // ── compile phases ──────────────────────────────────────────────────────────
 mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
   std::vector<int> decl = declaration_order(g);
@@ -434,21 +563,27 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
   }
   // order[] holds declaration positions; positions in the schedule are 1-based
   // below, as in the reference.
-  std::vector<int> pos_of(n);
-  for (int p = 0; p < n; ++p) pos_of[order[p]] = p + 1;
+  // Steps: every scheduled pass on its own or, when fusion is asked for, runs of
+  // consecutive elementwise passes merged into one kernel (fuse_steps). The
+  // phases below work on steps, so a fused run is one position: its resources
+  // are live together and the placer never gives two of them the same bytes.
+  auto& ts = g->transients;
+  std::vector<Step> steps;
+  std::vector<int64_t> elided_at(ts.size(), 0);  // fused position of an elided transient
+  fuse_steps(g, decl, order, o.fuse, steps, elided_at);
+  const int ns = (int)steps.size();
 
   // Liveness, ext/MantleLavaExt.jl:1478-1507: the interval of every transient
   // is recomputed from the scheduled order. A pass that names only a slice of a
   // transient counts as touching it (the reference keys this lookup by the
   // parent's id alone, so a slice-only use would not extend the interval and
   // the placer could hand those bytes to another transient live at that pass).
-  auto& ts = g->transients;
-  for (auto& t : ts) {
-    t.first = INT64_MAX;
-    t.last = 0;
+  for (size_t i = 0; i < ts.size(); ++i) {
+    ts[i].first = elided_at[i] ? elided_at[i] : INT64_MAX;
+    ts[i].last = elided_at[i];
   }
-  for (int p = 0; p < n; ++p)
-    for (auto& u : P(order[p]).usages) {
+  for (int p = 0; p < ns; ++p)
+    for (auto& u : steps[p].usages) {
       int ti = transient_of(g, u.first);
       if (ti < 0) continue;
       ts[ti].first = std::min<int64_t>(ts[ti].first, p + 1);
@@ -472,7 +607,7 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
     it.id = std::to_string(i + 1);
     it.lower = o.alias ? ts[i].first : 0;
     it.upper = o.alias ? ts[i].last + 1 : lastpass;
-    it.size = (int64_t)ts[i].bytes;
+    it.size = elided_at[i] ? 0 : (int64_t)ts[i].bytes;  // an elided transient takes no bytes
     it.alignment = ts[i].alignment;
     a.items.push_back(it);
   }
@@ -497,8 +632,7 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
       if (i == j) continue;
       const Transient &y = ts[i], &x = ts[j];
       if (!(x.last < y.first)) continue;
-      if (a.offsets[i] < a.offsets[j] + (int64_t)x.bytes &&
-          a.offsets[j] < a.offsets[i] + (int64_t)y.bytes)
+      if (a.offsets[i] < a.offsets[j] + a.items[j].size && a.offsets[j] < a.offsets[i] + a.items[i].size)
         a.alias_begins[(int)y.first].push_back({(int)i, (int)j});
     }
 
@@ -546,8 +680,8 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
   // A plan is replayed: each segment's state at the start of a replay is its
   // last usage in the schedule (ext/MantleLavaExt.jl:1694-1708).
   std::map<int, uint32_t> final_usage;
-  for (int p = 0; p < n; ++p)
-    for (auto& [id, U] : P(order[p]).usages)
+  for (int p = 0; p < ns; ++p)
+    for (auto& [id, U] : steps[p].usages)
       for (int sid : segments_of(id)) final_usage[sid] = U;
 
   std::map<int, ResourceState> states;
@@ -565,11 +699,11 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
   std::vector<std::vector<int>> touched_at(ts.size());
   std::map<int, std::vector<std::pair<int, uint32_t>>> accesses;
 
-  a.prepass.assign(n, {});
-  a.edges.assign(n, {});
+  a.prepass.assign(ns, {});
+  a.edges.assign(ns, {});
   a.transitions.clear();
-  for (int p = 0; p < n; ++p) {
-    const Pass& ps = P(order[p]);
+  for (int p = 0; p < ns; ++p) {
+    const Step& ps = steps[p];
     const int pos = p + 1;
     std::vector<Transition> pre;
     std::vector<int>& edges = a.edges[p];
@@ -651,10 +785,10 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
   // each pass's predecessors from the latest down, one that is already an
   // ancestor of a kept predecessor is redundant.
   {
-    const int W = (n + 64) / 64;
-    std::vector<std::vector<uint64_t>> reach(n + 1, std::vector<uint64_t>(W, 0));
+    const int W = (ns + 64) / 64;
+    std::vector<std::vector<uint64_t>> reach(ns + 1, std::vector<uint64_t>(W, 0));
     auto has = [&](const std::vector<uint64_t>& b, int q) { return (b[q >> 6] >> (q & 63)) & 1; };
-    for (int p = 0; p < n; ++p) {
+    for (int p = 0; p < ns; ++p) {
       std::vector<int>& e = a.edges[p];
       std::sort(e.begin(), e.end(), std::greater<int>());
       std::vector<uint64_t> covered(W, 0);
@@ -671,9 +805,17 @@ mtl_status analyze(mtl_graph* g, const CompileOpts& o, Analysis& a) {
     }
   }
 
-  // Report in pass ids (creation order), not declaration positions.
-  a.order.resize(n);
-  for (int p = 0; p < n; ++p) a.order[p] = decl[order[p]];
+  // Report in pass ids (creation order), not declaration positions: each
+  // step by its first pass, and every member of every step.
+  a.order.resize(ns);
+  a.steps.resize(ns);
+  for (int p = 0; p < ns; ++p) {
+    a.order[p] = steps[p].members[0];
+    a.steps[p] = steps[p].members;
+  }
+  a.elided.clear();
+  for (size_t i = 0; i < ts.size(); ++i)
+    if (elided_at[i]) a.elided.push_back(ts[i].rid);
   a.deps.assign(g->passes.size(), {});
   for (int j = 0; j < n; ++j)
     for (int i : deps[j]) a.deps[decl[j]].push_back(decl[i]);

@@ -148,6 +148,8 @@ struct EwMember {
 mtl_status ew_build_program(const std::vector<EwMember>& ms, const std::vector<uint64_t>& elided,
                             EwProgram& out);
 mtl_status ew_launch_single(const KernelDesc* kd, const LaunchArgs& la, void* stream);
+// Whether a built program is within the limits of the fused kernel.
+bool ew_program_fits(const EwProgram& p);
 // Validates and launches any built-in kernel (elementwise or not).
 mtl_status launch_kernel(int kernel, const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 
@@ -208,6 +210,10 @@ struct Analysis {
   std::vector<Transition> transitions;
   // Lowering: per scheduled position, the positions whose completion it waits on.
   std::vector<std::vector<int>> edges;
+  // Per scheduled position, the passes it runs (more than one: a fused run).
+  std::vector<std::vector<int>> steps;
+  // Transients a fused run keeps in registers: no storage, never stored.
+  std::vector<int> elided;
   std::map<int, std::vector<int>> segments;  // resource id -> atomic segment ids
 };
 

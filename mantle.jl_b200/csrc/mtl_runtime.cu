@@ -218,6 +218,38 @@ static mtl_status capture_dispatch(mtl_plan* pl, const Dispatch& d, cudaGraph_t*
   return capture_graph(pl, [&](cudaStream_t s) { return launch_kernel(kernel, la, ws, wsb, s); }, out);
 }
 
+// A fused run of elementwise passes (scheduled position p): one program, one
+// kernel. Transients the run keeps in registers are never stored.
+static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
+  const mtl_graph* g = pl->g;
+  std::vector<EwMember> ms;
+  for (int pid : pl->a.steps[p]) {
+    const Dispatch& d = g->passes[pid].dispatches[0];
+    EwMember m;
+    m.kd = kernel_desc(d.kernel);
+    void* ws;
+    uint64_t wsb;
+    resolve(pl, d, m.la, &ws, &wsb);
+    std::vector<uint64_t> bytes(m.la.a.size());
+    for (size_t i = 0; i < m.la.a.size(); ++i) bytes[i] = m.la.a[i].bytes;
+    if (mtl_status s = m.kd->check(m.la, bytes.data())) return s;
+    ms.push_back(m);
+  }
+  std::vector<uint64_t> elided;
+  for (int rid : pl->a.elided) elided.push_back(((uint64_t)1 << 63) | (uint64_t)rid);
+  EwProgram prog;
+  if (mtl_status s = ew_build_program(ms, elided, prog)) return s;
+  return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_program(prog, s); }, out);
+}
+
+// Scheduled position of a pass (the step that runs it), or -1.
+static int position_of(const mtl_plan* pl, int pass) {
+  for (size_t p = 0; p < pl->a.steps.size(); ++p)
+    for (int m : pl->a.steps[p])
+      if (m == pass) return (int)p;
+  return -1;
+}
+
 static mtl_status add_child(cudaGraph_t parent, const std::vector<cudaGraphNode_t>& deps,
                             cudaGraph_t child, cudaGraphNode_t* node) {
   CUDA_TRY(cudaGraphAddChildGraphNode(node, parent, deps.data(), deps.size(), child));
@@ -263,7 +295,18 @@ static mtl_status build_mode(mtl_plan* pl, int mode) {
       entry = {ev};
     }
     std::vector<cudaGraphNode_t> body;
-    if (ps.kind == MTL_PASS_COMPUTE) {
+    if (a.steps[p].size() > 1) {
+      cudaGraph_t child = nullptr;
+      mtl_status st = capture_fused(pl, p, &child);
+      if (st) return fail(st, "fused run from \"%s\": %s", ps.name.c_str(), std::string(mtl_last_error()).c_str());
+      m.nkernels += count_kernels(child);
+      cudaGraphNode_t nd;
+      st = add_child(m.graph, entry, child, &nd);
+      cudaGraphDestroy(child);
+      if (st) return st;
+      m.dispatch_nodes[p].push_back(nd);
+      body.push_back(nd);
+    } else if (ps.kind == MTL_PASS_COMPUTE) {
       std::vector<cudaGraphNode_t> prev = entry;
       for (const Dispatch& d : ps.dispatches) {
         cudaGraph_t child = nullptr;
@@ -763,14 +806,13 @@ mtl_status mtl_plan_set_arg(mtl_plan* pl, int32_t pass, int32_t dispatch, int32_
   cur = *arg;
   if (!g->dev) return MTL_OK;
   if (mtl_status s = use_device(g->dev)) return s;
-  int pos = -1;
-  for (size_t p = 0; p < pl->a.order.size(); ++p)
-    if (pl->a.order[p] == pass) pos = (int)p;
+  const int pos = position_of(pl, pass);
+  const bool fused = pos >= 0 && pl->a.steps[pos].size() > 1;
   for (auto& m : pl->modes) {
     if (!m.built || pos < 0) continue;
     cudaGraph_t child = nullptr;
-    if (mtl_status s = capture_dispatch(pl, d, &child)) return s;
-    cudaError_t e = cudaGraphExecChildGraphNodeSetParams(m.exec, m.dispatch_nodes[pos][dispatch], child);
+    if (mtl_status s = fused ? capture_fused(pl, pos, &child) : capture_dispatch(pl, d, &child)) return s;
+    cudaError_t e = cudaGraphExecChildGraphNodeSetParams(m.exec, m.dispatch_nodes[pos][fused ? 0 : dispatch], child);
     cudaGraphDestroy(child);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "set_arg: %s", cudaGetErrorString(e));
   }
@@ -893,7 +935,9 @@ mtl_status mtl_plan_timings(mtl_plan* pl, mtl_timing* out, int32_t cap, int32_t*
   for (int p = 0; p < np && p < cap; ++p) {
     const Pass& ps = pl->g->passes[pl->a.order[p]];
     memset(&out[p], 0, sizeof(mtl_timing));
-    snprintf(out[p].name, sizeof out[p].name, "%s", ps.name.c_str());
+    std::string name = ps.name;  // a fused run is named by its members, joined by '+'
+    for (size_t k = 1; k < pl->a.steps[p].size(); ++k) name += "+" + pl->g->passes[pl->a.steps[p][k]].name;
+    snprintf(out[p].name, sizeof out[p].name, "%s", name.c_str());
     out[p].kind = ps.kind;
     out[p].samples = (int32_t)pl->gpu_ms[p].size();
     out[p].gpu_ms = median(pl->gpu_ms[p]);

@@ -36,6 +36,39 @@ def test_chain_single_kernel_and_passes_agree(dev):
     assert np.array_equal(O.chain8_passes(I["x"], I["y"], I["z"]), O.chain8(I["x"], I["y"], I["z"]))
 
 
+def test_chain_fused_is_one_kernel_and_bit_exact(dev):
+    for n in (1 << 22, (1 << 16) + 3, 5):
+        w = build_chain(dev, n=n, seed=5, fuse=True)
+        M.run(w.plan)
+        I = w.inputs
+        assert np.array_equal(w.out.array(), O.chain8(I["x"], I["y"], I["z"]))
+        assert w.plan.nkernels() == 1
+        assert M.peakbytes(w.plan) == 0
+        # replaying is idempotent: the chain only reads x, y, z
+        M.run(w.plan)
+        M.run(w.plan, barriers="backend")
+        assert np.array_equal(w.out.array(), O.chain8(I["x"], I["y"], I["z"]))
+
+
+def test_fused_run_stores_a_transient_read_later(dev):
+    from test_phases import _chain_graph
+    n = (1 << 18) + 1
+    g, b = _chain_graph(dev, n, keep_t3=True)
+    x, y, z = (seeded_uniform(6, n, -1, 1, k) for k in range(3))
+    for name, h in (("x", x), ("y", y), ("z", z)):
+        b[name].update(h)
+    plan = M.Plan(g, fuse=True)
+    M.run(plan)
+    # the oracle's pass-by-pass run keeps every intermediate; t4 is the fourth
+    out = np.empty_like(x)
+    tmp = np.empty(7 * n, np.float32)
+    f = lambda a: a.ctypes.data_as(O.C.POINTER(O.C.c_float))  # noqa: E731
+    O.lib().oracle_chain8_passes(f(x), f(y), f(z), f(out), f(tmp), n, 0)
+    assert np.array_equal(b["side"].array(), tmp[3 * n:4 * n])
+    assert np.array_equal(b["out"].array(), O.chain8(x, y, z))
+    assert plan.nkernels() == 1
+
+
 def test_chain_transients_are_placed_in_two_slots(dev):
     # Stage k reads t[k] and writes t[k+1]: only adjacent transients are ever
     # live together, so the slab holds two, not seven (bench/chain.jl:1-10).

@@ -236,3 +236,49 @@ def test_edges_order_every_conflicting_pair():
                     for a in ps[i]["usages"] for b in ps[j]["usages"])
                 if conflict:
                     assert i in reach[j], (seed, i, j)
+
+
+def _chain_graph(dev, n, keep_t3=False):
+    """The eight-op chain over transients; with keep_t3 a copy pass reads the
+    fourth intermediate after the chain, so that value must reach memory."""
+    from mantle_cuda import kernels as K
+    g = M.Graph(dev)
+    mk = (lambda: M.VirtualBuffer(np.float32, n)) if dev is None else (lambda: M.Buffer(dev, np.float32, n))
+    x, y, z, out, side = mk(), mk(), mk(), mk(), mk()
+    t = [M.Transient.Buffer(g, np.float32, n) for _ in range(7)]
+    W = lambda p, b: M.use(p, b, write=True)  # noqa: E731
+    R = lambda p, b: M.use(p, b, read=True)  # noqa: E731
+    M.compute(g, "axpy", lambda p: M.dispatch(p, K.axpy, (W(p, t[0]), R(p, x), R(p, y), 0.5), n))
+    M.compute(g, "mul", lambda p: M.dispatch(p, K.mul, (W(p, t[1]), R(p, t[0]), R(p, z)), n))
+    M.compute(g, "add", lambda p: M.dispatch(p, K.add, (W(p, t[2]), R(p, t[1]), R(p, y)), n))
+    M.compute(g, "fma", lambda p: M.dispatch(p, K.fma, (W(p, t[3]), R(p, t[2]), R(p, x), R(p, z)), n))
+    M.compute(g, "abs", lambda p: M.dispatch(p, K.abs, (W(p, t[4]), R(p, t[3])), n))
+    M.compute(g, "sqrt", lambda p: M.dispatch(p, K.sqrt_abs, (W(p, t[5]), R(p, t[4])), n))
+    M.compute(g, "scale", lambda p: M.dispatch(p, K.scale, (W(p, t[6]), R(p, t[5]), 2.0), n))
+    M.compute(g, "sub", lambda p: M.dispatch(p, K.sub, (W(p, out), R(p, t[6]), R(p, x)), n))
+    if keep_t3:
+        M.copy(g, "keep t4", side, t[3])
+    return g, dict(x=x, y=y, z=z, out=out, side=side)
+
+
+def test_fusion_merges_the_chain_and_elides_its_transients():
+    n = 1 << 20
+    g, _ = _chain_graph(None, n)
+    unfused = M.Plan(g)
+    assert [p.name for p in unfused.passes] == ["axpy", "mul", "add", "fma", "abs", "sqrt", "scale", "sub"]
+    assert M.peakbytes(unfused) == 2 * 4 * n
+    fused = M.Plan(g, fuse=True)
+    assert len(fused.passes) == 1 and fused.passes[0].name == "axpy"
+    assert M.peakbytes(fused) == 0  # every intermediate lives in registers
+    assert M.naivebytes(fused) == 7 * 4 * n
+
+
+def test_fusion_keeps_a_transient_read_outside_the_run():
+    n = 1 << 16
+    g, _ = _chain_graph(None, n, keep_t3=True)
+    fused = M.Plan(g, fuse=True)
+    # the run ends before the copy; t4 is stored, the other six are not
+    assert [p.name for p in fused.passes] == ["axpy", "keep t4"]
+    assert M.peakbytes(fused) == 4 * n
+    # the copy waits for the fused run
+    assert fused.edges(1) == [0]
