@@ -14,6 +14,8 @@ int (*ew_emit_fn(const char* name))(const LaunchArgs&, std::vector<EwOp>&, int*,
 mtl_status scatter_check(const LaunchArgs& la, const uint64_t* bytes);
 uint64_t scatter_workspace(const LaunchArgs& la);
 mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status fft_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status fft_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -132,6 +134,8 @@ static KernelDesc g_kernels[] = {
     {"clear_and_tally", "BB", false, 0b10, 0b11, check_counter, nullptr, run_clear_and_tally, nullptr},
     {"scatter_add", "bbbBii", false, 0b001100, 0b000011, scatter_check, scatter_workspace, scatter_run,
      nullptr},
+    // batched complex FFT: out, in, length, inverse; ndrange = number of transforms
+    {"fft_c2c", "BBii", false, 0b10, 0b01, fft_check, nullptr, fft_run, nullptr},
 };
 #undef EW
 

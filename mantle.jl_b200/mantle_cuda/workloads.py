@@ -146,3 +146,45 @@ def build_scatter(dev, n: int = 1 << 24, nbins: int = 1 << 16, nupd: int = 1 << 
         use(p, B["b"], read=True, write=True), use(p, B["c"], read=True), use(p, B["d"], read=True)), nupd))
     plan = Plan(g, **plan_kw)
     return ScatterWorkload(n, nbins, nupd, bufs, g, plan, inputs, refs)
+
+
+# ── batched FFT, forward then inverse ───────────────────────────────────────
+@dataclass
+class FftWorkload:
+    batch: int
+    n: int
+    x: Buffer
+    spectrum: Buffer
+    back: Buffer
+    graph: Graph
+    plan: Plan
+    inputs: dict
+
+    @property
+    def bytes_step(self) -> int:
+        """Read and write 8 B per ComplexF32 point, once per direction."""
+        return 2 * 2 * 8 * self.batch * self.n
+
+
+def seeded_complex(seed: int, shape: tuple, stream: int = 0) -> np.ndarray:
+    """ComplexF32, real and imaginary parts uniform[-1, 1] (independent streams)."""
+    size = int(np.prod(shape))
+    re = seeded_uniform(seed, size, -1, 1, 2 * stream)
+    im = seeded_uniform(seed, size, -1, 1, 2 * stream + 1)
+    return (re + 1j * im).astype(np.complex64).reshape(shape)
+
+
+def build_fft(dev, batch: int = 16384, n: int = 4096, seed: int = 2, rank: int = 0, **plan_kw) -> FftWorkload:
+    """Two passes: the forward transform of x into the spectrum, then the
+    inverse of the spectrum back into x's shape."""
+    x_h = seeded_complex(seed, (batch, n), stream=rank)
+    x = Buffer(dev, x_h.reshape(-1))
+    spectrum = Buffer(dev, np.complex64, batch * n)
+    back = Buffer(dev, np.complex64, batch * n)
+    g = Graph(dev)
+    compute(g, "fft forward", lambda p: dispatch(p, kernels.fft_c2c, (
+        use(p, spectrum, write=True), use(p, x, read=True), n, 0), batch))
+    compute(g, "fft inverse", lambda p: dispatch(p, kernels.fft_c2c, (
+        use(p, back, write=True), use(p, spectrum, read=True), n, 1), batch))
+    plan = Plan(g, **plan_kw)
+    return FftWorkload(batch, n, x, spectrum, back, g, plan, {"x": x_h})

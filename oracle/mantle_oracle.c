@@ -12,9 +12,10 @@
  *   touch1!..touch3!   bench/stress.jl:30-45   a = a*1.0001 + b (+ c)
  *   mix!               bench/fuzz.jl:19-22     dst = a*0.5 + b*0.25 + k
  *   stir!              bench/independent.jl:37-40
- *   the eight-op chain and the scatter-add/histogram are stated by the
- *   workload definitions (no reference kernel exists for them: parity with
- *   the reference is unpinned there, and this file is the definition).
+ *   the eight-op chain, the scatter-add/histogram and the batched FFT are
+ *   stated by the workload definitions (no reference kernel exists for them:
+ *   parity with the reference is unpinned there, and this file is the
+ *   definition; the FFT checker is itself checked against numpy.fft).
  */
 #include <math.h>
 #include <omp.h>
@@ -177,6 +178,61 @@ void oracle_mix(float* dst, const float* a, const float* b, float k, int64_t n) 
     float u = b[i] * 0.25f;
     dst[i] = (t + u) + k;
   }
+}
+
+/* Batched complex DFT of length n (a power of two), interleaved re/im:
+ *   forward  X[k] = sum_j x[j] e^{-2 pi i jk/n},  inverse  (1/n) sum_j x[j] e^{+2 pi i jk/n}.
+ * Iterative radix-2 Cooley-Tukey (bit-reversal permutation, then log2 n
+ * butterfly stages), one transform per loop iteration across threads. The
+ * checker runs it in double (oracle_fft_f64); oracle_fft_f32 is the same
+ * algorithm in float with double-precision twiddles, the CPU timing leg. */
+#define FFT_BODY(T, in, out, batch, n, inverse, threads)                                          \
+  do {                                                                                            \
+    int lg = 0;                                                                                   \
+    while ((1 << lg) < n) ++lg;                                                                   \
+    const double sgn = inverse ? 1.0 : -1.0;                                                      \
+    T* tw = (T*)malloc(sizeof(T) * (size_t)n);                                                    \
+    for (int k = 0; k < n / 2; ++k) {                                                             \
+      double a = 6.283185307179586476925286766559 * (double)k / (double)n;                        \
+      tw[2 * k] = (T)cos(a);                                                                      \
+      tw[2 * k + 1] = (T)(sgn * sin(a));                                                          \
+    }                                                                                             \
+    _Pragma("omp parallel for num_threads(nthreads(threads)) schedule(static)")                   \
+    for (int64_t b = 0; b < batch; ++b) {                                                         \
+      T* y = out + (size_t)b * 2 * n;                                                             \
+      const float* x = in + (size_t)b * 2 * n;                                                    \
+      for (int j = 0; j < n; ++j) {                                                               \
+        int r = 0;                                                                                \
+        for (int q = 0; q < lg; ++q) r |= ((j >> q) & 1) << (lg - 1 - q);                         \
+        y[2 * r] = (T)x[2 * j];                                                                   \
+        y[2 * r + 1] = (T)x[2 * j + 1];                                                           \
+      }                                                                                           \
+      for (int len = 2; len <= n; len <<= 1) {                                                    \
+        const int half = len >> 1, step = n / len;                                                \
+        for (int s0 = 0; s0 < n; s0 += len)                                                       \
+          for (int k = 0; k < half; ++k) {                                                        \
+            T wr = tw[2 * k * step], wi = tw[2 * k * step + 1];                                   \
+            T* u = y + 2 * (s0 + k);                                                              \
+            T* v = y + 2 * (s0 + k + half);                                                       \
+            T tr = v[0] * wr - v[1] * wi, ti = v[0] * wi + v[1] * wr;                             \
+            v[0] = u[0] - tr;                                                                     \
+            v[1] = u[1] - ti;                                                                     \
+            u[0] = u[0] + tr;                                                                     \
+            u[1] = u[1] + ti;                                                                     \
+          }                                                                                       \
+      }                                                                                           \
+      if (inverse)                                                                                \
+        for (int j = 0; j < 2 * n; ++j) y[j] = y[j] / (T)n;                                       \
+    }                                                                                             \
+    free(tw);                                                                                     \
+  } while (0)
+
+void oracle_fft_f64(const float* in, double* out, int64_t batch, int n, int inverse, int threads) {
+  FFT_BODY(double, in, out, batch, n, inverse, threads);
+}
+
+void oracle_fft_f32(const float* in, float* out, int64_t batch, int n, int inverse, int threads) {
+  FFT_BODY(float, in, out, batch, n, inverse, threads);
 }
 
 int oracle_max_threads(void) { return omp_get_max_threads(); }

@@ -663,6 +663,8 @@ def lib():
         h.oracle_scatter_f64.argtypes = [f32p, i32p, C.c_int64, C.c_int32, f64p, u32p, C.c_int]
         h.oracle_scatter_f32.argtypes = [f32p, i32p, C.c_int64, C.c_int32, f32p, u32p, f32p, u32p, C.c_int]
         h.oracle_mix.argtypes = [f32p, f32p, f32p, C.c_float, C.c_int64]
+        h.oracle_fft_f64.argtypes = [f32p, f64p, C.c_int64, C.c_int, C.c_int, C.c_int]
+        h.oracle_fft_f32.argtypes = [f32p, f32p, C.c_int64, C.c_int, C.c_int, C.c_int]
         h.oracle_max_threads.restype = C.c_int
         _lib = h
     return _lib
@@ -698,6 +700,22 @@ def scatter_f64(v, idx, nbins, acc=True, hist=True, threads=0):
     lib().oracle_scatter_f64(_p(v, C.c_float), _p(idx, C.c_int32), idx.size, nbins, _p(a, C.c_double),
                              _p(h, C.c_uint32), threads)
     return a, h
+
+
+def fft(x, inverse=False, threads=0, f32=False):
+    """Batched DFT along the last axis of a complex64 array (batch, n):
+    complex128 from the double checker, or complex64 from the float variant."""
+    x = np.ascontiguousarray(x, dtype=np.complex64)
+    batch, n = (1, x.shape[0]) if x.ndim == 1 else x.shape
+    xv = x.view(np.float32)
+    if f32:
+        out = np.empty(x.shape, np.complex64)
+        lib().oracle_fft_f32(_p(xv, C.c_float), _p(out.view(np.float32), C.c_float), batch, n, int(inverse), threads)
+    else:
+        out = np.empty(x.shape, np.complex128)
+        lib().oracle_fft_f64(_p(xv, C.c_float), _p(out.view(np.float64), C.c_double), batch, n, int(inverse),
+                             threads)
+    return out
 
 
 def max_threads() -> int:
