@@ -420,6 +420,60 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
     }
 
 
+def bench_gemm(args, ws, rank, local, peaks, peak_kind):
+    """8 GEMMs of 8192^3 (bf16 in, fp32 accumulate and out) as one graph pass;
+    each rank runs its own batch of 8 (weak scaling, no collective)."""
+    import mantle_cuda as M
+    from mantle_cuda.workloads import build_gemm
+    from oracle import oracle as O
+
+    dev = M.Device(local)
+    w = build_gemm(dev, rank=rank)
+    for _ in range(args.warmup):
+        M.run(w.plan)
+    dev.synchronize()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = device_time_ms(dev.stream, lambda: M.run(w.plan), args.steps)
+    ms_step = max_over_ranks(ws, ms / args.steps)
+    tflops = ws * w.flops_step / (ms_step * 1e-3) / 1e12
+    per_gpu = w.flops_step / (ms_step * 1e-3) / 1e12
+    # The timed region is seconds of back-to-back GEMMs: the sustained peak is
+    # the denominator; the burst figure is reported beside it.
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    roofline = {"bound": "tensor", "kernel": "gemm_bf16_kernel (8 x 8192^3 per launch)",
+                "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(per_gpu / peak, 4),
+                "traffic": None, "algorithmic_flops": w.flops_step,
+                "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)",
+                "frac_of_burst_peak": round(per_gpu / peaks["bf16_tflops"], 4), "kernel_ms": round(ms_step, 4)}
+    tp = ROOT / "profiles" / "gemm_traffic.json"
+    if tp.exists():
+        roofline["traffic"] = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        A, B = w.host_operands()
+        A, B = A[:1], B[:1]
+        threads = O.max_threads()
+        rows, t0, done = 16, time.perf_counter(), 0
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            O.gemm_bf16(A, B, w.M, w.N, w.K, 1, row0=(done * rows) % w.M, rows=rows)
+            done += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(done * rows * 2 * w.N * w.K / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+               "kind": "port", "sample": f"{done * rows} rows of one 8192^3 GEMM (oracle, double, OpenMP) in {dt:.1f} s"}
+    return {
+        "metric": BASELINE_METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: torch Philox seed 1, normal(0,1)/sqrt(K) rounded to bf16",
+        "config": {"workload": "dense GEMM C = A.B, bf16 in, fp32 accumulate and out", "M": w.M, "N": w.N, "K": w.K,
+                   "batch": w.batch, "parallelism": f"{ws} independent batches",
+                   "l2": "A and B 1 GiB each per step, above the 126 MB L2; no flush"},
+        "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": w.plan.nkernels() * args.steps,
+        "clocks": clk.summary(),
+    }
+
+
 def profile_case(args, local):
     """Only the dominant kernel of a workload, three launches, for an ncu capture
     (`-k regex:<kernel> -c 3`); prints nothing but "ok"."""
@@ -438,6 +492,11 @@ def profile_case(args, local):
             scratch = torch.empty(max(wsb, 16), dtype=torch.uint8, device=f"cuda:{local}")
             for _ in range(3):
                 M.launch(M.kernels.scatter_add, kargs, w.n, stream=s, workspace=scratch)
+    elif args.profile == "gemm":
+        from mantle_cuda.workloads import build_gemm
+        w = build_gemm(dev, batch=1)
+        for _ in range(3):
+            M.run(w.plan)
     elif args.profile == "fft":
         from mantle_cuda.workloads import build_fft
         w = build_fft(dev, batch=4096)
@@ -494,11 +553,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["scatter", "chain", "fft"], default="scatter")
+    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm"], default="scatter")
     ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--profile", choices=["scatter", "fft"], default=None,
+    ap.add_argument("--profile", choices=["scatter", "fft", "gemm"], default=None,
                     help="launch only the workload's dominant kernel three times (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -522,6 +581,8 @@ def main():
             line = bench_chain(args, ws, rank, local, peaks, peak_kind)
         elif args.workload == "fft":
             line = bench_fft(args, ws, rank, local, peaks, peak_kind)
+        elif args.workload == "gemm":
+            line = bench_gemm(args, ws, rank, local, peaks, peak_kind)
         else:
             line = bench_scatter(args, ws, rank, local, peaks, peak_kind)
         if rank == 0:

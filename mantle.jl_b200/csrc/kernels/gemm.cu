@@ -1,0 +1,393 @@
+// Batched dense GEMM on the 5th-generation tensor cores:
+//
+//   C[b] = A[b] · B[b]     A: M×K bf16 row-major, B: K×N bf16 row-major,
+//                          C: M×N fp32 row-major, fp32 accumulation.
+//
+// One persistent CTA per SM walks output tiles of 128×256 (grouped so that the
+// CTAs running at the same time share A row-panels and B column-panels in L2).
+// Warp roles inside the 192-thread CTA:
+//   warp 0      TMA producer: one thread streams 128×64 A tiles (K-major) and
+//               four 64×64 B tiles (N-major) per k-block into a 4-stage ring
+//               of 48 KiB stages, 128-byte swizzled, completion counted on a
+//               per-stage mbarrier;
+//   warp 1      owns the tensor memory (512 columns: two 128×256 fp32
+//               accumulators) and one thread issues tcgen05.mma (M=128, N=256,
+//               K=16, both operands from shared memory through matrix
+//               descriptors), four per k-block; tcgen05.commit frees a stage
+//               when its MMAs have read it and publishes a finished
+//               accumulator;
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp reads its
+//               32 TMEM lanes = 32 rows), fp32 stores to C, then hand the
+//               accumulator back. With two accumulators the epilogue of tile
+//               i overlaps the main loop of tile i+1.
+// TMA loads use no cluster multicast: every CTA fetches its own tiles, and the
+// reuse between CTAs comes from L2.
+//
+// Shapes: any M; N and K multiples of 8 (TMA needs 16-byte row strides); edges
+// read as zeros (TMA out-of-bounds fill) and are masked on store. Buffers 16-byte
+// aligned.
+//
+// Every wait on an mbarrier is bounded by a wall-clock limit (%globaltimer);
+// a wait that runs out sets an abort flag that the other roles see, so the CTA
+// winds down, releases its tensor memory and returns, and the host reads the
+// count of such CTAs from g_gemm_timeouts.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "../mtl_internal.hpp"
+
+namespace mtl {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr uint32_t kAStage = kBM * kBK * 2;  // 16 KiB
+constexpr uint32_t kBStage = kBK * kBN * 2;  // 32 KiB
+constexpr uint32_t kStageBytes = kAStage + kBStage;
+constexpr int kGemmThreads = 192;
+constexpr int kGroupM = 16;  // tile rows per raster group
+constexpr uint32_t kTmemCols = 512;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+// ring + barriers + alignment slack
+constexpr int kGemmSmem = kStages * (int)kStageBytes + 1024 + 1024;
+
+__device__ int g_gemm_timeouts;
+
+// ── PTX wrappers ─────────────────────────────────────────────────────────────
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the phase of `bar` with the given parity. Returns false when
+// the CTA is aborting (this wait ran out, or another role's did).
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicAdd(&g_gemm_timeouts, 1);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): start address, leading and stride
+// byte offsets (all >> 4), version 1 at bit 46, 128-byte swizzle (2) at bit 61.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bit 4), bf16 A and B
+// (bits 7, 10), A K-major, B N-major (bit 16), N>>3 at bit 17, M>>4 at bit 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+struct TileCoord {
+  int b, m0, n0;
+};
+__device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tiles_n) {
+  const int64_t per = (int64_t)tiles_m * tiles_n;
+  TileCoord c;
+  c.b = (int)(t / per);
+  int r = (int)(t % per);
+  const int group = r / (kGroupM * tiles_n);
+  const int first_m = group * kGroupM;
+  const int gsize = min(kGroupM, tiles_m - first_m);
+  const int in_group = r % (kGroupM * tiles_n);
+  c.m0 = (first_m + in_group % gsize) * kBM;
+  c.n0 = (in_group / gsize) * kBN;
+  return c;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     float* __restrict__ C, int M, int N, int K, int batch) {
+  extern __shared__ unsigned char gsm_raw[];
+  // 1024-byte alignment: the 128-byte swizzle repeats every 8 rows of 128 B.
+  unsigned char* gsm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* ring = gsm;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStages * kStageBytes);
+  uint64_t* full = bars;                   // [kStages]
+  uint64_t* empty = bars + kStages;        // [kStages]
+  uint64_t* tfull = bars + 2 * kStages;    // [2]
+  uint64_t* tempty = bars + 2 * kStages + 2;  // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 4);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
+  const int64_t ntiles = (int64_t)tiles_m * tiles_n * batch;
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ── TMA producer ──
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort)) goto producer_done;
+          const uint32_t fb = smem_u32(&full[s]);
+          // B chunks that start past N feed only output columns that are never
+          // stored: they are not loaded (a box wholly outside the tensor).
+          const int nchunks = min(kBN / 64, (N - tc.n0 + 63) / 64);
+          mbar_expect_tx(fb, kAStage + (uint32_t)nchunks * (kBK * 128));
+          const uint32_t a_dst = smem_u32(ring + s * kStageBytes);
+          const uint32_t b_dst = a_dst + kAStage;
+          tma_load_3d(a_dst, &tmA, kb * kBK, tc.m0, tc.b, fb);
+          for (int c = 0; c < nchunks; ++c) tma_load_3d(b_dst + c * (kBK * 128), &tmB, tc.n0 + c * 64, kb * kBK, tc.b, fb);
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ── MMA issuer ──
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        const int a = i & 1;
+        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(a * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_phase(smem_u32(&full[s]), ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + s * kStageBytes);
+          const uint32_t b_addr = a_addr + kAStage;
+          // A: K-major, rows of 128 B, 8-row groups 1024 B apart (SBO); a K=16
+          // slice is 32 B further along the swizzled row.
+          // B: N-major, 64-column chunks kBK*128 B apart (LBO), 8-row K groups
+          // 1024 B apart (SBO); a K=16 slice is 16 rows = 2048 B further.
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc(b_addr + kk * 2048, kBK * 128, 1024);
+            tc_mma(d, ad, bd, kIdesc, (kb | kk) != 0);
+          }
+          tc_commit(smem_u32(&empty[s]));
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&tfull[a]));
+      }
+    }
+  } else {
+    // ── epilogue: warps 2..5 read TMEM lanes 32*(warp%4) .. +32 ──
+    const int q = warp & 3;
+    int i = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int a = i & 1;
+      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort)) break;
+      tc_fence_after();
+      const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+      const int row = tc.m0 + q * 32 + lane;
+      float* crow = C + ((int64_t)tc.b * M + row) * (int64_t)N;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        const int col = tc.n0 + c * 32;
+        if (row < M) {
+          if (col + 32 <= N) {
+            float4* dst = reinterpret_cast<float4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          } else {
+#pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (col + v < N) crow[col + v] = __uint_as_float(r[v]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// A 3-D bf16 tensor map: dims {inner, outer, batch}, box {64, box_outer, 1},
+// 128-byte swizzle, zeros outside the tensor.
+mtl_status make_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t batch,
+                         uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(MTL_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
+  cuuint32_t box[3] = {64, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTL_ERR_ARGUMENT, "gemm: tensor map rejected (CUresult %d)", (int)r);
+  return MTL_OK;
+}
+
+// Arguments: C (B, f32), A (B, bf16), B (B, bf16), M, N, K (i); ndrange = batch.
+mtl_status gemm_check(const LaunchArgs& la, const uint64_t* bytes) {
+  if (la.ndim != 1) return fail(MTL_ERR_ARGUMENT, "gemm: ndrange must be one-dimensional (the batch count)");
+  const int64_t M = la.a[3].i32, N = la.a[4].i32, K = la.a[5].i32, batch = la.nd[0];
+  if (M < 0 || N < 0 || K < 0) return fail(MTL_ERR_ARGUMENT, "gemm: negative dimension");
+  if (N % 8 || K % 8)
+    return fail(MTL_ERR_UNSUPPORTED, "gemm: N and K must be multiples of 8 (16-byte rows), got N=%lld K=%lld",
+                (long long)N, (long long)K);
+  const uint64_t need[3] = {(uint64_t)(batch * M * N * 4), (uint64_t)(batch * M * K * 2), (uint64_t)(batch * K * N * 2)};
+  const char* what[3] = {"C", "A", "B"};
+  for (int i = 0; i < 3; ++i) {
+    if (bytes[i] && bytes[i] < need[i])
+      return fail(MTL_ERR_ARGUMENT, "gemm: %s has %llu bytes, the launch touches %llu", what[i],
+                  (unsigned long long)bytes[i], (unsigned long long)need[i]);
+    if (la.a[i].ptr & 15) return fail(MTL_ERR_ARGUMENT, "gemm: %s must be 16-byte aligned", what[i]);
+  }
+  return MTL_OK;
+}
+
+mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  float* C = reinterpret_cast<float*>(la.a[0].ptr);
+  const void* A = reinterpret_cast<const void*>(la.a[1].ptr);
+  const void* B = reinterpret_cast<const void*>(la.a[2].ptr);
+  const int M = la.a[3].i32, N = la.a[4].i32, K = la.a[5].i32;
+  const int64_t batch = la.nd[0];
+  cudaStream_t s = (cudaStream_t)stream;
+  if (batch == 0 || M == 0 || N == 0) return MTL_OK;
+  if (batch > 65535) return fail(MTL_ERR_UNSUPPORTED, "gemm: batch above 65535");
+  if (K == 0) {
+    cudaError_t e = cudaMemsetAsync(C, 0, (size_t)batch * M * N * 4, s);
+    return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
+  }
+  CUtensorMap ta, tb;
+  if (mtl_status st = make_bf16_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, kBM)) return st;
+  if (mtl_status st = make_bf16_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, kBK)) return st;
+  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
+  const int64_t tiles = (int64_t)((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * batch;
+  const int grid = (int)std::min<int64_t>(tiles, la.sm_count);
+  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
+  return MTL_OK;
+}
+
+}  // namespace mtl

@@ -16,6 +16,8 @@ uint64_t scatter_workspace(const LaunchArgs& la);
 mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status fft_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status fft_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status gemm_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status gemm_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -136,6 +138,8 @@ static KernelDesc g_kernels[] = {
      nullptr},
     // batched complex FFT: out, in, length, inverse; ndrange = number of transforms
     {"fft_c2c", "BBii", false, 0b10, 0b01, fft_check, nullptr, fft_run, nullptr},
+    // batched bf16 GEMM, fp32 accumulate and output: C, A, B, M, N, K; ndrange = batch
+    {"gemm_bf16", "BBBiii", false, 0b110, 0b001, gemm_check, nullptr, gemm_run, nullptr},
 };
 #undef EW
 

@@ -194,6 +194,34 @@ class Buffer:
     def __len__(self) -> int:
         return self.n
 
+    @classmethod
+    def wrap(cls, dev: Device, owner, dtype=None, n: int | None = None) -> "Buffer":
+        """A persistent buffer over device memory someone else owns (a torch
+        tensor or any object with __cuda_array_interface__); `owner` is kept
+        alive as long as the buffer. dtype/n default to the owner's."""
+        if hasattr(owner, "data_ptr"):
+            ptr, nbytes = owner.data_ptr(), owner.numel() * owner.element_size()
+            dt = np.dtype(dtype) if dtype is not None else np.dtype(str(owner.dtype).replace("torch.", ""))
+        else:
+            cai = owner.__cuda_array_interface__
+            ptr = cai["data"][0]
+            dt = np.dtype(dtype) if dtype is not None else np.dtype(cai["typestr"])
+            nbytes = int(np.prod(cai["shape"])) * np.dtype(cai["typestr"]).itemsize
+        self = cls.__new__(cls)
+        self.dev = dev
+        self.dtype = dt
+        self.n = int(n) if n is not None else nbytes // dt.itemsize
+        self.shape = (self.n,)
+        self.elems = self.n
+        self.capacity = self.n
+        self.nbytes = nbytes
+        h = C.c_void_p()
+        check(lib().mtl_buffer_wrap(dev.handle, C.c_void_p(ptr), nbytes, C.byref(h)))
+        self.handle = h
+        self.ptr = ptr
+        self._owner = owner
+        return self
+
     @property
     def stride(self) -> int:
         return 1

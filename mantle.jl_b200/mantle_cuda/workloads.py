@@ -188,3 +188,55 @@ def build_fft(dev, batch: int = 16384, n: int = 4096, seed: int = 2, rank: int =
         use(p, back, write=True), use(p, spectrum, read=True), n, 1), batch))
     plan = Plan(g, **plan_kw)
     return FftWorkload(batch, n, x, spectrum, back, g, plan, {"x": x_h})
+
+
+# ── batched dense GEMM ──────────────────────────────────────────────────────
+@dataclass
+class GemmWorkload:
+    batch: int
+    M: int
+    N: int
+    K: int
+    A: Buffer
+    B: Buffer
+    C: Buffer
+    graph: Graph
+    plan: Plan
+    tensors: dict
+
+    @property
+    def flops_step(self) -> int:
+        return 2 * self.batch * self.M * self.N * self.K
+
+    def host_operands(self):
+        """A and B as bfloat16 bit patterns (uint16) on the host, (batch, M, K) and (batch, K, N)."""
+        import torch
+        a = self.tensors["A"].view(torch.int16).cpu().numpy().view(np.uint16)
+        b = self.tensors["B"].view(torch.int16).cpu().numpy().view(np.uint16)
+        return a.reshape(self.batch, self.M, self.K), b.reshape(self.batch, self.K, self.N)
+
+
+def gemm_operands(batch: int, M: int, N: int, K: int, seed: int = 1, device: str = "cuda"):
+    """A, B ~ normal(0, 1)/sqrt(K), rounded to bfloat16, drawn on the device by
+    torch's Philox generator (seed `seed`): A first, then B."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    scale = 1.0 / float(np.sqrt(K))
+    A = (torch.randn((batch, M, K), generator=g, device=device) * scale).to(torch.bfloat16)
+    B = (torch.randn((batch, K, N), generator=g, device=device) * scale).to(torch.bfloat16)
+    return A, B
+
+
+def build_gemm(dev, batch: int = 8, M: int = 8192, N: int = 8192, K: int = 8192, seed: int = 1, rank: int = 0,
+               **plan_kw) -> GemmWorkload:
+    """One pass: C[b] = A[b]·B[b] over the whole batch (bf16 in, fp32 out)."""
+    A_t, B_t = gemm_operands(batch, M, N, K, seed=seed + 1000 * rank, device=f"cuda:{dev.ordinal}")
+    A = Buffer.wrap(dev, A_t, dtype=np.uint16)
+    B = Buffer.wrap(dev, B_t, dtype=np.uint16)
+    C = Buffer(dev, np.float32, batch * M * N)
+    g = Graph(dev)
+    compute(g, "gemm", lambda p: dispatch(p, kernels.gemm_bf16, (
+        use(p, C, write=True), use(p, A, read=True), use(p, B, read=True), M, N, K), batch))
+    plan = Plan(g, **plan_kw)
+    return GemmWorkload(batch, M, N, K, A, B, C, g, plan, {"A": A_t, "B": B_t})

@@ -235,4 +235,39 @@ void oracle_fft_f32(const float* in, float* out, int64_t batch, int n, int inver
   FFT_BODY(float, in, out, batch, n, inverse, threads);
 }
 
+/* Dense GEMM checker: C[b][i][:] = sum_k A[b][i][k] * B[b][k][:] in double, for
+ * rows i in [row0, row0 + rows) of every batch b. A (M x K) and B (K x N) are
+ * row-major bfloat16 bit patterns (the top 16 bits of a float32); C is
+ * batch x rows x N doubles. Products of two bfloat16 values are exact in double,
+ * and the double sum is far inside the tolerance the GPU result is held to. */
+static inline double bf16_to_double(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return (double)f;
+}
+
+void oracle_gemm_bf16(const uint16_t* A, const uint16_t* B, double* C, int64_t M, int64_t N, int64_t K,
+                      int64_t batch, int64_t row0, int64_t rows, int threads) {
+  double* Bd = (double*)malloc(sizeof(double) * (size_t)K * (size_t)N);
+  for (int64_t b = 0; b < batch; ++b) {
+    const uint16_t* Bb = B + (size_t)b * K * N;
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
+    for (int64_t x = 0; x < K * N; ++x) Bd[x] = bf16_to_double(Bb[x]);
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(dynamic, 1)
+    for (int64_t r = 0; r < rows; ++r) {
+      const uint16_t* a = A + ((size_t)b * M + (size_t)(row0 + r)) * K;
+      double* c = C + ((size_t)b * rows + (size_t)r) * N;
+      for (int64_t n = 0; n < N; ++n) c[n] = 0.0;
+      for (int64_t k = 0; k < K; ++k) {
+        const double av = bf16_to_double(a[k]);
+        if (av == 0.0) continue;
+        const double* bk = Bd + (size_t)k * N;
+        for (int64_t n = 0; n < N; ++n) c[n] += av * bk[n];
+      }
+    }
+  }
+  free(Bd);
+}
+
 int oracle_max_threads(void) { return omp_get_max_threads(); }

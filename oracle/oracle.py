@@ -665,6 +665,9 @@ def lib():
         h.oracle_mix.argtypes = [f32p, f32p, f32p, C.c_float, C.c_int64]
         h.oracle_fft_f64.argtypes = [f32p, f64p, C.c_int64, C.c_int, C.c_int, C.c_int]
         h.oracle_fft_f32.argtypes = [f32p, f32p, C.c_int64, C.c_int, C.c_int, C.c_int]
+        u16p = C.POINTER(C.c_uint16)
+        h.oracle_gemm_bf16.argtypes = [u16p, u16p, f64p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                                       C.c_int64, C.c_int]
         h.oracle_max_threads.restype = C.c_int
         _lib = h
     return _lib
@@ -715,6 +718,29 @@ def fft(x, inverse=False, threads=0, f32=False):
         out = np.empty(x.shape, np.complex128)
         lib().oracle_fft_f64(_p(xv, C.c_float), _p(out.view(np.float64), C.c_double), batch, n, int(inverse),
                              threads)
+    return out
+
+
+def bf16_bits(x) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns (uint16), rounding to nearest, ties to even."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+def bf16_to_f32(h) -> np.ndarray:
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def gemm_bf16(A, B, M, N, K, batch=1, row0=0, rows=None, threads=0):
+    """C = A.B for bfloat16 bit-pattern inputs (batch, M, K) and (batch, K, N), in
+    double; only rows [row0, row0+rows) of each batch."""
+    rows = M - row0 if rows is None else rows
+    A = np.ascontiguousarray(A, dtype=np.uint16)
+    B = np.ascontiguousarray(B, dtype=np.uint16)
+    out = np.empty((batch, rows, N), np.float64)
+    lib().oracle_gemm_bf16(_p(A, C.c_uint16), _p(B, C.c_uint16), _p(out, C.c_double), M, N, K, batch, row0, rows,
+                           threads)
     return out
 
 
