@@ -474,6 +474,74 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
     }
 
 
+def bench_cnn(args, ws, rank, local, peaks, peak_kind):
+    """CNN inference at batch 256: the batch is split across the ranks ("scaling":
+    "strong"), each rank replays its forward graph on its images, and the
+    logits are all-gathered over NCCL every step (N > 1)."""
+    import mantle_cuda as M
+    from mantle_cuda.workloads import CNN_CLASSES, CNN_LAYERS, STEM_CPAD, build_cnn
+    from oracle import oracle as O
+
+    total = 256
+    if total % ws:
+        raise SystemExit(f"batch {total} does not split over {ws} GPUs")
+    dev = M.Device(local)
+    w = build_cnn(dev, batch=total, rank=rank, world=ws)
+    comm = gathered = None
+    if ws > 1:
+        import torch.distributed as dist
+        obj = [M.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = M.Comm(dev, ws, rank, obj[0])
+        gathered = M.Buffer(dev, np.float32, total * CNN_CLASSES)
+
+    def step():
+        M.run(w.plan)
+        if comm is not None:
+            comm.allgather(w.logits, gathered)
+
+    for _ in range(args.warmup):
+        step()
+    dev.synchronize()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = device_time_ms(dev.stream, step, args.steps)
+    ms_step = max_over_ranks(ws, ms / args.steps)
+    images_s = total / (ms_step * 1e-3)
+    flops = 2 * total * (w.flops_step // (2 * w.batch))
+    tflops = flops / (ms_step * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    per_gpu = tflops / ws
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        x, wts, fc = w.host_params()
+        threads = O.max_threads()
+        t0, done = time.perf_counter(), 0
+        while time.perf_counter() - t0 < args.cpu_seconds or done == 0:
+            O.cnn_forward(x[done % w.batch:done % w.batch + 1], wts, fc, CNN_LAYERS, STEM_CPAD)
+            done += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(done / dt, 3), "unit": "images/s", "cores": threads, "kind": "port",
+               "sample": f"{done} images through the oracle forward pass (double, OpenMP) in {dt:.1f} s"}
+    if comm is not None:
+        comm.release()
+    return {
+        "metric": BASELINE_METRIC, "value": round(images_s, 1), "unit": "images/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: torch Philox, input U[0,1) seed 4, He-normal weights seed 3",
+        "config": {"workload": "CNN inference: 7x7/2 stem, 4 stages of two 3x3 convs (64-512), ReLU, GAP, FC 1000",
+                   "global_batch": total, "image": [3, 224, 224], "parallelism": f"batch split over {ws} GPUs"
+                   + (", NCCL all-gather of the logits every step" if ws > 1 else ""),
+                   "tflops": round(tflops, 1)},
+        "roofline": {"bound": "tensor", "kernel": "the whole forward graph (9 conv2d_bf16 + 2 small kernels)",
+                     "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(per_gpu / peak, 4),
+                     "traffic": None, "algorithmic_flops": flops // ws,
+                     "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)"},
+        "cpu_baseline": cpu, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
+    }
+
+
 def profile_case(args, local):
     """Only the dominant kernel of a workload, three launches, for an ncu capture
     (`-k regex:<kernel> -c 3`); prints nothing but "ok"."""
@@ -495,6 +563,11 @@ def profile_case(args, local):
     elif args.profile == "gemm":
         from mantle_cuda.workloads import build_gemm
         w = build_gemm(dev, batch=1)
+        for _ in range(3):
+            M.run(w.plan)
+    elif args.profile == "cnn":
+        from mantle_cuda.workloads import build_cnn
+        w = build_cnn(dev, batch=64)
         for _ in range(3):
             M.run(w.plan)
     elif args.profile == "fft":
@@ -553,11 +626,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm"], default="scatter")
+    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm", "cnn"], default="scatter")
     ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--profile", choices=["scatter", "fft", "gemm"], default=None,
+    ap.add_argument("--profile", choices=["scatter", "fft", "gemm", "cnn"], default=None,
                     help="launch only the workload's dominant kernel three times (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -583,6 +656,8 @@ def main():
             line = bench_fft(args, ws, rank, local, peaks, peak_kind)
         elif args.workload == "gemm":
             line = bench_gemm(args, ws, rank, local, peaks, peak_kind)
+        elif args.workload == "cnn":
+            line = bench_cnn(args, ws, rank, local, peaks, peak_kind)
         else:
             line = bench_scatter(args, ws, rank, local, peaks, peak_kind)
         if rank == 0:

@@ -39,6 +39,7 @@
 #include <mutex>
 
 #include "../mtl_internal.hpp"
+#include "tc_common.cuh"
 
 namespace mtl {
 
@@ -49,96 +50,14 @@ constexpr uint32_t kStageBytes = kAStage + kBStage;
 constexpr int kGemmThreads = 192;
 constexpr int kGroupM = 16;  // tile rows per raster group
 constexpr uint32_t kTmemCols = 512;
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 // ring + barriers + alignment slack
 constexpr int kGemmSmem = kStages * (int)kStageBytes + 1024 + 1024;
 
 __device__ int g_gemm_timeouts;
 
-// ── PTX wrappers ─────────────────────────────────────────────────────────────
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait for the phase of `bar` with the given parity. Returns false when
-// the CTA is aborting (this wait ran out, or another role's did).
-__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        atomicAdd(&g_gemm_timeouts, 1);
-        return false;
-      }
-    }
-  }
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor (tcgen05): start address, leading and stride
-// byte offsets (all >> 4), version 1 at bit 46, 128-byte swizzle (2) at bit 61.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
-}
 // Instruction descriptor, kind::f16: fp32 accumulator (bit 4), bf16 A and B
 // (bits 7, 10), A K-major, B N-major (bit 16), N>>3 at bit 17, M>>4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, false, true);
 
 struct TileCoord {
   int b, m0, n0;
@@ -209,7 +128,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort)) goto producer_done;
+          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_gemm_timeouts)) goto producer_done;
           const uint32_t fb = smem_u32(&full[s]);
           // B chunks that start past N feed only output columns that are never
           // stored: they are not loaded (a box wholly outside the tensor).
@@ -235,12 +154,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int i = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
         const int a = i & 1;
-        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort)) break;
+        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_gemm_timeouts)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * kBN);
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!wait_phase(smem_u32(&full[s]), ph, abort)) {
+          if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_gemm_timeouts)) {
             ok = false;
             break;
           }
@@ -273,7 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int i = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const int a = i & 1;
-      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort)) break;
+      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_gemm_timeouts)) break;
       tc_fence_after();
       const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
       const int row = tc.m0 + q * 32 + lane;

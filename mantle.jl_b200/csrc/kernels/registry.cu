@@ -18,6 +18,12 @@ mtl_status fft_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status fft_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status gemm_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gemm_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status conv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status nhwc_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -140,6 +146,13 @@ static KernelDesc g_kernels[] = {
     {"fft_c2c", "BBii", false, 0b10, 0b01, fft_check, nullptr, fft_run, nullptr},
     // batched bf16 GEMM, fp32 accumulate and output: C, A, B, M, N, K; ndrange = batch
     {"gemm_bf16", "BBBiii", false, 0b110, 0b001, gemm_check, nullptr, gemm_run, nullptr},
+    // NHWC bf16 convolution (implicit GEMM): out, in, w (HWIO), H, W, Cin, Cout,
+    // k, stride, pad, relu; ndrange = images
+    {"conv2d_bf16", "BBBiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
+    // NCHW -> NHWC with zero-padded channels: out, in, C, H, W, Cpad; ndrange = images
+    {"nchw_to_nhwc_bf16", "BBiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},
+    // global average pool + fully connected: logits, act, w, HW, C, classes; ndrange = images
+    {"gap_fc", "BBBiii", false, 0b110, 0b001, gapfc_check, nullptr, gapfc_run, nullptr},
 };
 #undef EW
 

@@ -43,7 +43,7 @@ __all__ = [
     "Device", "Buffer", "Scalar", "Graph", "Transient", "compute", "custom", "use", "dispatch",
     "copy", "Update", "Plan", "run", "timings", "peakbytes", "naivebytes", "storage", "update",
     "backend", "kernels", "PassTiming", "NSAMPLES", "Overlap", "Compact", "ArgumentError",
-    "MantleError", "Storage", "CopySrc", "CopyDst", "Indirect", "Unordered", "transitions",
+    "MantleError", "Storage", "CopySrc", "CopyDst", "Indirect", "Unordered", "transitions", "Comm",
     "needs_transition", "reads", "writes", "npipelines", "Array",
 ]
 
@@ -892,3 +892,41 @@ def maxload(items: Sequence[Item]) -> int:
 def inject_failure(entry_point: str, count: int = 1) -> None:
     """Make the next `count` calls of an entry point fail (host-side fault injection)."""
     check(lib().mtl_inject_failure(entry_point.encode(), count))
+
+
+class Comm:
+    """An NCCL communicator over the GPUs of one node (one per process/GPU),
+    for the final all-gather of a sharded run. `unique_id` is NCCL's 128-byte
+    id, made by one rank with Comm.unique_id() and shared over any host channel."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().mtl_comm_unique_id(buf))
+        return buf.raw
+
+    def __init__(self, dev: Device, nranks: int, rank: int, unique_id: bytes):
+        if len(unique_id) != 128:
+            raise ArgumentError(L.ERR_ARGUMENT, "Comm: the NCCL unique id is 128 bytes")
+        h = C.c_void_p()
+        idb = C.create_string_buffer(bytes(unique_id), 128)
+        check(lib().mtl_comm_init(dev.handle, nranks, rank, idb, C.byref(h)))
+        self.handle, self.dev, self.nranks, self.rank = h, dev, nranks, rank
+
+    def allgather(self, send: Buffer, recv: Buffer, nbytes: int | None = None) -> None:
+        """recv = the concatenation of every rank's `send` (nbytes each), on the
+        device's stream."""
+        nbytes = send.nbytes if nbytes is None else int(nbytes)
+        if recv.nbytes < nbytes * self.nranks:
+            raise ArgumentError(L.ERR_ARGUMENT, f"allgather: recv holds {recv.nbytes} bytes, needs {nbytes * self.nranks}")
+        check(lib().mtl_allgather(self.handle, C.c_void_p(send.ptr), C.c_void_p(recv.ptr), nbytes))
+
+    def release(self) -> None:
+        if getattr(self, "handle", None):
+            lib().mtl_comm_release(self.handle)
+            self.handle = None
+
+    def abort(self) -> None:
+        if getattr(self, "handle", None):
+            lib().mtl_comm_abort(self.handle)
+            self.handle = None

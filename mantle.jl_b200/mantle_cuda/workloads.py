@@ -240,3 +240,116 @@ def build_gemm(dev, batch: int = 8, M: int = 8192, N: int = 8192, K: int = 8192,
         use(p, C, write=True), use(p, A, read=True), use(p, B, read=True), M, N, K), batch))
     plan = Plan(g, **plan_kw)
     return GemmWorkload(batch, M, N, K, A, B, C, g, plan, {"A": A_t, "B": B_t})
+
+
+# ── CNN inference ───────────────────────────────────────────────────────────
+# (name, kernel, cin, cout, stride): a 7x7 stride-2 stem to 64 channels, then
+# four stages of two 3x3 convolutions (64/128/256/512 channels, stride 2 at
+# each stage start), every one followed by ReLU; global average pool; 512->1000.
+CNN_LAYERS = [("stem", 7, 3, 64, 2),
+              ("s1c1", 3, 64, 64, 2), ("s1c2", 3, 64, 64, 1),
+              ("s2c1", 3, 64, 128, 2), ("s2c2", 3, 128, 128, 1),
+              ("s3c1", 3, 128, 256, 2), ("s3c2", 3, 256, 256, 1),
+              ("s4c1", 3, 256, 512, 2), ("s4c2", 3, 512, 512, 1)]
+CNN_CLASSES = 1000
+STEM_CPAD = 8  # input channels padded 3 -> 8 (16-byte pixels for the gather)
+
+
+def cnn_macs_per_image(h: int = 224, w: int = 224) -> int:
+    macs = 0
+    for _, k, cin, cout, s in CNN_LAYERS:
+        p = k // 2
+        h, w = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+        macs += h * w * cout * k * k * cin
+    return macs + CNN_LAYERS[-1][3] * CNN_CLASSES
+
+
+@dataclass
+class CnnWorkload:
+    batch: int
+    x: Buffer
+    logits: Buffer
+    weights: dict
+    graph: Graph
+    plan: Plan
+    tensors: dict
+
+    @property
+    def flops_step(self) -> int:
+        return 2 * cnn_macs_per_image() * self.batch
+
+    def host_params(self):
+        """Input (NCHW) and conv weights (HWIO, channels as stored) as bfloat16
+        bits, FC weights as float32, all on the host."""
+        import torch
+        bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+        x = bits(self.tensors["x"])
+        ws = {name: bits(self.tensors[name]) for name, *_ in CNN_LAYERS}
+        return x, ws, self.tensors["fc"].cpu().numpy()
+
+
+def cnn_parameters(seed: int = 3, device: str = "cuda"):
+    """He-normal weights (std sqrt(2 / fan_in), fan_in = k*k*Cin) in bfloat16,
+    HWIO layout, drawn in layer order from torch's Philox generator seeded
+    `seed`; the stem's padding channels are zero. FC weights float32
+    (classes x 512), drawn last."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = {}
+    for name, k, cin, cout, _ in CNN_LAYERS:
+        std = float(np.sqrt(2.0 / (k * k * cin)))
+        w = torch.randn((k, k, cin, cout), generator=g, device=device) * std
+        if name == "stem":
+            pad = torch.zeros((k, k, STEM_CPAD, cout), device=device)
+            pad[:, :, :cin] = w
+            w = pad
+        out[name] = w.to(torch.bfloat16).contiguous()
+    c = CNN_LAYERS[-1][3]
+    out["fc"] = (torch.randn((CNN_CLASSES, c), generator=g, device=device) * float(np.sqrt(2.0 / c))).contiguous()
+    return out
+
+
+def cnn_input(batch_total: int, seed: int = 3, device: str = "cuda"):
+    """NCHW bfloat16 input, uniform[0, 1), from a generator seeded seed + 1."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    return torch.rand((batch_total, 3, 224, 224), generator=g, device=device).to(torch.bfloat16)
+
+
+def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 1, **plan_kw) -> CnnWorkload:
+    """The forward pass as one graph: NCHW->NHWC, nine conv+ReLU passes over
+    transients (aliased by the placer), then GAP+FC into the logits. With
+    world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
+    import torch
+    device = f"cuda:{dev.ordinal}"
+    per = batch // world
+    x_all = cnn_input(batch, seed, device)
+    x_t = x_all[rank * per:(rank + 1) * per].contiguous()
+    del x_all
+    params = cnn_parameters(seed, device)
+    x = Buffer.wrap(dev, x_t, dtype=np.uint16)
+    W = {name: Buffer.wrap(dev, params[name], dtype=np.uint16) for name, *_ in CNN_LAYERS}
+    fc = Buffer.wrap(dev, params["fc"], dtype=np.float32)
+    logits = Buffer(dev, np.float32, per * CNN_CLASSES)
+    g = Graph(dev)
+    h = w = 224
+    cur = Transient.Buffer(g, np.uint16, per * h * w * STEM_CPAD)
+    compute(g, "to_nhwc", lambda p: dispatch(p, kernels.nchw_to_nhwc_bf16, (
+        use(p, cur, write=True), use(p, x, read=True), 3, h, w, STEM_CPAD), per))
+    cin = STEM_CPAD
+    for name, k, _, cout, s in CNN_LAYERS:
+        pad = k // 2
+        ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+        nxt = Transient.Buffer(g, np.uint16, per * ho * wo * cout)
+        compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad:
+                dispatch(p, kernels.conv2d_bf16, (use(p, dst, write=True), use(p, src, read=True),
+                                                  use(p, wt, read=True), h, w, cin, cout, k, s, pad, 1), per))
+        cur, h, w, cin = nxt, ho, wo, cout
+    compute(g, "gap_fc", lambda p: dispatch(p, kernels.gap_fc, (
+        use(p, logits, write=True), use(p, cur, read=True), use(p, fc, read=True), h * w, cin, CNN_CLASSES), per))
+    plan = Plan(g, **plan_kw)
+    tensors = dict(params)
+    tensors["x"] = x_t
+    return CnnWorkload(per, x, logits, W, g, plan, tensors)

@@ -270,4 +270,81 @@ void oracle_gemm_bf16(const uint16_t* A, const uint16_t* B, double* C, int64_t M
   free(Bd);
 }
 
+static inline uint16_t double_to_bf16(double d) {
+  float f = (float)d;
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+  return (uint16_t)u;
+}
+
+/* NHWC convolution, bf16 bit patterns in, double accumulation:
+ *   out[n][oh][ow][co] = sum_{r,c,ci} in[n][oh*s-p+r][ow*s-p+c][ci] * w[r][c][ci][co]
+ * (zero outside the image), then ReLU when relu != 0. `out_d` (may be NULL)
+ * receives the double result, `out_h` (may be NULL) the result rounded once
+ * to bfloat16 (nearest even) — the form the next layer reads. */
+void oracle_conv_bf16(const uint16_t* in, const uint16_t* w, double* out_d, uint16_t* out_h, int n, int h, int wd,
+                      int cin, int cout, int k, int stride, int pad, int relu, int threads) {
+  const int ho = (h + 2 * pad - k) / stride + 1, wo = (wd + 2 * pad - k) / stride + 1;
+  const int64_t wsz = (int64_t)k * k * cin * cout;
+  double* wf = (double*)malloc(sizeof(double) * (size_t)wsz);
+  for (int64_t x = 0; x < wsz; ++x) wf[x] = bf16_to_double(w[x]);
+#pragma omp parallel num_threads(nthreads(threads))
+  {
+    double* acc = (double*)malloc(sizeof(double) * (size_t)cout);
+#pragma omp for schedule(static) collapse(2)
+    for (int b = 0; b < n; ++b)
+      for (int oh = 0; oh < ho; ++oh)
+        for (int ow = 0; ow < wo; ++ow) {
+          for (int co = 0; co < cout; ++co) acc[co] = 0.0;
+          for (int r = 0; r < k; ++r) {
+            const int ih = oh * stride - pad + r;
+            if (ih < 0 || ih >= h) continue;
+            for (int c = 0; c < k; ++c) {
+              const int iw = ow * stride - pad + c;
+              if (iw < 0 || iw >= wd) continue;
+              const uint16_t* px = in + (((int64_t)b * h + ih) * wd + iw) * cin;
+              const double* wr = wf + ((int64_t)(r * k + c) * cin) * cout;
+              for (int ci = 0; ci < cin; ++ci) {
+                const double a = bf16_to_double(px[ci]);
+                if (a == 0.0) continue;
+                const double* wc = wr + (int64_t)ci * cout;
+                for (int co = 0; co < cout; ++co) acc[co] += a * wc[co];
+              }
+            }
+          }
+          const int64_t o = (((int64_t)b * ho + oh) * wo + ow) * cout;
+          for (int co = 0; co < cout; ++co) {
+            double v = acc[co];
+            if (relu && v < 0) v = 0;
+            if (out_d) out_d[o + co] = v;
+            if (out_h) out_h[o + co] = double_to_bf16(v);
+          }
+        }
+    free(acc);
+  }
+  free(wf);
+}
+
+/* Global average pool over hw pixels of NHWC bf16 activations, then logits =
+ * W (classes x c, float) times the means, all in double. */
+void oracle_gap_fc(const uint16_t* act, const float* w, double* logits, int n, int hw, int c, int classes,
+                   int threads) {
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
+  for (int b = 0; b < n; ++b) {
+    double* mean = (double*)malloc(sizeof(double) * (size_t)c);
+    for (int ch = 0; ch < c; ++ch) {
+      double s = 0;
+      for (int p = 0; p < hw; ++p) s += bf16_to_double(act[((int64_t)b * hw + p) * c + ch]);
+      mean[ch] = s / hw;
+    }
+    for (int j = 0; j < classes; ++j) {
+      double s = 0;
+      for (int ch = 0; ch < c; ++ch) s += mean[ch] * (double)w[(int64_t)j * c + ch];
+      logits[(int64_t)b * classes + j] = s;
+    }
+    free(mean);
+  }
+}
+
 int oracle_max_threads(void) { return omp_get_max_threads(); }

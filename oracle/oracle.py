@@ -668,6 +668,8 @@ def lib():
         u16p = C.POINTER(C.c_uint16)
         h.oracle_gemm_bf16.argtypes = [u16p, u16p, f64p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
                                        C.c_int64, C.c_int]
+        h.oracle_conv_bf16.argtypes = [u16p, u16p, f64p, u16p] + [C.c_int] * 10
+        h.oracle_gap_fc.argtypes = [u16p, f32p, f64p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
         h.oracle_max_threads.restype = C.c_int
         _lib = h
     return _lib
@@ -742,6 +744,50 @@ def gemm_bf16(A, B, M, N, K, batch=1, row0=0, rows=None, threads=0):
     lib().oracle_gemm_bf16(_p(A, C.c_uint16), _p(B, C.c_uint16), _p(out, C.c_double), M, N, K, batch, row0, rows,
                            threads)
     return out
+
+
+def conv_bf16(x, w, stride, pad, relu=True, threads=0):
+    """NHWC conv of bfloat16 bit patterns x (n, h, w, cin) with HWIO weights w
+    (k, k, cin, cout): (double result, bfloat16 result), both (n, ho, wo, cout)."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    w = np.ascontiguousarray(w, dtype=np.uint16)
+    n, h, wd, cin = x.shape
+    k, _, _, cout = w.shape
+    ho, wo = (h + 2 * pad - k) // stride + 1, (wd + 2 * pad - k) // stride + 1
+    od = np.empty((n, ho, wo, cout), np.float64)
+    oh = np.empty((n, ho, wo, cout), np.uint16)
+    lib().oracle_conv_bf16(_p(x, C.c_uint16), _p(w, C.c_uint16), _p(od, C.c_double), _p(oh, C.c_uint16), n, h, wd,
+                           cin, cout, k, stride, pad, int(relu), threads)
+    return od, oh
+
+
+def gap_fc(act, w, threads=0):
+    """act: (n, h, w, c) bfloat16 bits; w: (classes, c) float32 -> (n, classes) double."""
+    act = np.ascontiguousarray(act, dtype=np.uint16)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, h, wd, c = act.shape
+    classes = w.shape[0]
+    out = np.empty((n, classes), np.float64)
+    lib().oracle_gap_fc(_p(act, C.c_uint16), _p(w, C.c_float), _p(out, C.c_double), n, h * wd, c, classes, threads)
+    return out
+
+
+def nchw_to_nhwc(x, cpad):
+    """bfloat16 bits (n, c, h, w) -> (n, h, w, cpad) with zero channels appended."""
+    n, c, h, w = x.shape
+    out = np.zeros((n, h, w, cpad), np.uint16)
+    out[..., :c] = np.transpose(x, (0, 2, 3, 1))
+    return out
+
+
+def cnn_forward(x_nchw_bits, ws, fc, layers, cpad, threads=0):
+    """A CNN forward pass on the CPU: NCHW->NHWC (channels padded to cpad), then
+    for each (name, k, cin, cout, stride) a conv (padding k//2) in double with
+    ReLU, rounded to bfloat16 like stored activations; GAP+FC in double."""
+    a = nchw_to_nhwc(x_nchw_bits, cpad)
+    for name, k, _, cout, s in layers:
+        _, a = conv_bf16(a, ws[name], s, k // 2, relu=True, threads=threads)
+    return gap_fc(a, fc, threads=threads)
 
 
 def max_threads() -> int:

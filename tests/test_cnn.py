@@ -1,0 +1,122 @@
+"""Implicit-GEMM convolution and the CNN forward pass: the oracle against torch
+on the CPU, each CUDA kernel against the oracle on the GPU.
+
+Tolerances. A conv layer's stored output is its fp32 sum rounded once to
+bfloat16: against the oracle's double result the error is at most half a
+bfloat16 ulp (2^-9 relative) plus the fp32 accumulation error, so the layer
+tests hold |got - ref| <= 2^-8 |ref| + 1e-3 max|ref|. Logits of the whole
+network (nine bf16 roundings deep) are held to the workload's 1e-2: max|got -
+ref| <= 1e-2 max|ref|.
+"""
+import numpy as np
+import pytest
+
+import mantle_cuda as M
+from mantle_cuda.workloads import CNN_CLASSES, CNN_LAYERS, STEM_CPAD, build_cnn
+from oracle import oracle as O
+
+
+def close_layer(got_bits, ref):
+    got = O.bf16_to_f32(got_bits).astype(np.float64)
+    assert got.shape == ref.shape
+    tol = 2.0 ** -8 * np.abs(ref) + 1e-3 * np.abs(ref).max()
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance, worst {np.abs(got - ref).max()}"
+
+
+def test_oracle_conv_matches_torch():
+    import torch
+    rng = np.random.default_rng(1)
+    for (n, h, w, cin, cout, k, s, p) in [(2, 9, 11, 8, 16, 3, 2, 1), (1, 16, 16, 3, 8, 7, 2, 3), (1, 5, 5, 4, 4, 3, 1, 1)]:
+        x = O.bf16_bits(rng.standard_normal((n, h, w, cin)).astype(np.float32))
+        wt = O.bf16_bits(rng.standard_normal((k, k, cin, cout)).astype(np.float32))
+        od, oh = O.conv_bf16(x, wt, s, p, relu=True)
+        xt = torch.tensor(O.bf16_to_f32(x), dtype=torch.float64).permute(0, 3, 1, 2)
+        wtt = torch.tensor(O.bf16_to_f32(wt), dtype=torch.float64).permute(3, 2, 0, 1)
+        ref = torch.relu(torch.nn.functional.conv2d(xt, wtt, stride=s, padding=p)).permute(0, 2, 3, 1).numpy()
+        assert np.abs(od - ref).max() <= 1e-12 * max(1.0, np.abs(ref).max())
+        assert np.array_equal(oh, O.bf16_bits(od.astype(np.float32)))
+
+
+def test_oracle_gap_fc_and_layout():
+    rng = np.random.default_rng(2)
+    act = O.bf16_bits(rng.random((3, 2, 3, 16)).astype(np.float32))
+    w = rng.standard_normal((5, 16)).astype(np.float32)
+    want = O.bf16_to_f32(act).astype(np.float64).mean(axis=(1, 2)) @ w.astype(np.float64).T
+    assert np.allclose(O.gap_fc(act, w), want, rtol=1e-13, atol=1e-13)
+    x = np.arange(2 * 3 * 4 * 5, dtype=np.uint16).reshape(2, 3, 4, 5)
+    y = O.nchw_to_nhwc(x, 8)
+    assert y.shape == (2, 4, 5, 8) and np.array_equal(y[..., :3], np.transpose(x, (0, 2, 3, 1))) and not y[..., 3:].any()
+
+
+def test_cnn_flop_count():
+    from mantle_cuda.workloads import cnn_macs_per_image
+    assert cnn_macs_per_image() == 869961728
+
+
+def _rand_bits(rng, shape, scale=1.0, nonneg=False):
+    x = rng.standard_normal(shape).astype(np.float32) * scale
+    return O.bf16_bits(np.abs(x) if nonneg else x)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,h,w,cin,cout,k,s,relu", [
+    (2, 14, 14, 64, 64, 3, 1, 1),     # BN = 64, stride 1
+    (3, 15, 13, 64, 128, 3, 2, 1),    # BN = 128, stride 2, odd sizes
+    (2, 7, 7, 256, 512, 3, 1, 0),     # BN = 256, two column tiles, no ReLU
+    (2, 30, 22, 8, 64, 7, 2, 1),      # stem-like: 8 channels, 7x7, K not a multiple of 64
+    (1, 9, 9, 128, 256, 3, 2, 1),     # fewer pixels than one tile
+])
+def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
+    import torch
+    rng = np.random.default_rng(7)
+    x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
+    wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
+    pad = k // 2
+    ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
+    out = torch.full((n, ho, wo, cout), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, relu), n, stream=st)
+    torch.cuda.synchronize()
+    ref, _ = O.conv_bf16(x, wt, s, pad, relu=bool(relu))
+    close_layer(out.cpu().numpy().view(np.uint16), ref)
+
+
+@pytest.mark.gpu
+def test_conv_refusals(dev):
+    import torch
+    t = torch.zeros(1 << 20, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    with pytest.raises(M.MantleError, match="Cin must be a multiple of 8"):
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 3, 64, 3, 1, 1, 1), 1, stream=st)
+    with pytest.raises(M.MantleError, match="Cout must be a multiple of 64"):
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 8, 32, 3, 1, 1, 1), 1, stream=st)
+    with pytest.raises(M.MantleError, match="bytes"):
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 64, 64, 64, 64, 3, 1, 1, 1), 8, stream=st)
+
+
+@pytest.mark.gpu
+def test_cnn_small_batch_matches_oracle(dev):
+    w = build_cnn(dev, batch=2)
+    M.run(w.plan)
+    x, ws, fc = w.host_params()
+    want = O.cnn_forward(x, ws, fc, CNN_LAYERS, STEM_CPAD)
+    got = w.logits.array().reshape(2, CNN_CLASSES)
+    assert np.abs(got - want).max() <= 1e-2 * np.abs(want).max()
+    assert np.corrcoef(got.ravel(), want.ravel())[0, 1] > 0.9999
+    # the activations are transients: the placer aliases them
+    assert M.peakbytes(w.plan) < M.naivebytes(w.plan)
+
+
+@pytest.mark.gpu
+def test_cnn_full_batch_sampled_images(dev):
+    # The benchmark shape (batch 256); two images checked against the oracle.
+    w = build_cnn(dev)
+    M.run(w.plan)
+    x, ws, fc = w.host_params()
+    got = w.logits.array().reshape(256, CNN_CLASSES)
+    for i in (0, 201):
+        want = O.cnn_forward(x[i:i + 1], ws, fc, CNN_LAYERS, STEM_CPAD)
+        assert np.abs(got[i:i + 1] - want).max() <= 1e-2 * np.abs(want).max()
