@@ -229,11 +229,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ── host side ────────────────────────────────────────────────────────────────
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
+EncodeTiledFn encode_tiled_fn() {
   static std::once_flag once;
   static EncodeTiledFn fn = nullptr;
   std::call_once(once, [] {
@@ -251,7 +247,7 @@ static EncodeTiledFn encode_fn() {
 // 128-byte swizzle, zeros outside the tensor.
 mtl_status make_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t batch,
                          uint32_t box_outer) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return fail(MTL_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[3] = {inner, outer, batch};
   cuuint64_t strides[2] = {inner * 2, inner * outer * 2};

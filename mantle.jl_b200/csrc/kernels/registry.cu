@@ -24,6 +24,7 @@ mtl_status nhwc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+uint64_t gapfc_workspace(const LaunchArgs& la);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -147,12 +148,13 @@ static KernelDesc g_kernels[] = {
     // batched bf16 GEMM, fp32 accumulate and output: C, A, B, M, N, K; ndrange = batch
     {"gemm_bf16", "BBBiii", false, 0b110, 0b001, gemm_check, nullptr, gemm_run, nullptr},
     // NHWC bf16 convolution (implicit GEMM): out, in, w (HWIO), H, W, Cin, Cout,
-    // k, stride, pad, relu; ndrange = images
-    {"conv2d_bf16", "BBBiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
-    // NCHW -> NHWC with zero-padded channels: out, in, C, H, W, Cpad; ndrange = images
-    {"nchw_to_nhwc_bf16", "BBiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},
+    // k, stride, pad, relu, in_wpad; ndrange = images
+    {"conv2d_bf16", "BBBiiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
+    // NCHW -> NHWC with zero-padded channels and Wpad zero columns each side:
+    // out, in, C, H, W, Cpad, Wpad; ndrange = images
+    {"nchw_to_nhwc_bf16", "BBiiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},
     // global average pool + fully connected: logits, act, w, HW, C, classes; ndrange = images
-    {"gap_fc", "BBBiii", false, 0b110, 0b001, gapfc_check, nullptr, gapfc_run, nullptr},
+    {"gap_fc", "BBBiii", false, 0b110, 0b001, gapfc_check, gapfc_workspace, gapfc_run, nullptr},
 };
 #undef EW
 

@@ -252,7 +252,8 @@ CNN_LAYERS = [("stem", 7, 3, 64, 2),
               ("s3c1", 3, 128, 256, 2), ("s3c2", 3, 256, 256, 1),
               ("s4c1", 3, 256, 512, 2), ("s4c2", 3, 512, 512, 1)]
 CNN_CLASSES = 1000
-STEM_CPAD = 8  # input channels padded 3 -> 8 (16-byte pixels for the gather)
+STEM_CPAD = 8  # input channels padded 3 -> 8 (16-byte pixels)
+STEM_WPAD = 3  # zero columns stored each side of the stem's input rows (its padding)
 
 
 def cnn_macs_per_image(h: int = 224, w: int = 224) -> int:
@@ -292,7 +293,7 @@ def cnn_parameters(seed: int = 3, device: str = "cuda"):
     """He-normal weights (std sqrt(2 / fan_in), fan_in = k*k*Cin) in bfloat16,
     HWIO layout, drawn in layer order from torch's Philox generator seeded
     `seed`; the stem's padding channels are zero. FC weights float32
-    (classes x 512), drawn last."""
+    (512 x classes, inputs by outputs), drawn last."""
     import torch
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -306,7 +307,7 @@ def cnn_parameters(seed: int = 3, device: str = "cuda"):
             w = pad
         out[name] = w.to(torch.bfloat16).contiguous()
     c = CNN_LAYERS[-1][3]
-    out["fc"] = (torch.randn((CNN_CLASSES, c), generator=g, device=device) * float(np.sqrt(2.0 / c))).contiguous()
+    out["fc"] = (torch.randn((c, CNN_CLASSES), generator=g, device=device) * float(np.sqrt(2.0 / c))).contiguous()
     return out
 
 
@@ -319,7 +320,8 @@ def cnn_input(batch_total: int, seed: int = 3, device: str = "cuda"):
 
 
 def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 1, **plan_kw) -> CnnWorkload:
-    """The forward pass as one graph: NCHW->NHWC, nine conv+ReLU passes over
+    """The forward pass as one graph: NCHW->NHWC (channels padded to 8, the
+    stem's 3 padding columns stored as zeros), nine conv+ReLU passes over
     transients (aliased by the placer), then GAP+FC into the logits. With
     world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
     import torch
@@ -335,18 +337,19 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
     logits = Buffer(dev, np.float32, per * CNN_CLASSES)
     g = Graph(dev)
     h = w = 224
-    cur = Transient.Buffer(g, np.uint16, per * h * w * STEM_CPAD)
+    cur = Transient.Buffer(g, np.uint16, per * h * (w + 2 * STEM_WPAD) * STEM_CPAD)
     compute(g, "to_nhwc", lambda p: dispatch(p, kernels.nchw_to_nhwc_bf16, (
-        use(p, cur, write=True), use(p, x, read=True), 3, h, w, STEM_CPAD), per))
-    cin = STEM_CPAD
+        use(p, cur, write=True), use(p, x, read=True), 3, h, w, STEM_CPAD, STEM_WPAD), per))
+    cin, wpad = STEM_CPAD, STEM_WPAD
     for name, k, _, cout, s in CNN_LAYERS:
         pad = k // 2
         ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
         nxt = Transient.Buffer(g, np.uint16, per * ho * wo * cout)
-        compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad:
-                dispatch(p, kernels.conv2d_bf16, (use(p, dst, write=True), use(p, src, read=True),
-                                                  use(p, wt, read=True), h, w, cin, cout, k, s, pad, 1), per))
-        cur, h, w, cin = nxt, ho, wo, cout
+        compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad,
+                wpad=wpad: dispatch(p, kernels.conv2d_bf16, (use(p, dst, write=True), use(p, src, read=True),
+                                                             use(p, wt, read=True), h, w, cin, cout, k, s, pad, 1, wpad),
+                                    per))
+        cur, h, w, cin, wpad = nxt, ho, wo, cout, 0
     compute(g, "gap_fc", lambda p: dispatch(p, kernels.gap_fc, (
         use(p, logits, write=True), use(p, cur, read=True), use(p, fc, read=True), h * w, cin, CNN_CLASSES), per))
     plan = Plan(g, **plan_kw)

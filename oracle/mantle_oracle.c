@@ -326,8 +326,8 @@ void oracle_conv_bf16(const uint16_t* in, const uint16_t* w, double* out_d, uint
   free(wf);
 }
 
-/* Global average pool over hw pixels of NHWC bf16 activations, then logits =
- * W (classes x c, float) times the means, all in double. */
+/* Global average pool over hw pixels of NHWC bf16 activations, then logits[j]
+ * = sum_ch mean[ch] * w[ch][j] (w is c x classes, float), all in double. */
 void oracle_gap_fc(const uint16_t* act, const float* w, double* logits, int n, int hw, int c, int classes,
                    int threads) {
 #pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
@@ -340,7 +340,7 @@ void oracle_gap_fc(const uint16_t* act, const float* w, double* logits, int n, i
     }
     for (int j = 0; j < classes; ++j) {
       double s = 0;
-      for (int ch = 0; ch < c; ++ch) s += mean[ch] * (double)w[(int64_t)j * c + ch];
+      for (int ch = 0; ch < c; ++ch) s += mean[ch] * (double)w[(int64_t)ch * classes + j];
       logits[(int64_t)b * classes + j] = s;
     }
     free(mean);

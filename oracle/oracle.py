@@ -762,11 +762,11 @@ def conv_bf16(x, w, stride, pad, relu=True, threads=0):
 
 
 def gap_fc(act, w, threads=0):
-    """act: (n, h, w, c) bfloat16 bits; w: (classes, c) float32 -> (n, classes) double."""
+    """act: (n, h, w, c) bfloat16 bits; w: (c, classes) float32 -> (n, classes) double."""
     act = np.ascontiguousarray(act, dtype=np.uint16)
     w = np.ascontiguousarray(w, dtype=np.float32)
     n, h, wd, c = act.shape
-    classes = w.shape[0]
+    classes = w.shape[1]
     out = np.empty((n, classes), np.float64)
     lib().oracle_gap_fc(_p(act, C.c_uint16), _p(w, C.c_float), _p(out, C.c_double), n, h * wd, c, classes, threads)
     return out

@@ -41,8 +41,8 @@ def test_oracle_conv_matches_torch():
 def test_oracle_gap_fc_and_layout():
     rng = np.random.default_rng(2)
     act = O.bf16_bits(rng.random((3, 2, 3, 16)).astype(np.float32))
-    w = rng.standard_normal((5, 16)).astype(np.float32)
-    want = O.bf16_to_f32(act).astype(np.float64).mean(axis=(1, 2)) @ w.astype(np.float64).T
+    w = rng.standard_normal((16, 5)).astype(np.float32)
+    want = O.bf16_to_f32(act).astype(np.float64).mean(axis=(1, 2)) @ w.astype(np.float64)
     assert np.allclose(O.gap_fc(act, w), want, rtol=1e-13, atol=1e-13)
     x = np.arange(2 * 3 * 4 * 5, dtype=np.uint16).reshape(2, 3, 4, 5)
     y = O.nchw_to_nhwc(x, 8)
@@ -59,13 +59,22 @@ def _rand_bits(rng, shape, scale=1.0, nonneg=False):
     return O.bf16_bits(np.abs(x) if nonneg else x)
 
 
+# Inputs under 128 KiB take the cp.async gather path; larger ones with Cin a
+# multiple of 64 the TMA im2col path, and with Cin = 8 the 8-channel im2col path.
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,h,w,cin,cout,k,s,relu", [
-    (2, 14, 14, 64, 64, 3, 1, 1),     # BN = 64, stride 1
-    (3, 15, 13, 64, 128, 3, 2, 1),    # BN = 128, stride 2, odd sizes
-    (2, 7, 7, 256, 512, 3, 1, 0),     # BN = 256, two column tiles, no ReLU
-    (2, 30, 22, 8, 64, 7, 2, 1),      # stem-like: 8 channels, 7x7, K not a multiple of 64
-    (1, 9, 9, 128, 256, 3, 2, 1),     # fewer pixels than one tile
+    (2, 14, 14, 64, 64, 3, 1, 1),     # gather; BN = 64, stride 1
+    (3, 15, 13, 64, 128, 3, 2, 1),    # gather; BN = 128, stride 2, odd sizes
+    (2, 7, 7, 256, 512, 3, 1, 0),     # gather; BN = 256, two column tiles, no ReLU
+    (2, 30, 22, 8, 64, 7, 2, 1),      # gather; 8 channels, 7x7, K not a multiple of 64
+    (1, 9, 9, 128, 256, 3, 2, 1),     # gather; fewer pixels than one tile
+    (4, 28, 28, 64, 64, 3, 1, 1),     # im2col; BN = 64
+    (2, 56, 56, 64, 128, 3, 2, 1),    # im2col; stride 2, BN = 128
+    (5, 15, 17, 128, 256, 3, 1, 1),   # im2col; tiles span rows and images, ragged last tile
+    (6, 14, 14, 256, 512, 3, 2, 1),   # im2col; 7x7 outputs, BN = 256
+    (3, 7, 7, 512, 512, 3, 1, 0),     # im2col; 7x7 in and out, no ReLU
+    (2, 112, 96, 8, 64, 7, 2, 1),     # 8-channel im2col (the stem's shape)
+    (3, 61, 45, 8, 128, 7, 2, 1),     # 8-channel im2col; odd sizes
 ])
 def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     import torch
@@ -78,10 +87,56 @@ def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     wtt = torch.from_numpy(wt.view(np.int16)).cuda()
     out = torch.full((n, ho, wo, cout), -1, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, relu), n, stream=st)
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, relu, 0), n, stream=st)
     torch.cuda.synchronize()
     ref, _ = O.conv_bf16(x, wt, s, pad, relu=bool(relu))
     close_layer(out.cpu().numpy().view(np.uint16), ref)
+
+
+# An input stored with its padding columns: the 8-channel window path when the
+# stored margin equals the padding (and the input is at least 128 KiB), the
+# gather path otherwise.
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,h,w,cout,k,s,pad,wpad", [
+    (2, 112, 96, 64, 7, 2, 3, 3),     # window: the stem's geometry
+    (3, 57, 121, 128, 7, 2, 3, 3),    # window; odd sizes, BN = 128
+    (2, 40, 40, 64, 5, 1, 2, 2),      # im2col-chunk: the 8-wide window would leave the stored row
+    (1, 20, 18, 64, 7, 2, 3, 3),      # gather (small input) with a margin
+    (2, 112, 96, 64, 7, 2, 3, 4),     # im2col-chunk path: margin wider than the padding
+])
+def test_conv_with_stored_margin(dev, n, h, w, cout, k, s, pad, wpad):
+    import torch
+    rng = np.random.default_rng(11)
+    x = _rand_bits(rng, (n, h, w, 8), nonneg=True)
+    x[..., 3:] = 0  # padded channels, as the network stores them
+    wt = _rand_bits(rng, (k, k, 8, cout), scale=float(np.sqrt(2.0 / (k * k * 3))))
+    stored = np.zeros((n, h, w + 2 * wpad, 8), np.uint16)
+    stored[:, :, wpad:wpad + w] = x
+    ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+    xt = torch.from_numpy(stored.view(np.int16)).cuda()
+    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
+    out = torch.full((n, ho, wo, cout), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, 8, cout, k, s, pad, 1, wpad), n, stream=st)
+    torch.cuda.synchronize()
+    ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
+    close_layer(out.cpu().numpy().view(np.uint16), ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("w", [23, 24])  # scalar path, vector path (W a multiple of 8)
+def test_nchw_to_nhwc_with_margin(dev, w):
+    import torch
+    rng = np.random.default_rng(12)
+    x = _rand_bits(rng, (3, 3, 17, w))
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.full((3, 17, w + 6, 8), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.nchw_to_nhwc_bf16, (out, xt, 3, 17, w, 8, 3), 3, stream=st)
+    torch.cuda.synchronize()
+    want = np.zeros((3, 17, w + 6, 8), np.uint16)
+    want[:, :, 3:3 + w] = O.nchw_to_nhwc(x, 8)
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
 
 
 @pytest.mark.gpu
@@ -90,11 +145,11 @@ def test_conv_refusals(dev):
     t = torch.zeros(1 << 20, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     with pytest.raises(M.MantleError, match="Cin must be a multiple of 8"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 3, 64, 3, 1, 1, 1), 1, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 3, 64, 3, 1, 1, 1, 0), 1, stream=st)
     with pytest.raises(M.MantleError, match="Cout must be a multiple of 64"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 8, 32, 3, 1, 1, 1), 1, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 8, 32, 3, 1, 1, 1, 0), 1, stream=st)
     with pytest.raises(M.MantleError, match="bytes"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 64, 64, 64, 64, 3, 1, 1, 1), 8, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 64, 64, 64, 64, 3, 1, 1, 1, 0), 8, stream=st)
 
 
 @pytest.mark.gpu
@@ -120,3 +175,23 @@ def test_cnn_full_batch_sampled_images(dev):
     for i in (0, 201):
         want = O.cnn_forward(x[i:i + 1], ws, fc, CNN_LAYERS, STEM_CPAD)
         assert np.abs(got[i:i + 1] - want).max() <= 1e-2 * np.abs(want).max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,hw,c,classes", [(37, 49, 512, 1000), (3, 5, 64, 10)])
+def test_gap_fc_matches_oracle(dev, n, hw, c, classes):
+    import torch
+    rng = np.random.default_rng(13)
+    act = _rand_bits(rng, (n, hw, 1, c), nonneg=True)
+    w = (rng.standard_normal((c, classes)) * np.sqrt(2.0 / c)).astype(np.float32)
+    at = torch.from_numpy(act.view(np.int16)).cuda()
+    wt = torch.from_numpy(w).cuda()
+    logits = torch.full((n, classes), float("nan"), device="cuda")
+    args = (logits, at, wt, hw, c, classes)
+    scratch = torch.empty(M.workspace_bytes(M.kernels.gap_fc, args, n), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.gap_fc, args, n, stream=st, workspace=scratch)
+    torch.cuda.synchronize()
+    want = O.gap_fc(act, w)
+    got = logits.cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
