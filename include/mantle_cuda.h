@@ -307,6 +307,14 @@ mtl_status mtl_kernel_workspace(int32_t kernel, const mtl_arg* args, int32_t nar
 mtl_status mtl_launch(int32_t kernel, const mtl_arg* args, int32_t nargs, const int64_t* ndrange,
                       int32_t ndim, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Failure detection for the kernels' bounded waits (no counterpart in the
+ * reference, whose Vulkan queue waits are host-side): every spin on an
+ * mbarrier in the tensor-core and FFT kernels gives up after a
+ * wall-clock limit, records it in a device counter and lets its CTA wind
+ * down instead of hanging. *count receives how many waits ran out on the
+ * current device since the last reset; reset != 0 clears the counters. */
+mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count);
+
 /* Scatter-add / histogram that allocates nothing (no counterpart in the
  * reference). For callers that cannot call cudaMalloc on this path: scratch
  * comes from a fixed MTL_NOALLOC_SCRATCH_BYTES array compiled into the library,

@@ -64,7 +64,9 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         objs = list(ex.map(lambda s: compile_one(s, force), srcs))
     newest = max(o.stat().st_mtime for o in objs)
     if force or not OUT.exists() or OUT.stat().st_mtime < newest:
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(OUT), *map(str, objs), "-ldl", "-lpthread"]
+        # --no-undefined: a symbol missing from the library fails the build, not the first load
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-Xlinker", "--no-undefined", "-o", str(OUT),
+               *map(str, objs), "-ldl", "-lpthread", "-lrt"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

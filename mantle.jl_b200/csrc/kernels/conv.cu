@@ -732,4 +732,20 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
   return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
 }
 
+// Host: read (and with reset, clear) this file's count of bounded waits that
+// ran out on the current device.
+int conv_timeouts(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_conv_timeouts, sizeof v) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_conv_timeouts, &zero, sizeof zero);
+  }
+  return v;
+}
+
 }  // namespace mtl
+

@@ -378,4 +378,20 @@ mtl_status fft_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   return MTL_OK;
 }
 
+// Host: read (and with reset, clear) this file's count of bounded waits that
+// ran out on the current device.
+int fft_timeouts(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fft_timeouts, sizeof v) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_fft_timeouts, &zero, sizeof zero);
+  }
+  return v;
+}
+
 }  // namespace mtl
+

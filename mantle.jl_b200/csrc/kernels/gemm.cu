@@ -305,4 +305,20 @@ mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   return MTL_OK;
 }
 
+// Host: read (and with reset, clear) this file's count of bounded waits that
+// ran out on the current device.
+int gemm_timeouts(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_timeouts, sizeof v) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemm_timeouts, &zero, sizeof zero);
+  }
+  return v;
+}
+
 }  // namespace mtl
+

@@ -25,6 +25,9 @@ mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* str
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 uint64_t gapfc_workspace(const LaunchArgs& la);
+int gemm_timeouts(bool reset);
+int conv_timeouts(bool reset);
+int fft_timeouts(bool reset);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -216,5 +219,16 @@ mtl_status mtl_kernel_info(int32_t kernel, const char** name, const char** signa
 }
 
 int32_t mtl_kernel_count(void) { return mtl::kernel_count(); }
+
+mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count) {
+  if (!count) return mtl::fail(MTL_ERR_ARGUMENT, "mtl_kernel_timeouts: NULL argument");
+  int64_t total = 0;
+  for (int v : {mtl::gemm_timeouts(reset != 0), mtl::conv_timeouts(reset != 0), mtl::fft_timeouts(reset != 0)}) {
+    if (v < 0) return mtl::fail(MTL_ERR_CUDA, "mtl_kernel_timeouts: cannot read the device counters");
+    total += v;
+  }
+  *count = total;
+  return MTL_OK;
+}
 
 }  // extern "C"

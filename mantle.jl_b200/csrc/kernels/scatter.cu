@@ -196,14 +196,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) scatter_cluster_kernel(
   if (vec) {
     int64_t q = g0 + threadIdx.x;
     const int64_t stride = blockDim.x;
-    // Two groups of four per iteration keep 64 bytes per thread in flight.
-    for (; q + stride < g1; q += 2 * stride) {
-      int4 b0 = ld_nc_v4(idx + 4 * q);
-      int4 b1 = ld_nc_v4(idx + 4 * (q + stride));
-      float4 v0 = make_float4(0, 0, 0, 0), v1 = v0;
+    // Two groups of four per iteration, and the next iteration's two groups
+    // are loaded before this one's atomics are issued (the loads are volatile
+    // asm, so they stay in this order): 64 bytes per thread stay in flight
+    // while the thread works through its shared-memory atomics.
+    int4 nb0 = make_int4(0, 0, 0, 0), nb1 = nb0;
+    float4 nv0 = make_float4(0, 0, 0, 0), nv1 = nv0;
+    if (q + stride < g1) {
+      nb0 = ld_nc_v4(idx + 4 * q);
+      nb1 = ld_nc_v4(idx + 4 * (q + stride));
       if (ACC) {
-        v0 = ld_nc_v4f(v + 4 * q);
-        v1 = ld_nc_v4f(v + 4 * (q + stride));
+        nv0 = ld_nc_v4f(v + 4 * q);
+        nv1 = ld_nc_v4f(v + 4 * (q + stride));
+      }
+    }
+    for (; q + stride < g1; q += 2 * stride) {
+      const int4 b0 = nb0, b1 = nb1;
+      const float4 v0 = nv0, v1 = nv1;
+      const int64_t qn = q + 2 * stride;
+      if (qn + stride < g1) {
+        nb0 = ld_nc_v4(idx + 4 * qn);
+        nb1 = ld_nc_v4(idx + 4 * (qn + stride));
+        if (ACC) {
+          nv0 = ld_nc_v4f(v + 4 * qn);
+          nv1 = ld_nc_v4f(v + 4 * (qn + stride));
+        }
       }
       scatter_one<ACC, HIST>(b0.x, v0.x, rank, shift, acc_base, hist_base);
       scatter_one<ACC, HIST>(b0.y, v0.y, rank, shift, acc_base, hist_base);
@@ -250,11 +267,13 @@ __global__ void scatter_reduce_kernel(const float* __restrict__ ws_acc,
   if (b >= nbins) return;
   if (acc) {
     float s = accumulate ? acc[b] : 0.f;
+#pragma unroll 8
     for (int c = 0; c < nclusters; ++c) s += ws_acc[(int64_t)c * nbins + b];
     acc[b] = s;
   }
   if (hist) {
     uint32_t s = accumulate ? hist[b] : 0u;
+#pragma unroll 8
     for (int c = 0; c < nclusters; ++c) s += ws_hist[(int64_t)c * nbins + b];
     hist[b] = s;
   }

@@ -100,6 +100,7 @@ mtl_status mtl_comm_init(mtl_device* dev, int32_t nranks, int32_t rank, const vo
   if (mtl_status s = load_nccl()) return s;
   auto* c = new mtl_comm();
   c->dev = dev;
+  retain_device(dev);
   c->nranks = nranks;
   c->rank = rank;
   void* st = nullptr;
@@ -111,12 +112,14 @@ mtl_status mtl_comm_init(mtl_device* dev, int32_t nranks, int32_t rank, const vo
   cfg.blocking = 0;
   ncclResult_t r = g_nccl.CommInitRankConfig(&c->comm, nranks, u, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
+    release_device(c->dev);
     delete c;
     return fail(MTL_ERR_NCCL, "ncclCommInitRankConfig: %s", g_nccl.GetErrorString(r));
   }
   if (mtl_status s = wait_ready(c, 60.0)) {
     std::string msg = mtl_last_error();
     g_nccl.CommAbort(c->comm);
+    release_device(c->dev);
     delete c;
     return fail(s, "%s", msg.c_str());
   }
@@ -127,6 +130,7 @@ mtl_status mtl_comm_init(mtl_device* dev, int32_t nranks, int32_t rank, const vo
 mtl_status mtl_comm_release(mtl_comm* c) {
   if (!c) return MTL_OK;
   if (c->comm) g_nccl.CommDestroy(c->comm);
+  release_device(c->dev);
   delete c;
   return MTL_OK;
 }
@@ -134,6 +138,7 @@ mtl_status mtl_comm_release(mtl_comm* c) {
 mtl_status mtl_comm_abort(mtl_comm* c) {
   if (!c) return MTL_OK;
   if (c->comm) g_nccl.CommAbort(c->comm);
+  release_device(c->dev);
   delete c;
   return MTL_OK;
 }

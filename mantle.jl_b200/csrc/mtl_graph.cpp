@@ -932,11 +932,12 @@ mtl_status mtl_graph_create(mtl_device* dev, mtl_graph** out) {
   if (mtl_status s = injected("mtl_graph_create")) return s;
   *out = new mtl_graph();
   (*out)->dev = dev;
+  if (dev) retain_device(dev);
   return MTL_OK;
 }
 
 mtl_status mtl_graph_release(mtl_graph* g) {
-  delete g;
+  if (g) release_graph(g);
   return MTL_OK;
 }
 
@@ -958,7 +959,10 @@ mtl_status mtl_graph_persistent(mtl_graph* g, mtl_buffer* buf, uint64_t elems, u
   r.buf = buf;
   g->res.push_back(r);
   *rid = (int32_t)g->res.size();
-  if (buf) g->persistent_ids[buf] = *rid;
+  if (buf) {
+    g->persistent_ids[buf] = *rid;
+    retain_buffer(buf);
+  }
   return MTL_OK;
 }
 
@@ -1181,3 +1185,23 @@ mtl_status mtl_graph_pass_name(mtl_graph* g, int32_t pass, const char** name) {
 }
 
 }  // extern "C"
+
+namespace mtl {
+static std::mutex g_graph_refs_mu;
+
+void retain_graph(mtl_graph* g) {
+  std::lock_guard<std::mutex> lk(g_graph_refs_mu);
+  ++g->refs;
+}
+
+void release_graph(mtl_graph* g) {
+  {
+    std::lock_guard<std::mutex> lk(g_graph_refs_mu);
+    if (--g->refs > 0) return;
+  }
+  for (auto& kv : g->persistent_ids) release_buffer(kv.first);
+  mtl_device* dev = g->dev;
+  delete g;
+  if (dev) release_device(dev);
+}
+}  // namespace mtl

@@ -220,6 +220,7 @@ struct Analysis {
 }  // namespace mtl
 
 struct mtl_graph {
+  int refs = 1;  // the handle's own reference + one per plan
   mtl_device* dev = nullptr;
   std::vector<mtl::Resource> res;  // index = rid - 1
   std::vector<mtl::Transient> transients;
@@ -231,6 +232,17 @@ struct mtl_graph {
 };
 
 namespace mtl {
+// Lifetimes. Handles reference what they use — a graph its device and the
+// buffers it names, a plan its graph, a buffer its device — so the owner's
+// release call (Python finalizers, Julia finalizers) may come in any order;
+// the object is freed when its last reference goes.
+void retain_device(mtl_device* d);
+void release_device(mtl_device* d);
+void retain_buffer(mtl_buffer* b);
+void release_buffer(mtl_buffer* b);
+void retain_graph(mtl_graph* g);
+void release_graph(mtl_graph* g);
+
 struct CompileOpts {
   bool alias = true, coalesce = true, profile = false, fuse = false;
   int policy = MTL_POLICY_OVERLAP;

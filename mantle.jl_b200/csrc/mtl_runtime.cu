@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -30,6 +31,7 @@
 using namespace mtl;
 
 struct mtl_device {
+  std::atomic<int> refs{1};  // the handle + every graph, buffer and communicator on it
   int ordinal = 0;
   cudaStream_t stream = nullptr;
   int sm_count = 148;
@@ -40,6 +42,7 @@ struct mtl_device {
 };
 
 struct mtl_buffer {
+  std::atomic<int> refs{1};  // the handle + every graph that names it
   mtl_device* dev = nullptr;
   void* ptr = nullptr;
   uint64_t bytes = 0;
@@ -48,6 +51,31 @@ struct mtl_buffer {
 
 namespace mtl {
 int device_sm_count(mtl_device* d) { return d ? d->sm_count : 148; }
+
+void retain_device(mtl_device* d) { d->refs.fetch_add(1); }
+void release_device(mtl_device* d) {
+  if (d->refs.fetch_sub(1) != 1) return;
+  cudaSetDevice(d->ordinal);
+  if (d->stream) {
+    cudaStreamSynchronize(d->stream);
+    cudaStreamDestroy(d->stream);
+  }
+  delete d;
+}
+void retain_buffer(mtl_buffer* b) { b->refs.fetch_add(1); }
+void release_buffer(mtl_buffer* b) {
+  if (b->refs.fetch_sub(1) != 1) return;
+  mtl_device* d = b->dev;
+  if (b->owned && b->ptr) {
+    if (d) {
+      cudaSetDevice(d->ordinal);
+      cudaStreamSynchronize(d->stream);
+    }
+    cudaFree(b->ptr);
+  }
+  delete b;
+  if (d) release_device(d);
+}
 int device_ordinal(mtl_device* d) { return d ? d->ordinal : -1; }
 }
 
@@ -405,7 +433,9 @@ static void plan_free(mtl_plan* pl) {
     }
     if (pl->capture) cudaStreamDestroy(pl->capture);
   }
+  mtl_graph* g = pl->g;
   delete pl;
+  if (g) release_graph(g);
 }
 
 static double median(std::deque<double> v) {
@@ -482,13 +512,7 @@ mtl_status mtl_device_open(int32_t ordinal, uint64_t pool_cap_bytes, mtl_device*
 }
 
 mtl_status mtl_device_close(mtl_device* d) {
-  if (!d) return MTL_OK;
-  cudaSetDevice(d->ordinal);
-  if (d->stream) {
-    cudaStreamSynchronize(d->stream);
-    cudaStreamDestroy(d->stream);
-  }
-  delete d;
+  if (d) release_device(d);
   return MTL_OK;
 }
 
@@ -530,6 +554,7 @@ mtl_status mtl_buffer_alloc(mtl_device* d, uint64_t bytes, mtl_buffer** out) {
   b->dev = d;
   b->ptr = p;
   b->bytes = bytes;
+  retain_device(d);
   *out = b;
   return MTL_OK;
 }
@@ -541,6 +566,7 @@ mtl_status mtl_buffer_wrap(mtl_device* d, void* ptr, uint64_t bytes, mtl_buffer*
   b->ptr = ptr;
   b->bytes = bytes;
   b->owned = false;
+  if (d) retain_device(d);
   *out = b;
   return MTL_OK;
 }
@@ -576,15 +602,7 @@ mtl_status mtl_buffer_device_ptr(mtl_buffer* b, void** p) {
 }
 
 mtl_status mtl_buffer_release(mtl_buffer* b) {
-  if (!b) return MTL_OK;
-  if (b->owned && b->ptr) {
-    if (b->dev) {
-      cudaSetDevice(b->dev->ordinal);
-      cudaStreamSynchronize(b->dev->stream);
-    }
-    cudaFree(b->ptr);
-  }
-  delete b;
+  if (b) release_buffer(b);
   return MTL_OK;
 }
 
@@ -594,6 +612,7 @@ mtl_status mtl_plan_compile(mtl_graph* g, const mtl_plan_opts* opts, mtl_plan** 
   if (mtl_status s = injected("mtl_plan_compile")) return s;
   auto* pl = new mtl_plan();
   pl->g = g;
+  retain_graph(g);  // the plan keeps its graph (and through it the buffers) alive
   if (opts) {
     pl->o.coalesce = opts->coalesce != 0;
     pl->o.alias = opts->alias != 0;
@@ -602,12 +621,12 @@ mtl_status mtl_plan_compile(mtl_graph* g, const mtl_plan_opts* opts, mtl_plan** 
     pl->o.fuse = opts->fuse != 0;
   }
   if (pl->o.policy != MTL_POLICY_OVERLAP && pl->o.policy != MTL_POLICY_COMPACT) {
-    delete pl;
+    plan_free(pl);
     return fail(MTL_ERR_ARGUMENT, "Plan: unknown policy %d", pl->o.policy);
   }
   mtl_status st = analyze(g, pl->o, pl->a);
   if (st) {
-    delete pl;
+    plan_free(pl);
     return st;
   }
   if (!g->dev) {  // analysis only
@@ -616,13 +635,13 @@ mtl_status mtl_plan_compile(mtl_graph* g, const mtl_plan_opts* opts, mtl_plan** 
   }
   mtl_device* d = g->dev;
   if ((st = use_device(d))) {
-    delete pl;
+    plan_free(pl);
     return st;
   }
   // Every persistent resource named by the graph must have storage.
   for (size_t i = 0; i < g->res.size(); ++i)
     if (g->res[i].kind == RES_PERSISTENT && !g->res[i].buf) {
-      delete pl;
+      plan_free(pl);
       return fail(MTL_ERR_ARGUMENT, "Plan: resource %zu has no buffer", i + 1);
     }
   auto cleanup = [&](mtl_status s) {

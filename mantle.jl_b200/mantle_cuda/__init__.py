@@ -198,8 +198,16 @@ class Buffer:
     def wrap(cls, dev: Device, owner, dtype=None, n: int | None = None) -> "Buffer":
         """A persistent buffer over device memory someone else owns (a torch
         tensor or any object with __cuda_array_interface__); `owner` is kept
-        alive as long as the buffer. dtype/n default to the owner's."""
+        alive as long as the buffer. dtype/n default to the owner's.
+
+        The library runs on its own stream, which is not ordered after the
+        owner's: wrapping a torch tensor synchronises its device, so writes
+        still pending on torch's streams land before any plan reads it. Later
+        writes through the owner need the same care (or the library's stream)."""
         if hasattr(owner, "data_ptr"):
+            import torch
+            if owner.is_cuda:
+                torch.cuda.synchronize(owner.device)
             ptr, nbytes = owner.data_ptr(), owner.numel() * owner.element_size()
             dt = np.dtype(dtype) if dtype is not None else np.dtype(str(owner.dtype).replace("torch.", ""))
         else:
@@ -886,6 +894,14 @@ def maxload(items: Sequence[Item]) -> int:
     arr, keep = _items(items)
     v = C.c_int64()
     check(lib().mtl_maxload(arr, len(items), C.byref(v)))
+    return v.value
+
+
+def kernel_timeouts(reset: bool = False) -> int:
+    """How many bounded waits inside the library's kernels ran out on the
+    current device (0 in a healthy run); reset clears the count."""
+    v = C.c_int64()
+    check(lib().mtl_kernel_timeouts(int(reset), C.byref(v)))
     return v.value
 
 

@@ -132,6 +132,7 @@ PROTOTYPES = {
     "mtl_kernel_workspace": (I32, [I32, C.POINTER(Arg), I32, PI64, I32, PU64]),
     "mtl_launch": (I32, [I32, C.POINTER(Arg), I32, PI64, I32, P, U64, P]),
     "mtl_scatter_add_noalloc": (I32, [P, P, P, P, I64, I32, I32, P]),
+    "mtl_kernel_timeouts": (I32, [I32, C.POINTER(C.c_int64)]),
     "mtl_comm_unique_id": (I32, [P]),
     "mtl_comm_init": (I32, [P, I32, I32, P, PP]),
     "mtl_comm_release": (I32, [P]),

@@ -96,6 +96,26 @@ def test_scatter_matches_oracle(dev, nbins):
     np.testing.assert_allclose(acc.array(), want_a, rtol=RTOL, atol=1e-5)
 
 
+@pytest.mark.parametrize("offset", [0, 1, 3])  # elements: 0 streams tiles by bulk copy, else direct loads
+@pytest.mark.parametrize("with_acc", [True, False])
+def test_scatter_alignment_and_histogram_only(dev, offset, with_acc):
+    import torch
+    n, nbins = (1 << 19) + 3, 1 << 16
+    v = seeded_uniform(2, n + offset, 0, 1, 0)
+    idx = seeded_integers(2, n + offset, nbins, 1)
+    vt, it = torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda()
+    acc = torch.zeros(nbins, device="cuda") if with_acc else None
+    hist = torch.zeros(nbins, dtype=torch.int32, device="cuda")
+    args = (acc, hist, vt[offset:], it[offset:], nbins, 0)
+    ws = torch.empty(M.workspace_bytes(M.kernels.scatter_add, args, n), dtype=torch.uint8, device="cuda")
+    M.launch(M.kernels.scatter_add, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
+    torch.cuda.synchronize()
+    want_a, want_h = O.scatter_f64(v[offset:], idx[offset:], nbins)
+    assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h)
+    if with_acc:
+        np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
+
+
 def test_scatter_edge_cases(dev):
     nbins = 1000
     # out-of-range indices (negative and >= nbins) are skipped, never written
