@@ -25,6 +25,18 @@ mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* str
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 uint64_t gapfc_workspace(const LaunchArgs& la);
+mtl_status advect_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status advect_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status clear_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status clear_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status splat_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status splat_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status pack_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status pack_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status unpack_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status unpack_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status blur_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status blur_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 int gemm_timeouts(bool reset);
 int conv_timeouts(bool reset);
 int fft_timeouts(bool reset);
@@ -158,6 +170,13 @@ static KernelDesc g_kernels[] = {
     {"nchw_to_nhwc_bf16", "BBiiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},
     // global average pool + fully connected: logits, act, w, HW, C, classes; ndrange = images
     {"gap_fc", "BBBiii", false, 0b110, 0b001, gapfc_check, gapfc_workspace, gapfc_run, nullptr},
+    // point clouds and image chains (bench/two_scatters.jl, bench/chain.jl), headless
+    {"advect_points", "BBff", false, 0b11, 0b11, advect_check, nullptr, advect_run, nullptr},
+    {"clear_rgba", "Bffff", false, 0b0, 0b1, clear_check, nullptr, clear_run, nullptr},
+    {"splat_points", "BBBBBiiii", false, 0b11110, 0b00001, splat_check, nullptr, splat_run, nullptr},
+    {"pack_bgra8", "BB", false, 0b10, 0b01, pack_check, nullptr, pack_run, nullptr},
+    {"unpack_bgra8", "BBii", false, 0b10, 0b01, unpack_check, nullptr, unpack_run, nullptr},
+    {"blur3x3", "BBii", false, 0b10, 0b01, blur_check, nullptr, blur_run, nullptr},
 };
 #undef EW
 

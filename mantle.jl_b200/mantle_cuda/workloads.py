@@ -356,3 +356,99 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
     tensors = dict(params)
     tensors["x"] = x_t
     return CnnWorkload(per, x, logits, W, g, plan, tensors)
+
+
+# ── point clouds and the image chain (bench/two_scatters.jl, bench/chain.jl) ─
+RASTER_W, RASTER_H = 1000, 750
+
+
+def camera(angle: float, w: int = RASTER_W, h: int = RASTER_H) -> np.ndarray:
+    """The reference's orbit camera (bench/two_scatters.jl:28-40): proj * view
+    as 16 float32, column-major."""
+    eye = np.array([3.2 * np.cos(angle), 1.2, 3.2 * np.sin(angle)])
+    f = -eye / np.linalg.norm(eye)
+    r = np.cross(f, [0.0, 1.0, 0.0])
+    r /= np.linalg.norm(r)
+    u = np.cross(r, f)
+    view = np.array([[r[0], r[1], r[2], -r @ eye], [u[0], u[1], u[2], -u @ eye],
+                     [-f[0], -f[1], -f[2], f @ eye], [0, 0, 0, 1.0]])
+    tn = np.tan(60.0 * np.pi / 360.0)
+    near, far = 0.1, 100.0
+    proj = np.array([[1 / ((w / h) * tn), 0, 0, 0], [0, -1 / tn, 0, 0],
+                     [0, 0, far / (near - far), near * far / (near - far)], [0, 0, -1, 0]])
+    return (proj @ view).astype(np.float32).T.reshape(-1).copy()  # column-major
+
+
+def point_cloud(seed: int, n: int, stream: int = 0):
+    """Positions on a noisy unit sphere, the reference's `cloud` (unit normal
+    direction times 1 + 0.05 N(0,1)), and a drift velocity 0.35 N(0,1)."""
+    rng = np.random.Generator(np.random.PCG64([seed, stream]))
+    d = rng.standard_normal((n, 3)).astype(np.float32)
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    pos = (d * (1.0 + 0.05 * rng.standard_normal((n, 1)))).astype(np.float32)
+    vel = (0.35 * rng.standard_normal((n, 3))).astype(np.float32)
+    return pos, vel
+
+
+def tint(pos: np.ndarray) -> np.ndarray:
+    """The reference's colour ramp: 0.06 * (0.45 + 0.55 y, 0.55, 1 - 0.35 y, 1)."""
+    y = pos[:, 1]
+    c = np.stack([0.45 + 0.55 * y, np.full_like(y, 0.55), 1.0 - 0.35 * y, np.ones_like(y)], axis=1)
+    return (np.float32(0.06) * c.astype(np.float32)).astype(np.float32)
+
+
+@dataclass
+class RasterWorkload:
+    bufs: dict
+    graph: Graph
+    plan: Plan
+    inputs: dict
+
+
+def build_raster(dev, na: int = 200_000, nb: int = 100_000, seed: int = 0, stages: int = 3, dt: float = 1.0 / 60,
+                 angle: float = 0.0, **plan_kw) -> RasterWorkload:
+    """bench/two_scatters.jl + bench/chain.jl as one graph: advect both clouds,
+    clear the framebuffer, splat cloud A (per-point colour, size 2) and cloud B
+    (one colour, per-point sizes 1 + 3 U[0,1)) additively, read the
+    framebuffer as BGRA8, unpack it and blur it `stages` times."""
+    w, h = RASTER_W, RASTER_H
+    pa, va = point_cloud(seed, na, 0)
+    pb, vb = point_cloud(seed, nb, 1)
+    rng = np.random.Generator(np.random.PCG64([seed, 2]))
+    inputs = {"pos_a": pa, "vel_a": va, "col_a": tint(pa), "size_a": np.array([2.0], np.float32),
+              "pos_b": pb, "vel_b": vb, "col_b": np.array([[0.10, 0.04, 0.01, 1.0]], np.float32),
+              "size_b": (1.0 + 3.0 * rng.random(nb)).astype(np.float32), "mvp": camera(angle)}
+    B = {k: Buffer(dev, v.reshape(-1)) for k, v in inputs.items()}
+    B["fb"] = Buffer(dev, np.float32, 4 * w * h)
+    B["raw"] = Buffer(dev, np.uint8, 4 * w * h)
+    B["out"] = Buffer(dev, np.float32, 4 * w * h)
+    g = Graph(dev)
+    stage = [Transient.Buffer(g, np.float32, 4 * w * h) for _ in range(stages)]
+
+    def advect(p):
+        for x, v, n in (("pos_a", "vel_a", na), ("pos_b", "vel_b", nb)):
+            dispatch(p, kernels.advect_points, (use(p, B[x], read=True, write=True),
+                                                use(p, B[v], read=True, write=True), dt, 1.6), n)
+    compute(g, "advect", advect)
+    compute(g, "clear", lambda p: dispatch(p, kernels.clear_rgba, (use(p, B["fb"], write=True), 0.02, 0.02, 0.04, 1.0),
+                                           w * h))
+
+    def scatters(p):
+        fb = use(p, B["fb"], read=True, write=True)
+        for s, n, cs, ss in (("a", na, 1, 0), ("b", nb, 0, 1)):
+            dispatch(p, kernels.splat_points, (fb, use(p, B["pos_" + s], read=True), use(p, B["col_" + s], read=True),
+                                               use(p, B["size_" + s], read=True), use(p, B["mvp"], read=True),
+                                               w, h, cs, ss), n)
+    compute(g, "scatters", scatters)
+    compute(g, "copy", lambda p: dispatch(p, kernels.pack_bgra8, (use(p, B["raw"], write=True),
+                                                                  use(p, B["fb"], read=True)), w * h))
+    compute(g, "unpack", lambda p: dispatch(p, kernels.unpack_bgra8, (use(p, stage[0], write=True),
+                                                                      use(p, B["raw"], read=True), w, h), (w, h)))
+    src = stage[0]
+    for k in range(stages):
+        dst = B["out"] if k == stages - 1 else stage[k + 1]
+        compute(g, f"blur {k + 1}", lambda p, s=src, d=dst: dispatch(p, kernels.blur3x3, (
+            use(p, d, write=True), use(p, s, read=True), w, h), (w, h)))
+        src = dst
+    plan = Plan(g, **plan_kw)
+    return RasterWorkload(B, g, plan, inputs)

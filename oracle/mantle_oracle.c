@@ -12,6 +12,10 @@
  *   touch1!..touch3!   bench/stress.jl:30-45   a = a*1.0001 + b (+ c)
  *   mix!               bench/fuzz.jl:19-22     dst = a*0.5 + b*0.25 + k
  *   stir!              bench/independent.jl:37-40
+ *   advect!            bench/two_scatters.jl:46-62
+ *   unpack!, blur!     bench/chain.jl:27-40
+ *   point splat        bench/two_scatters.jl:11-26 (SCATTER: MVP projection,
+ *                      s x s point square, additive blend), restated headless
  *   the eight-op chain, the scatter-add/histogram and the batched FFT are
  *   stated by the workload definitions (no reference kernel exists for them:
  *   parity with the reference is unpinned there, and this file is the
@@ -345,6 +349,116 @@ void oracle_gap_fc(const uint16_t* act, const float* w, double* logits, int n, i
     }
     free(mean);
   }
+}
+
+/* advect!: p = pos + v*dt; if |p| > radius: n = p/r, p = n*radius,
+ * v = v - (2*(v.n))*n. pos, vel: 3 floats per point. */
+void oracle_advect(float* pos, float* vel, float dt, float radius, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float* P = pos + 3 * i;
+    float* V = vel + 3 * i;
+    const float v0 = V[0], v1 = V[1], v2 = V[2];
+    float p0 = P[0] + v0 * dt, p1 = P[1] + v1 * dt, p2 = P[2] + v2 * dt;
+    const float r = sqrtf((p0 * p0 + p1 * p1) + p2 * p2);
+    if (r > radius) {
+      const float n0 = p0 / r, n1 = p1 / r, n2 = p2 / r;
+      p0 = n0 * radius;
+      p1 = n1 * radius;
+      p2 = n2 * radius;
+      const float d = (v0 * n0 + v1 * n1) + v2 * n2;
+      const float d2 = 2.0f * d;
+      V[0] = v0 - d2 * n0;
+      V[1] = v1 - d2 * n1;
+      V[2] = v2 - d2 * n2;
+    }
+    P[0] = p0;
+    P[1] = p1;
+    P[2] = p2;
+  }
+}
+
+/* The pixels a point covers: project by the column-major MVP (the sum over
+ * columns left to right), clip to -w <= x, y <= w, 0 <= z <= w, map NDC to the
+ * W x H framebuffer, and take the pixels whose centres px + 0.5 lie in
+ * [f - s/2, f + s/2). Returns 0 when the point is clipped. */
+static int point_rect(const float* m, const float* p, float s, int w, int h, int* x0, int* x1, int* y0, int* y1) {
+  float cl[4];
+  for (int r = 0; r < 4; ++r) cl[r] = ((m[r] * p[0] + m[4 + r] * p[1]) + m[8 + r] * p[2]) + m[12 + r];
+  const float cw = cl[3];
+  if (!(cw > 0.f && cl[0] >= -cw && cl[0] <= cw && cl[1] >= -cw && cl[1] <= cw && cl[2] >= 0.f && cl[2] <= cw))
+    return 0;
+  const float hw = 0.5f * (float)w, hh = 0.5f * (float)h;
+  const float fx = (cl[0] / cw) * hw + hw, fy = (cl[1] / cw) * hh + hh;
+  float half = 0.5f * s;
+  if (half > 1e6f) half = 1e6f;
+  if (!(half > 0.f)) return 0;
+  int a = (int)ceilf((fx - half) - 0.5f), b = (int)ceilf((fx + half) - 0.5f) - 1;
+  int c = (int)ceilf((fy - half) - 0.5f), d = (int)ceilf((fy + half) - 0.5f) - 1;
+  *x0 = a < 0 ? 0 : a;
+  *x1 = b > w - 1 ? w - 1 : b;
+  *y0 = c < 0 ? 0 : c;
+  *y1 = d > h - 1 ? h - 1 : d;
+  return 1;
+}
+
+/* Additive point splat into a double RGBA framebuffer [h][w] (caller clears
+ * it); colours/sizes per point (stride 1) or shared (stride 0). */
+void oracle_splat(double* fb, const float* pos, const float* col, const float* size, const float* mvp, int w, int h,
+                  int col_stride, int size_stride, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    int x0, x1, y0, y1;
+    if (!point_rect(mvp, pos + 3 * i, size[size_stride * i], w, h, &x0, &x1, &y0, &y1)) continue;
+    const float* c = col + 4 * col_stride * i;
+    for (int py = y0; py <= y1; ++py)
+      for (int px = x0; px <= x1; ++px)
+        for (int k = 0; k < 4; ++k) fb[4 * ((int64_t)py * w + px) + k] += (double)c[k];
+  }
+}
+
+/* Framebuffer (float RGBA) to BGRA8: round(clamp(x, 0, 1) * 255), ties to even. */
+void oracle_pack_bgra8(uint8_t* dst, const float* src, int64_t npix) {
+  for (int64_t i = 0; i < npix; ++i) {
+    const int order[4] = {2, 1, 0, 3};
+    for (int k = 0; k < 4; ++k) {
+      float x = src[4 * i + order[k]];
+      x = x < 0.f ? 0.f : (x > 1.f ? 1.f : x);
+      dst[4 * i + k] = (uint8_t)nearbyintf(x * 255.0f);
+    }
+  }
+}
+
+/* unpack!: dst[i*h + j] = (R, G, B, 255)/255 from the BGRA8 pixel (i, j) at
+ * byte (j*w + i)*4. */
+void oracle_unpack_bgra8(float* dst, const uint8_t* src, int w, int h) {
+  for (int i = 0; i < w; ++i)
+    for (int j = 0; j < h; ++j) {
+      const uint8_t* b = src + ((int64_t)j * w + i) * 4;
+      float* d = dst + 4 * ((int64_t)i * h + j);
+      d[0] = (float)b[2] / 255.0f;
+      d[1] = (float)b[1] / 255.0f;
+      d[2] = (float)b[0] / 255.0f;
+      d[3] = 255.0f / 255.0f;
+    }
+}
+
+/* blur!: 3x3 box with clamp-to-edge, nine adds (di fastest), then /9. */
+void oracle_blur3x3(float* dst, const float* src, int w, int h) {
+  for (int i = 0; i < w; ++i)
+    for (int j = 0; j < h; ++j) {
+      float acc[4] = {0, 0, 0, 0};
+      for (int dj = -1; dj <= 1; ++dj) {
+        int jj = j + dj;
+        jj = jj < 0 ? 0 : (jj > h - 1 ? h - 1 : jj);
+        for (int di = -1; di <= 1; ++di) {
+          int ii = i + di;
+          ii = ii < 0 ? 0 : (ii > w - 1 ? w - 1 : ii);
+          const float* v = src + 4 * ((int64_t)ii * h + jj);
+          for (int k = 0; k < 4; ++k) acc[k] = acc[k] + v[k];
+        }
+      }
+      float* d = dst + 4 * ((int64_t)i * h + j);
+      for (int k = 0; k < 4; ++k) d[k] = acc[k] / 9.0f;
+    }
 }
 
 int oracle_max_threads(void) { return omp_get_max_threads(); }

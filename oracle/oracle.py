@@ -670,6 +670,12 @@ def lib():
                                        C.c_int64, C.c_int]
         h.oracle_conv_bf16.argtypes = [u16p, u16p, f64p, u16p] + [C.c_int] * 10
         h.oracle_gap_fc.argtypes = [u16p, f32p, f64p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        u8p = C.POINTER(C.c_uint8)
+        h.oracle_advect.argtypes = [f32p, f32p, C.c_float, C.c_float, C.c_int64]
+        h.oracle_splat.argtypes = [f64p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int64]
+        h.oracle_pack_bgra8.argtypes = [u8p, f32p, C.c_int64]
+        h.oracle_unpack_bgra8.argtypes = [f32p, u8p, C.c_int, C.c_int]
+        h.oracle_blur3x3.argtypes = [f32p, f32p, C.c_int, C.c_int]
         h.oracle_max_threads.restype = C.c_int
         _lib = h
     return _lib
@@ -788,6 +794,46 @@ def cnn_forward(x_nchw_bits, ws, fc, layers, cpad, threads=0):
     for name, k, _, cout, s in layers:
         _, a = conv_bf16(a, ws[name], s, k // 2, relu=True, threads=threads)
     return gap_fc(a, fc, threads=threads)
+
+
+def advect(pos, vel, dt, radius):
+    """advect! on copies of pos, vel (n, 3) float32; returns (pos, vel)."""
+    pos = np.ascontiguousarray(pos, np.float32).copy()
+    vel = np.ascontiguousarray(vel, np.float32).copy()
+    lib().oracle_advect(_p(pos, C.c_float), _p(vel, C.c_float), dt, radius, pos.shape[0])
+    return pos, vel
+
+
+def splat(fb, pos, col, size, mvp, w, h, col_stride, size_stride):
+    """Additive splat into fb ((h, w, 4) float64, modified and returned)."""
+    pos = np.ascontiguousarray(pos, np.float32)
+    col = np.ascontiguousarray(col, np.float32)
+    size = np.ascontiguousarray(size, np.float32)
+    mvp = np.ascontiguousarray(mvp, np.float32)
+    lib().oracle_splat(_p(fb, C.c_double), _p(pos, C.c_float), _p(col, C.c_float), _p(size, C.c_float),
+                       _p(mvp, C.c_float), w, h, col_stride, size_stride, pos.shape[0])
+    return fb
+
+
+def pack_bgra8(src):
+    src = np.ascontiguousarray(src, np.float32)
+    out = np.empty(src.shape[:-1] + (4,), np.uint8)
+    lib().oracle_pack_bgra8(_p(out, C.c_uint8), _p(src, C.c_float), src.size // 4)
+    return out
+
+
+def unpack_bgra8(src, w, h):
+    src = np.ascontiguousarray(src, np.uint8)
+    out = np.empty((w, h, 4), np.float32)
+    lib().oracle_unpack_bgra8(_p(out, C.c_float), _p(src, C.c_uint8), w, h)
+    return out
+
+
+def blur3x3(src, w, h):
+    src = np.ascontiguousarray(src, np.float32)
+    out = np.empty((w, h, 4), np.float32)
+    lib().oracle_blur3x3(_p(out, C.c_float), _p(src, C.c_float), w, h)
+    return out
 
 
 def max_threads() -> int:
