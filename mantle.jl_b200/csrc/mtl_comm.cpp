@@ -64,7 +64,10 @@ struct mtl_comm {
   int nranks = 0, rank = 0;
 };
 
-// Bounded wait for a non-blocking communicator to leave ncclInProgress.
+// Bounded wait for a non-blocking communicator to leave ncclInProgress. An
+// enqueued collective is ready within microseconds, so the first few
+// milliseconds spin (yielding the core); only a longer wait (communicator
+// setup, a peer that is late) sleeps between polls.
 static mtl_status wait_ready(mtl_comm* c, double seconds) {
   auto t0 = std::chrono::steady_clock::now();
   for (;;) {
@@ -74,7 +77,10 @@ static mtl_status wait_ready(mtl_comm* c, double seconds) {
     if (st != ncclInProgress) return fail(MTL_ERR_NCCL, "NCCL: %s", g_nccl.GetErrorString(st));
     double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (dt > seconds) return fail(MTL_ERR_TIMEOUT, "NCCL: communicator not ready after %.1f s", seconds);
-    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    if (dt < 0.005)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
   }
 }
 
