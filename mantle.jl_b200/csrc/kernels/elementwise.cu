@@ -24,20 +24,6 @@
 
 namespace mtl {
 
-enum EwOpcode : uint8_t {
-  EW_MOV = 0,
-  EW_ADD,
-  EW_SUB,
-  EW_MUL,
-  EW_FMA,
-  EW_ABS,
-  EW_SQRT,
-  EW_SIN,
-  EW_MULK,  // a * imm
-  EW_ADDK,  // a + imm
-  EW_CONST  // imm
-};
-
 constexpr int EW_MAX_IN = 6;
 constexpr int EW_MAX_OUT = 8;
 constexpr int EW_MAX_OPS = 40;

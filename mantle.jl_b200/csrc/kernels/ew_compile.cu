@@ -1,0 +1,216 @@
+// Fused elementwise runs compiled to straight-line kernels when a plan is
+// built — the counterpart of the reference's Pipelines phase, which compiles
+// each dispatch's kernel at Plan time (ext/MantleLavaExt.jl:1832-1934), never
+// per frame.
+//
+// A fused run's micro-op program (kernels/elementwise.cu) is printed as CUDA
+// C++: one __global__ function whose body is the program's ops as plain
+// statements on scalar registers, applied to the four lanes of each 128-bit
+// load. It is compiled with NVRTC for sm_100a straight to a cubin (no PTX is
+// read or kept), loaded with cudaLibraryLoadData and cached by its source
+// text, so a plan rebuilt with the same chain reuses the kernel. The
+// statements use the same round-to-nearest intrinsics as the interpreter, so
+// results are bit-identical to it and to the oracle.
+//
+// NVRTC is opened with dlopen; where it is missing, or a pointer is not 16-byte
+// aligned, the run keeps the interpreter kernel.
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "../mtl_internal.hpp"
+
+namespace mtl {
+
+namespace {
+struct Nvrtc {
+  void* h = nullptr;
+  nvrtcResult (*Create)(nvrtcProgram*, const char*, const char*, int, const char* const*, const char* const*) = nullptr;
+  nvrtcResult (*Compile)(nvrtcProgram, int, const char* const*) = nullptr;
+  nvrtcResult (*LogSize)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*Log)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*CubinSize)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*Cubin)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*Destroy)(nvrtcProgram*) = nullptr;
+  bool tried = false;
+};
+Nvrtc g_rtc;
+std::mutex g_rtc_mu;
+std::map<std::string, cudaKernel_t> g_compiled;
+
+bool load_nvrtc() {
+  if (g_rtc.tried) return g_rtc.h != nullptr;
+  g_rtc.tried = true;
+  void* h = dlopen("libnvrtc.so.12", RTLD_NOW | RTLD_LOCAL);
+  if (!h) h = dlopen("libnvrtc.so", RTLD_NOW | RTLD_LOCAL);
+  if (!h) return false;
+#define SYM(f, n)                           \
+  *(void**)(&g_rtc.f) = dlsym(h, n);        \
+  if (!g_rtc.f) {                           \
+    dlclose(h);                             \
+    return false;                           \
+  }
+  SYM(Create, "nvrtcCreateProgram");
+  SYM(Compile, "nvrtcCompileProgram");
+  SYM(LogSize, "nvrtcGetProgramLogSize");
+  SYM(Log, "nvrtcGetProgramLog");
+  SYM(CubinSize, "nvrtcGetCUBINSize");
+  SYM(Cubin, "nvrtcGetCUBIN");
+  SYM(Destroy, "nvrtcDestroyProgram");
+#undef SYM
+  g_rtc.h = h;
+  return true;
+}
+
+std::string reg(int r) { return "r" + std::to_string(r); }
+
+std::string imm(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  char buf[40];
+  snprintf(buf, sizeof buf, "__int_as_float(0x%08x)", u);
+  return buf;
+}
+
+std::string op_expr(const EwOp& o) {
+  const std::string a = reg(o.a), b = reg(o.b), c = reg(o.c);
+  switch (o.op) {
+    case EW_MOV: return a;
+    case EW_ADD: return "__fadd_rn(" + a + ", " + b + ")";
+    case EW_SUB: return "__fsub_rn(" + a + ", " + b + ")";
+    case EW_MUL: return "__fmul_rn(" + a + ", " + b + ")";
+    case EW_FMA: return "__fmaf_rn(" + a + ", " + b + ", " + c + ")";
+    case EW_ABS: return "fabsf(" + a + ")";
+    case EW_SQRT: return "__fsqrt_rn(" + a + ")";
+    case EW_SIN: return "sinf(" + a + ")";
+    case EW_MULK: return "__fmul_rn(" + a + ", " + imm(o.imm) + ")";
+    case EW_ADDK: return "__fadd_rn(" + a + ", " + imm(o.imm) + ")";
+    default: return imm(o.imm);
+  }
+}
+
+std::string source(const EwProgram& p) {
+  const int nin = (int)p.inputs.size(), nout = (int)p.outputs.size();
+  std::string params;
+  for (int i = 0; i < nin; ++i) params += "const float* __restrict__ in" + std::to_string(i) + ", ";
+  for (int j = 0; j < nout; ++j) params += "float* __restrict__ out" + std::to_string(j) + ", ";
+  // elem(): the program on one element. Registers r0..r(nin-1) start as the
+  // inputs; the ops are the program's, in order; outputs are read at the end.
+  std::string loads;
+  for (int i = 0; i < nin; ++i) loads += "  " + reg(i) + " = x" + std::to_string(i) + ";\n";
+  std::string decls, ops;
+  for (int r = 0; r < p.nregs; ++r) decls += "  float " + reg(r) + " = 0.f; (void)" + reg(r) + ";\n";
+  for (const EwOp& o : p.ops) ops += "  " + reg(o.dst) + " = " + op_expr(o) + ";\n";
+  std::string stores;
+  for (int j = 0; j < nout; ++j) stores += "  y" + std::to_string(j) + " = " + reg(p.out_regs[j]) + ";\n";
+  std::string fn = "__device__ __forceinline__ void elem(";
+  for (int i = 0; i < nin; ++i) fn += "float x" + std::to_string(i) + ", ";
+  for (int j = 0; j < nout; ++j) fn += std::string(j ? ", " : "") + "float& y" + std::to_string(j);
+  fn += ") {\n" + decls + loads + ops + stores + "}\n";
+
+  std::string k = fn + "extern \"C\" __global__ void __launch_bounds__(256) mtl_fused(" + params + "long long n) {\n";
+  k += "  const long long groups = n >> 2;\n";
+  k += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
+  k += "  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += stride) {\n";
+  for (int i = 0; i < nin; ++i)
+    k += "    const float4 v" + std::to_string(i) + " = __ldg(reinterpret_cast<const float4*>(in" + std::to_string(i) +
+         ") + g);\n";
+  for (int j = 0; j < nout; ++j) k += "    float4 w" + std::to_string(j) + ";\n";
+  for (const char* lane : {"x", "y", "z", "w"}) {
+    k += "    elem(";
+    for (int i = 0; i < nin; ++i) k += "v" + std::to_string(i) + "." + lane + ", ";
+    for (int j = 0; j < nout; ++j) k += std::string(j ? ", " : "") + "w" + std::to_string(j) + "." + lane;
+    k += ");\n";
+  }
+  for (int j = 0; j < nout; ++j)
+    k += "    reinterpret_cast<float4*>(out" + std::to_string(j) + ")[g] = w" + std::to_string(j) + ";\n";
+  k += "  }\n";
+  // the ragged tail (at most three elements), one per thread of block 0
+  k += "  const long long t = (groups << 2) + threadIdx.x;\n";
+  k += "  if (blockIdx.x == 0 && t < n) {\n";
+  for (int j = 0; j < nout; ++j) k += "    float y" + std::to_string(j) + ";\n";
+  k += "    elem(";
+  for (int i = 0; i < nin; ++i) k += "in" + std::to_string(i) + "[t], ";
+  for (int j = 0; j < nout; ++j) k += std::string(j ? ", " : "") + "y" + std::to_string(j);
+  k += ");\n";
+  for (int j = 0; j < nout; ++j) k += "    out" + std::to_string(j) + "[t] = y" + std::to_string(j) + ";\n";
+  k += "  }\n}\n";
+  return k;
+}
+}  // namespace
+
+// Compile (or find) the straight-line kernel of a program. Returns MTL_OK with
+// *kernel set, or MTL_ERR_UNSUPPORTED when it cannot be compiled here (the
+// caller then keeps the interpreter). Makes no stream operation: call it
+// outside stream capture.
+mtl_status ew_compile(const EwProgram& p, void** kernel) {
+  *kernel = nullptr;
+  if (p.outputs.empty()) return fail(MTL_ERR_UNSUPPORTED, "nothing to compile");
+  const std::string src = source(p);
+  std::lock_guard<std::mutex> lk(g_rtc_mu);
+  auto it = g_compiled.find(src);
+  if (it != g_compiled.end()) {
+    *kernel = (void*)it->second;
+    return MTL_OK;
+  }
+  if (!load_nvrtc()) return fail(MTL_ERR_UNSUPPORTED, "NVRTC is not available");
+  nvrtcProgram prog;
+  if (g_rtc.Create(&prog, src.c_str(), "mtl_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
+    return fail(MTL_ERR_UNSUPPORTED, "NVRTC: cannot create the program");
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17"};
+  nvrtcResult r = g_rtc.Compile(prog, 2, opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    g_rtc.LogSize(prog, &n);
+    std::string log(n, '\0');
+    if (n) g_rtc.Log(prog, &log[0]);
+    g_rtc.Destroy(&prog);
+    return fail(MTL_ERR_UNSUPPORTED, "NVRTC could not compile a fused run: %s", log.c_str());
+  }
+  size_t n = 0;
+  g_rtc.CubinSize(prog, &n);
+  std::string cubin(n, '\0');
+  g_rtc.Cubin(prog, &cubin[0]);
+  g_rtc.Destroy(&prog);
+  cudaLibrary_t lib = nullptr;
+  cudaError_t e = cudaLibraryLoadData(&lib, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
+  cudaKernel_t k = nullptr;
+  if (e == cudaSuccess) e = cudaLibraryGetKernel(&k, lib, "mtl_fused");
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MTL_ERR_UNSUPPORTED, "loading a compiled fused run: %s", cudaGetErrorString(e));
+  }
+  g_compiled[src] = k;  // libraries stay loaded for the process: plans may share them
+  *kernel = (void*)k;
+  return MTL_OK;
+}
+
+// Launch a compiled program (pointers must be 16-byte aligned).
+mtl_status ew_launch_compiled(void* kernel, const EwProgram& p, void* stream) {
+  const int nin = (int)p.inputs.size(), nout = (int)p.outputs.size();
+  std::vector<void*> args;
+  std::vector<uint64_t> ptrs(nin + nout);
+  for (int i = 0; i < nin; ++i) ptrs[i] = p.inputs[i];
+  for (int j = 0; j < nout; ++j) ptrs[nin + j] = p.outputs[j];
+  long long n = p.n;
+  for (auto& x : ptrs) args.push_back(&x);
+  args.push_back(&n);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long groups = n / 4;
+  const long long blocks = std::max<long long>(1, std::min<long long>((groups + 255) / 256, (long long)sms * 4));
+  cudaError_t e = cudaLaunchKernel((const void*)kernel, dim3((unsigned)blocks), dim3(256), args.data(), 0,
+                                   (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "compiled fused run: %s", cudaGetErrorString(e));
+  return MTL_OK;
+}
+
+}  // namespace mtl

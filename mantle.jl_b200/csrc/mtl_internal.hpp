@@ -102,6 +102,19 @@ struct EwOp {
   uint8_t op, dst, a, b, c;
   float imm;
 };
+enum EwOpcode : uint8_t {
+  EW_MOV = 0,
+  EW_ADD,
+  EW_SUB,
+  EW_MUL,
+  EW_FMA,
+  EW_ABS,
+  EW_SQRT,
+  EW_SIN,
+  EW_MULK,  // a * imm
+  EW_ADDK,  // a + imm
+  EW_CONST  // imm
+};
 
 struct KernelDesc {
   const char* name;
@@ -150,6 +163,10 @@ mtl_status ew_build_program(const std::vector<EwMember>& ms, const std::vector<u
 mtl_status ew_launch_single(const KernelDesc* kd, const LaunchArgs& la, void* stream);
 // Whether a built program is within the limits of the fused kernel.
 bool ew_program_fits(const EwProgram& p);
+// A program compiled to a straight-line kernel (kernels/ew_compile.cu): compile
+// (cached; outside stream capture) and launch.
+mtl_status ew_compile(const EwProgram& p, void** kernel);
+mtl_status ew_launch_compiled(void* kernel, const EwProgram& p, void* stream);
 // Validates and launches any built-in kernel (elementwise or not).
 mtl_status launch_kernel(int kernel, const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 

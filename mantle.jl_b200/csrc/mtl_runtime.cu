@@ -267,6 +267,15 @@ static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
   for (int rid : pl->a.elided) elided.push_back(((uint64_t)1 << 63) | (uint64_t)rid);
   EwProgram prog;
   if (mtl_status s = ew_build_program(ms, elided, prog)) return s;
+  // Straight-line code for the run, compiled now (never per frame); the
+  // interpreter kernel when that is not possible here.
+  bool aligned = prog.n > 0 && ew_program_fits(prog);
+  for (uint64_t x : prog.inputs) aligned &= x % 16 == 0;
+  for (uint64_t x : prog.outputs) aligned &= x % 16 == 0;
+  void* compiled = nullptr;
+  if (aligned && ew_compile(prog, &compiled) != MTL_OK) compiled = nullptr;
+  if (compiled)
+    return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_compiled(compiled, prog, s); }, out);
   return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_program(prog, s); }, out);
 }
 
