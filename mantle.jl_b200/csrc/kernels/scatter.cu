@@ -327,11 +327,27 @@ mtl_status scatter_check(const LaunchArgs& la, const uint64_t* bytes) {
   return need(3, (uint64_t)n * 4, "indices");
 }
 
+// Scratch for the clusters' partial bins. With both an accumulator and a
+// histogram the two tables are best applied by two launches of one table each
+// (2-CTA clusters on every SM instead of 4-CTA clusters, which fit 132 of 148
+// SMs): that takes scatter_workspace bytes. scatter_workspace_min is what the
+// one-launch form needs; scatter_run picks the form the scratch it gets allows.
+static uint64_t combined_bytes(const LaunchArgs& la, int tables) {
+  ScatterShape sh = scatter_shape(la.a[4].i32, tables, la.sm_count, la.device);
+  return sh.cluster ? (uint64_t)sh.nclusters * tables * (uint64_t)la.a[4].i32 * 4 : 0;
+}
+static uint64_t split_bytes(const LaunchArgs& la) {
+  ScatterShape sh = scatter_shape(la.a[4].i32, 1, la.sm_count, la.device);
+  return sh.cluster ? 2 * (uint64_t)sh.nclusters * (uint64_t)la.a[4].i32 * 4 : 0;
+}
+uint64_t scatter_workspace_min(const LaunchArgs& la) {
+  int tables = (la.a[0].kind != MTL_ARG_NULL) + (la.a[1].kind != MTL_ARG_NULL);
+  return combined_bytes(la, tables);
+}
 uint64_t scatter_workspace(const LaunchArgs& la) {
   int tables = (la.a[0].kind != MTL_ARG_NULL) + (la.a[1].kind != MTL_ARG_NULL);
-  ScatterShape sh = scatter_shape(la.a[4].i32, tables, la.sm_count, la.device);
-  if (!sh.cluster) return 0;
-  return (uint64_t)sh.nclusters * tables * (uint64_t)la.a[4].i32 * 4;
+  const uint64_t one = combined_bytes(la, tables);
+  return tables == 2 && one ? std::max(one, split_bytes(la)) : one;
 }
 
 template <bool ACC, bool HIST>
@@ -369,7 +385,24 @@ mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* 
   const int tables = (acc != nullptr) + (hist != nullptr);
   ScatterShape sh = scatter_shape(nbins, tables, la.sm_count, la.device);
   cudaError_t e = cudaSuccess;
-  if (sh.cluster) {
+  if (sh.cluster && tables == 2 && ws && ws_bytes >= split_bytes(la)) {
+    // Two launches of one table each, then one reduction of both.
+    ScatterShape s1 = scatter_shape(nbins, 1, la.sm_count, la.device);
+    float* ws_acc = reinterpret_cast<float*>(ws);
+    uint32_t* ws_hist = reinterpret_cast<uint32_t*>(ws) + (uint64_t)s1.nclusters * nbins;
+    int ncl = s1.nclusters;
+    if (n > 0) {
+      e = launch_cluster<true, false>(s1, s, v, idx, n, nbins, ws_acc, nullptr);
+      if (e == cudaSuccess) e = launch_cluster<false, true>(s1, s, v, idx, n, nbins, nullptr, ws_hist);
+    } else {
+      ncl = 0;
+    }
+    if (e == cudaSuccess) {
+      unsigned blocks = (unsigned)((nbins + 255) / 256);
+      scatter_reduce_kernel<<<blocks, 256, 0, s>>>(ws_acc, ws_hist, ncl, nbins, acc, hist, accumulate);
+      e = cudaGetLastError();
+    }
+  } else if (sh.cluster) {
     uint64_t need = (uint64_t)sh.nclusters * tables * (uint64_t)nbins * 4;
     if (!ws || ws_bytes < need)
       return fail(MTL_ERR_ARGUMENT, "scatter_add: needs %llu bytes of scratch, got %llu",

@@ -28,7 +28,7 @@
 #include "mtl_internal.hpp"
 
 namespace mtl {
-uint64_t scatter_workspace(const LaunchArgs& la);
+uint64_t scatter_workspace_min(const LaunchArgs& la);
 }
 
 using namespace mtl;
@@ -103,7 +103,8 @@ extern "C" mtl_status mtl_scatter_add_noalloc(float* acc, uint32_t* hist, const 
   la.a.push_back(accu);
   if (nbins <= 0) return fail(MTL_ERR_ARGUMENT, "scatter_add_noalloc: nbins must be positive");
 
-  const uint64_t need = scatter_workspace(la);
+  // the smallest scratch the scatter can run with (its one-launch form)
+  const uint64_t need = scatter_workspace_min(la);
   if (need > MTL_NOALLOC_SCRATCH_BYTES)
     return fail(MTL_ERR_ARGUMENT,
                 "scatter_add_noalloc: %d bins need %llu bytes of scratch; this entry point has a fixed "
