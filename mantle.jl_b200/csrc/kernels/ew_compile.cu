@@ -118,20 +118,35 @@ std::string source(const EwProgram& p) {
   std::string k = fn + "extern \"C\" __global__ void __launch_bounds__(256) mtl_fused(" + params + "long long n) {\n";
   k += "  const long long groups = n >> 2;\n";
   k += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
-  k += "  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += stride) {\n";
-  for (int i = 0; i < nin; ++i)
-    k += "    const float4 v" + std::to_string(i) + " = __ldg(reinterpret_cast<const float4*>(in" + std::to_string(i) +
-         ") + g);\n";
-  for (int j = 0; j < nout; ++j) k += "    float4 w" + std::to_string(j) + ";\n";
-  for (const char* lane : {"x", "y", "z", "w"}) {
-    k += "    elem(";
-    for (int i = 0; i < nin; ++i) k += "v" + std::to_string(i) + "." + lane + ", ";
-    for (int j = 0; j < nout; ++j) k += std::string(j ? ", " : "") + "w" + std::to_string(j) + "." + lane;
-    k += ");\n";
-  }
-  for (int j = 0; j < nout; ++j)
-    k += "    reinterpret_cast<float4*>(out" + std::to_string(j) + ")[g] = w" + std::to_string(j) + ";\n";
+  // Two groups per thread per iteration (g and g + stride): every load of
+  // both is issued before any arithmetic, so twice the bytes are in flight.
+  auto group = [&](const std::string& gi, const std::string& tag) {
+    std::string t;
+    for (int i = 0; i < nin; ++i)
+      t += "      const float4 v" + tag + std::to_string(i) + " = __ldg(reinterpret_cast<const float4*>(in" +
+           std::to_string(i) + ") + " + gi + ");\n";
+    return t;
+  };
+  auto apply = [&](const std::string& gi, const std::string& tag) {
+    std::string t;
+    for (int j = 0; j < nout; ++j) t += "      float4 w" + tag + std::to_string(j) + ";\n";
+    for (const char* lane : {"x", "y", "z", "w"}) {
+      t += "      elem(";
+      for (int i = 0; i < nin; ++i) t += "v" + tag + std::to_string(i) + "." + lane + ", ";
+      for (int j = 0; j < nout; ++j) t += std::string(j ? ", " : "") + "w" + tag + std::to_string(j) + "." + lane;
+      t += ");\n";
+    }
+    for (int j = 0; j < nout; ++j)
+      t += "      reinterpret_cast<float4*>(out" + std::to_string(j) + ")[" + gi + "] = w" + tag + std::to_string(j) +
+           ";\n";
+    return t;
+  };
+  k += "  long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
+  k += "  for (; g + stride < groups; g += 2 * stride) {\n";
+  k += "    {\n" + group("g", "a") + group("g + stride", "b") + apply("g", "a") + apply("g + stride", "b") +
+       "    }\n";
   k += "  }\n";
+  k += "  if (g < groups) {\n" + group("g", "a") + apply("g", "a") + "  }\n";
   // the ragged tail (at most three elements), one per thread of block 0
   k += "  const long long t = (groups << 2) + threadIdx.x;\n";
   k += "  if (blockIdx.x == 0 && t < n) {\n";
@@ -147,9 +162,9 @@ std::string source(const EwProgram& p) {
 }  // namespace
 
 // Compile (or find) the straight-line kernel of a program. Returns MTL_OK with
-// *kernel set, or MTL_ERR_UNSUPPORTED when it cannot be compiled here (the
-// caller then keeps the interpreter). Makes no stream operation: call it
-// outside stream capture.
+// *kernel set; MTL_ERR_UNSUPPORTED when NVRTC is not on this machine (the
+// caller then keeps the interpreter); any other failure is an error. Makes no
+// stream operation: call it outside stream capture.
 mtl_status ew_compile(const EwProgram& p, void** kernel) {
   *kernel = nullptr;
   if (p.outputs.empty()) return fail(MTL_ERR_UNSUPPORTED, "nothing to compile");
@@ -163,7 +178,7 @@ mtl_status ew_compile(const EwProgram& p, void** kernel) {
   if (!load_nvrtc()) return fail(MTL_ERR_UNSUPPORTED, "NVRTC is not available");
   nvrtcProgram prog;
   if (g_rtc.Create(&prog, src.c_str(), "mtl_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
-    return fail(MTL_ERR_UNSUPPORTED, "NVRTC: cannot create the program");
+    return fail(MTL_ERR_CUDA, "NVRTC: cannot create the program");
   const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17"};
   nvrtcResult r = g_rtc.Compile(prog, 2, opts);
   if (r != NVRTC_SUCCESS) {
@@ -172,7 +187,7 @@ mtl_status ew_compile(const EwProgram& p, void** kernel) {
     std::string log(n, '\0');
     if (n) g_rtc.Log(prog, &log[0]);
     g_rtc.Destroy(&prog);
-    return fail(MTL_ERR_UNSUPPORTED, "NVRTC could not compile a fused run: %s", log.c_str());
+    return fail(MTL_ERR_CUDA, "NVRTC could not compile a fused run: %s", log.c_str());
   }
   size_t n = 0;
   g_rtc.CubinSize(prog, &n);
@@ -185,7 +200,7 @@ mtl_status ew_compile(const EwProgram& p, void** kernel) {
   if (e == cudaSuccess) e = cudaLibraryGetKernel(&k, lib, "mtl_fused");
   if (e != cudaSuccess) {
     cudaGetLastError();
-    return fail(MTL_ERR_UNSUPPORTED, "loading a compiled fused run: %s", cudaGetErrorString(e));
+    return fail(MTL_ERR_CUDA, "loading a compiled fused run: %s", cudaGetErrorString(e));
   }
   g_compiled[src] = k;  // libraries stay loaded for the process: plans may share them
   *kernel = (void*)k;

@@ -273,7 +273,10 @@ static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
   for (uint64_t x : prog.inputs) aligned &= x % 16 == 0;
   for (uint64_t x : prog.outputs) aligned &= x % 16 == 0;
   void* compiled = nullptr;
-  if (aligned && ew_compile(prog, &compiled) != MTL_OK) compiled = nullptr;
+  if (aligned) {
+    mtl_status st = ew_compile(prog, &compiled);
+    if (st != MTL_OK && st != MTL_ERR_UNSUPPORTED) return st;  // NVRTC present but failing: an error
+  }
   if (compiled)
     return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_compiled(compiled, prog, s); }, out);
   return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_program(prog, s); }, out);
