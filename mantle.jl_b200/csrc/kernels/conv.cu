@@ -24,6 +24,7 @@
 // gap_fc: global average pool over H×W per channel (fp32, into scratch), then
 //   a fully connected layer (fp32 weights [C][classes]) to fp32 logits.
 
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -31,6 +32,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "../mtl_internal.hpp"
 #include "tc_common.cuh"
@@ -41,7 +43,14 @@ __device__ int g_conv_timeouts;
 
 struct ConvShape {
   int n, h, w, cin, cout, k, stride, pad, ho, wo;
+  // Rectangular M tiles (the *_RECT paths): th x tw output pixels of one image,
+  // tiles_x x tiles_y of them per image. 0 for flat tiles of 128 pixels.
+  int tw, th, tiles_x, tiles_y;
   int wpad, ws;   // zero columns stored on each side of every input row; stored width w + 2*wpad
+  int owp, wso;   // the same for the output rows (written as zeros); stored output width wo + 2*owp
+  // A_HALO: halo rows per channel block, tiles per image, A stages and their
+  // bytes, column blocks (Cout / BN)
+  int halo_rows, halo_tiles, halo_stages, halo_stage_bytes, nblk;
   int taps, cpt;  // kh*kw; 16-byte chunks per pixel (cin / 8)
   int kblocks;    // ceil(taps * cin / 64)
   int64_t mtot;   // n * ho * wo
@@ -69,8 +78,24 @@ enum AMode {
   // 16*(8 - stride) bytes) stepping `stride` pixels per output column. The
   // filter row is widened to 8 taps; the weights come through a 4-D map whose
   // out-of-range 8th column reads as zero (the stem: 7x7, stride 2).
-  A_WINDOW = 3
+  A_WINDOW = 3,
+  // The same with Cin = 4: a window is 8 pixels x 4 channels = 64 B, so a
+  // 64-wide K block holds two filter rows, each loaded by one im2col load into
+  // its own 8 KiB half of the A stage with the 64-byte swizzle (K-major,
+  // 64-byte rows). Half the bytes and half the K of the 8-channel form.
+  A_WINDOW4 = 4,
+  // Rectangular tiles: a tile is th x tw output pixels of one image, and the
+  // A tile of a K block is ONE tiled TMA box — {64 channels, tw, th} with
+  // traversal stride `stride` — instead of 128 pixel requests: the im2col
+  // request rate, not bytes, bounds the narrow-N layers (Cin % 64 == 0).
+  A_RECT = 5,
+  // The 4-channel window as rectangles: per filter row one box {8 stored
+  // pixels x 4 channels, tw windows, th rows} of the overlapping window view.
+  A_WINDOW4_RECT = 6,
+  // Stride 1 over a flat halo with resident weights: conv_halo_kernel.
+  A_HALO = 7
 };
+__host__ __device__ constexpr bool is_rect(int am) { return am == A_RECT || am == A_WINDOW4_RECT; }
 
 template <int BN, int AM>
 struct ConvCfg {
@@ -107,7 +132,8 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tiles_m = (int)((sh.mtot + 127) / 128), tiles_n = sh.cout / BN;
+  const int tiles_m = is_rect(AM) ? sh.n * sh.tiles_x * sh.tiles_y : (int)((sh.mtot + 127) / 128);
+  const int tiles_n = sh.cout / BN;
   const int64_t ntiles = (int64_t)tiles_m * tiles_n;
 
   if (threadIdx.x == 0) {
@@ -135,14 +161,23 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
+  // Tile t -> M tile and column offset, grouped 16 M tiles at a time. Flat
+  // tiles start at pixel m0 = mt * 128; rectangles at (img, oh0, ow0).
   auto coord = [&](int64_t t, int& m0, int& n0) {
     const int r = (int)t;
     const int group = r / (kConvGroupM * tiles_n);
     const int first_m = group * kConvGroupM;
     const int gsize = min(kConvGroupM, tiles_m - first_m);
     const int in_group = r % (kConvGroupM * tiles_n);
-    m0 = (first_m + in_group % gsize) * 128;
+    m0 = (first_m + in_group % gsize) * (is_rect(AM) ? 1 : 128);  // rect: the M tile's index
     n0 = (in_group / gsize) * BN;
+  };
+  auto rect_of = [&](int mt, int& img, int& oh0, int& ow0) {
+    const int per = sh.tiles_x * sh.tiles_y;
+    img = mt / per;
+    const int r = mt - img * per;
+    oh0 = (r / sh.tiles_x) * sh.th;
+    ow0 = (r - (r / sh.tiles_x) * sh.tiles_x) * sh.tw;
   };
 
   if (warp == 0) {
@@ -152,17 +187,24 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
       uint32_t ph = 0;
       const int cblocks = sh.cin / 64;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        int m0, n0;
+        int m0, n0, img, oh, ow;
         coord(t, m0, n0);
-        const int img = m0 / (sh.ho * sh.wo);
-        const int rem = m0 - img * sh.ho * sh.wo;
-        const int oh = rem / sh.wo, ow = rem - (rem / sh.wo) * sh.wo;
+        if (is_rect(AM)) {
+          rect_of(m0, img, oh, ow);
+        } else {
+          img = m0 / (sh.ho * sh.wo);
+          const int rem = m0 - img * sh.ho * sh.wo;
+          oh = rem / sh.wo;
+          ow = rem - (rem / sh.wo) * sh.wo;
+        }
         const int bw = ow * sh.stride - sh.pad + sh.wpad, bh = oh * sh.stride - sh.pad;
         int tap = 0, cb = 0;
         for (int kb = 0; kb < sh.kblocks; ++kb) {
           if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto w_done;
           const uint32_t fb = smem_u32(&full[s]);
-          mbar_expect_tx(fb, Cfg::kB + (AM == A_GATHER ? 0u : kConvA));
+          // rectangles land th*tw rows (the rest of the 128-row tile is unused)
+          const uint32_t a_bytes = AM == A_GATHER ? 0u : is_rect(AM) ? (uint32_t)(sh.th * sh.tw * 128) : kConvA;
+          mbar_expect_tx(fb, Cfg::kB + a_bytes);
           const uint32_t a_dst = smem_u32(ring + s * Cfg::kStage);
           const uint32_t b_dst = a_dst + kConvA;
           if (AM == A_IM2COL) {
@@ -175,6 +217,22 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
           } else if (AM == A_WINDOW) {
             // K block kb = filter row kb; the view's pixel index is the output column
             tma_load_im2col_4d(a_dst, &tmA, 0, ow, bh, img, 0, (uint16_t)kb, fb);
+          } else if (AM == A_WINDOW4) {
+            // K block kb = filter rows 2kb, 2kb+1; a row past the filter meets
+            // zero weight rows: load a real one
+            for (int half = 0; half < 2; ++half)
+              tma_load_im2col_4d(a_dst + half * 8192, &tmA, 0, ow, bh, img, 0, (uint16_t)min(2 * kb + half, sh.k - 1),
+                                 fb);
+          } else if (AM == A_RECT) {
+            const int r = tap / sh.k, c = tap - (tap / sh.k) * sh.k;
+            tma_load_4d(a_dst, &tmA, cb * 64, bw + c, bh + r, img, fb);
+            if (++cb == cblocks) {
+              cb = 0;
+              ++tap;
+            }
+          } else if (AM == A_WINDOW4_RECT) {
+            for (int half = 0; half < 2; ++half)
+              tma_load_4d(a_dst + half * 8192, &tmA, 0, ow, bh + min(2 * kb + half, sh.k - 1), img, fb);
           } else if (AM == A_IM2COL_CHUNK) {
             for (int j = 0; j < 8; ++j) {
               // taps past the filter multiply zero weight rows: load any real tap
@@ -187,6 +245,8 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
           for (int c = 0; c < BN / 64; ++c) {
             if (AM == A_WINDOW)  // {co, ci, filter column 0..7, filter row kb}
               tma_load_4d(b_dst + c * 8192, &tmW, n0 + c * 64, 0, 0, kb, fb);
+            else if (AM == A_WINDOW4 || AM == A_WINDOW4_RECT)  // {co, ci, column 0..7, rows 2kb, 2kb+1}
+              tma_load_4d(b_dst + c * 8192, &tmW, n0 + c * 64, 0, 0, 2 * kb, fb);
             else
               tma_load_3d(b_dst + c * 8192, &tmW, n0 + c * 64, kb * 64, 0, fb);
           }
@@ -204,6 +264,16 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
       int s = 0;
       uint32_t ph = 0;
       int i = 0;
+      // Descriptors of stage 0; a stage or K step moves only the start address
+      // field (address >> 4 in the low bits, which never carries: shared memory
+      // is below 256 KiB), so each MMA costs two adds. One thread issues every
+      // MMA: with N = 64 an MMA is 32 tensor cycles of work, and the issue loop
+      // must stay shorter than that.
+      const uint32_t ring0 = smem_u32(ring);
+      const uint64_t a0 = AM == A_IM2COL_CHUNK ? smem_desc_noswizzle(ring0, 2048, 128)
+                          : (AM == A_WINDOW4 || AM == A_WINDOW4_RECT) ? smem_desc(ring0, 16, 512, 4)
+                                                                       : smem_desc(ring0, 16, 1024);
+      const uint64_t b0 = smem_desc(ring0 + kConvA, 64 * 128, 1024);
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
         const int a = i & 1;
         if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) break;
@@ -216,13 +286,13 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(ring + s * Cfg::kStage);
-          const uint32_t b_addr = a_addr + kConvA;
+          const uint64_t so = (uint64_t)((s * Cfg::kStage) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = AM == A_IM2COL_CHUNK ? smem_desc_noswizzle(a_addr + kk * 4096, 2048, 128)
-                                                     : smem_desc(a_addr + kk * 32, 16, 1024);
-            tc_mma(d, ad, smem_desc(b_addr + kk * 2048, 64 * 128, 1024), Cfg::kIdesc, (kb | kk) != 0);
+            const uint32_t ao = AM == A_IM2COL_CHUNK                        ? kk * 256
+                                : (AM == A_WINDOW4 || AM == A_WINDOW4_RECT) ? (kk >> 1) * 512 + (kk & 1) * 2
+                                                                             : kk * 2;
+            tc_mma(d, a0 + so + ao, b0 + so + kk * 128, Cfg::kIdesc, (kb | kk) != 0);
           }
           tc_commit(smem_u32(&empty[s]));
           if (++s == kConvStages) {
@@ -244,14 +314,35 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
       tc_fence_after();
       int m0, n0;
       coord(t, m0, n0);
-      const int64_t m = (int64_t)m0 + q * 32 + lane;
+      int64_t m = (int64_t)m0 + q * 32 + lane;  // output pixel of this thread's row
+      bool mok;
+      int img = 0, y = 0, x = 0;
+      if (is_rect(AM)) {
+        int oh0, ow0;
+        rect_of(m0, img, oh0, ow0);
+        const int ml = q * 32 + lane;
+        y = oh0 + ml / sh.tw;
+        x = ow0 + ml - (ml / sh.tw) * sh.tw;
+        mok = ml < sh.th * sh.tw && y < sh.ho && x < sh.wo;
+      } else {
+        mok = m < sh.mtot;
+        if (sh.owp && mok) {
+          img = (int)(m / ((int64_t)sh.ho * sh.wo));
+          const int rem = (int)(m - (int64_t)img * sh.ho * sh.wo);
+          y = rem / sh.wo;
+          x = rem - y * sh.wo;
+        }
+      }
+      if (is_rect(AM) || sh.owp) m = ((int64_t)img * sh.ho + y) * sh.wso + sh.owp + x;  // stored output pixel
+      // the first and last pixel of an output row also zero the row's margins
+      const int margin = sh.owp && mok && (x == 0 || x == sh.wo - 1) ? (x == 0 ? -1 : 1) : 0;
       __nv_bfloat16* orow = out + m * sh.cout + n0;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
-        if (m < sh.mtot) {
+        if (mok) {
           uint32_t pk[16];
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
@@ -266,6 +357,11 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          for (int e = 1; margin && e <= sh.owp; ++e) {
+            uint4* z = reinterpret_cast<uint4*>(orow + (int64_t)margin * e * sh.cout + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) z[v] = make_uint4(0, 0, 0, 0);
+          }
         }
       }
       tc_fence_before();
@@ -342,6 +438,214 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols) : "memory");
 }
 
+// ── stride-1 convolution over a flat halo (A_HALO) ──
+// For stride 1 with the input stored with `pad` zero columns on each side,
+// output pixel (y, x) at stored position q = y*ws + x + pad reads, for filter
+// tap (r, c), the stored pixel q + (r - pad)*ws + (c - pad): every tap is the
+// same run of positions shifted by a constant. A tile is 128 consecutive
+// stored positions q0.. of one image (margin positions included, their
+// results discarded or written as zeros); per 64-channel block ONE tiled TMA
+// load brings the halo run q0 - pad*ws - pad .. q0 + 127 + pad*ws + pad
+// (rows above and below the image are out of range, so zero), and each tap's
+// A operand is that run shifted by r*ws + c rows: the shared-memory
+// descriptor's start moves by whole 128-byte rows. The 128-byte swizzle is a
+// function of the shared-memory address bits (chunk bits 4-6 XOR row bits
+// 7-9), for the TMA writes and the MMA reads alike, so a start that is not
+// 1024-byte aligned reads the rows the TMA wrote with base offset 0 (measured:
+// every tap exact with 0; with (start >> 7) & 7 all but the aligned tap wrong). The weights of this CTA's
+// BN-column block stay resident in shared memory for the whole kernel
+// (taps * Cin/64 K blocks of 64 x BN). Roles as in conv_bf16_kernel: warp 0
+// loads, warp 1 issues tcgen05.mma into two TMEM accumulators, warps 2-5 read
+// them back.
+template <int BN>
+struct HaloCfg {
+  static constexpr uint32_t kBBlock = 64 * BN * 2;  // one K block of weights
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false, true);
+};
+
+__host__ __device__ inline uint32_t halo_smem_bytes(const ConvShape& sh, uint32_t bblock) {
+  return 1024 + (uint32_t)sh.kblocks * bblock + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 256;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+                     __nv_bfloat16* __restrict__ out, const ConvShape sh, int relu) {
+  using Cfg = HaloCfg<BN>;
+  extern __shared__ unsigned char hsm_raw[];
+  unsigned char* bres =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(hsm_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* astage = bres + (size_t)sh.kblocks * Cfg::kBBlock;
+  const int S = sh.halo_stages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(astage + (size_t)S * sh.halo_stage_bytes);
+  uint64_t* full = bars;           // [S]
+  uint64_t* empty = bars + 4;      // [S], S <= 4
+  uint64_t* tfull = bars + 8;      // [2]
+  uint64_t* tempty = bars + 10;    // [2]
+  uint64_t* bfull = bars + 12;     // resident weights landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int cblocks = sh.cin / 64;
+  const int nb = blockIdx.x % sh.nblk, n0 = nb * BN;
+  const int64_t first = blockIdx.x / sh.nblk, step = gridDim.x / sh.nblk;
+  const int64_t mtiles = (int64_t)sh.n * sh.halo_tiles;
+  const int halo0 = sh.pad * sh.ws + sh.pad;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    mbar_init(smem_u32(bfull), 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(Cfg::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weights of column block nb, once
+      mbar_expect_tx(smem_u32(bfull), (uint32_t)sh.kblocks * Cfg::kBBlock);
+      for (int kb = 0; kb < sh.kblocks; ++kb)
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          tma_load_3d(smem_u32(bres + (size_t)kb * Cfg::kBBlock + c * 8192), &tmW, n0 + c * 64, kb * 64, 0,
+                      smem_u32(bfull));
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t t = first; t < mtiles; t += step) {
+        const int img = (int)(t / sh.halo_tiles);
+        const int q0 = (int)(t - (int64_t)img * sh.halo_tiles) * 128;
+        for (int cb = 0; cb < cblocks; ++cb) {
+          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto p_done;
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, (uint32_t)sh.halo_rows * 128);
+          tma_load_3d(smem_u32(astage + (size_t)s * sh.halo_stage_bytes), &tmA, cb * 64, q0 - halo0, img, fb);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    p_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts)) {
+      tc_fence_after();
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      // descriptors as offsets in 16-byte units from stage 0 / weight block 0
+      // (two adds per MMA; see conv_bf16_kernel)
+      const uint64_t adesc = smem_desc(smem_u32(astage), 16, 1024);
+      const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
+      const uint32_t bstep = (uint32_t)cblocks * (Cfg::kBBlock >> 4);  // next tap's weights
+      const uint32_t rowskip = (uint32_t)(sh.ws - sh.k) * 8;            // end of a filter row
+      for (int64_t t = first; t < mtiles; t += step, ++i) {
+        const int a = i & 1;
+        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(a * BN);
+        bool ok = true;
+        for (int cb = 0; cb < cblocks; ++cb) {
+          if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
+          uint32_t ao = 0;                                // tap (r, c): r*ws + c rows of 128 B
+          uint32_t bo = (uint32_t)cb * (Cfg::kBBlock >> 4);  // weights of (tap, cb)
+          uint32_t acc = cb != 0;
+          for (int r = 0; r < sh.k; ++r) {
+            for (int c = 0; c < sh.k; ++c) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) tc_mma(d, as + ao + kk * 2, bdesc + bo + kk * 128, Cfg::kIdesc, acc | kk);
+              acc = 1;
+              ao += 8;
+              bo += bstep;
+            }
+            ao += rowskip;
+          }
+          tc_commit(smem_u32(&empty[s]));
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&tfull[a]));
+      }
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;
+    int i = 0;
+    const int hws = sh.h * sh.ws;
+    for (int64_t t = first; t < mtiles; t += step, ++i) {
+      const int a = i & 1;
+      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) break;
+      tc_fence_after();
+      const int img = (int)(t / sh.halo_tiles);
+      const int pos = (int)(t - (int64_t)img * sh.halo_tiles) * 128 + q * 32 + lane;  // stored position
+      const int y = pos / sh.ws, xs = pos - (pos / sh.ws) * sh.ws;
+      const bool inner = xs >= sh.pad && xs < sh.pad + sh.w;
+      // with stored output margins every position of the image is written
+      // (zeros at the margins); without, only the output pixels
+      const bool store = pos < hws && (sh.owp ? true : inner);
+      const int64_t dpos = sh.owp ? (int64_t)img * hws + pos : ((int64_t)img * sh.h + y) * sh.w + xs - sh.pad;
+      __nv_bfloat16* orow = out + dpos * sh.cout + n0;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        if (store) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+            if (relu) {
+              x0 = fmaxf(x0, 0.f);
+              x1 = fmaxf(x1, 0.f);
+            }
+            if (!inner) x0 = x1 = 0.f;
+            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+            pk[v] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols) : "memory");
+}
+
 // ── NCHW -> NHWC, channels zero-padded to cpad, wpad zero columns each side ──
 __global__ void nchw_to_nhwc_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int c,
                                     int cpad, int h, int w, int wpad, int64_t n_stored) {
@@ -366,11 +670,14 @@ __global__ void nchw_to_nhwc_kernel(const __nv_bfloat16* __restrict__ in, __nv_b
   }
 }
 
-// Vector form for W a multiple of 8, C <= 8 and Cpad = 8: a thread converts 8
-// consecutive pixels of one row (one 16-byte load per channel plane, eight
-// 16-byte stores); thread group w/8 of each row writes the 2*wpad margin pixels.
-__global__ void nchw_to_nhwc8_vec_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int c,
-                                         int h, int w, int wpad, int64_t rows) {
+// Vector form for W a multiple of 8, C <= CP and CP = 4 or 8: a thread
+// converts 8 consecutive pixels of one row (one 16-byte load per channel
+// plane, one CP-channel store per pixel); thread group w/8 of each row writes
+// the 2*wpad margin pixels.
+template <int CP>
+__global__ void nchw_to_nhwc_vec_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int c,
+                                        int h, int w, int wpad, int64_t rows) {
+  using Px = typename std::conditional<CP == 8, uint4, uint2>::type;
   const int groups = w / 8 + 1;
   const int ws = w + 2 * wpad;
   const int64_t hw = (int64_t)h * w;
@@ -379,19 +686,21 @@ __global__ void nchw_to_nhwc8_vec_kernel(const __nv_bfloat16* __restrict__ in, _
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
     const int64_t row = t / groups;
     const int g = (int)(t - row * groups);
-    uint4* orow = reinterpret_cast<uint4*>(out + row * ws * 8);
+    Px* orow = reinterpret_cast<Px*>(out + row * ws * CP);
     if (g == w / 8) {
+      Px z;
+      memset(&z, 0, sizeof z);
       for (int x = 0; x < wpad; ++x) {
-        orow[x] = make_uint4(0, 0, 0, 0);
-        orow[wpad + w + x] = make_uint4(0, 0, 0, 0);
+        orow[x] = z;
+        orow[wpad + w + x] = z;
       }
       continue;
     }
     const int64_t img = row / h, y = row - img * h;
     const __nv_bfloat16* src = in + img * c * hw + y * w + g * 8;
-    __align__(16) __nv_bfloat16 plane[8][8];  // [channel][pixel]
+    __align__(16) __nv_bfloat16 plane[CP][8];  // [channel][pixel]
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < CP; ++k) {
       if (k < c)
         *reinterpret_cast<uint4*>(plane[k]) = __ldcs(reinterpret_cast<const uint4*>(src + k * hw));
       else
@@ -399,87 +708,157 @@ __global__ void nchw_to_nhwc8_vec_kernel(const __nv_bfloat16* __restrict__ in, _
     }
 #pragma unroll
     for (int px = 0; px < 8; ++px) {
-      __align__(16) __nv_bfloat16 v[8];
+      __align__(16) __nv_bfloat16 v[CP];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = plane[k][px];
-      orow[wpad + g * 8 + px] = *reinterpret_cast<const uint4*>(v);
+      for (int k = 0; k < CP; ++k) v[k] = plane[k][px];
+      orow[wpad + g * 8 + px] = *reinterpret_cast<const Px*>(v);
     }
   }
 }
 
 // ── global average pool + fully connected ──
-// Two kernels. gap_kernel: one thread per (image, channel pair), summing the
-// H×W pixels in order (fp32, 4-byte coalesced loads), means into scratch.
-// fc_kernel: logits = means · W with W stored [C][classes]; a CTA computes a
-// 32-image × 64-class tile, staging 32-channel slices of both operands in
-// shared memory, each thread 2 images × 4 classes, channels summed in order.
-__global__ void gap_kernel(const __nv_bfloat16* __restrict__ act, float* __restrict__ mean, int nimg, int hw,
-                           int c) {
-  const int pairs = c / 2;
-  const int64_t items = (int64_t)nimg * pairs;
-  const float inv = 1.f / (float)hw;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < items; t += stride) {
-    const int64_t img = t / pairs;
-    const int cp = (int)(t - img * pairs);
-    const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(act + img * hw * c) + cp;
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll 7
-    for (int p = 0; p < hw; ++p) {
-      const float2 v = __bfloat1622float2(a[(int64_t)p * pairs]);
-      s0 += v.x;
-      s1 += v.y;
+// Two kernels. gap_kernel: one CTA per image; its threads split the channels
+// into V-pair (4V-byte) units and the pixels into G interleaved groups, each
+// thread summing its unit over its pixels (fp32, loads independent of one
+// another), then the G partial sums per channel are added in group order into
+// the mean (scratch). fc_kernel: logits = means · W with W stored [C][classes]
+// (below).
+constexpr int kGapMaxGroups = 8;
+
+template <int V>
+__global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restrict__ act, float* __restrict__ mean,
+                                                  int hw, int c) {
+  extern __shared__ float part[];  // [G][c]
+  const int img = blockIdx.x;
+  const int units = c / (2 * V);
+  const int G = max(1, min(kGapMaxGroups, (int)blockDim.x / units));
+  const __nv_bfloat16* a = act + (int64_t)img * hw * c;
+  for (int idx = threadIdx.x; idx < G * units; idx += blockDim.x) {
+    const int g = idx / units, u = idx - (idx / units) * units;
+    float sum[2 * V];
+#pragma unroll
+    for (int e = 0; e < 2 * V; ++e) sum[e] = 0.f;
+    const __nv_bfloat16* src = a + u * 2 * V;
+#pragma unroll 4
+    for (int p = g; p < hw; p += G) {
+      if (V == 4) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)p * c));
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[e]));
+          sum[2 * e] += f.x;
+          sum[2 * e + 1] += f.y;
+        }
+      } else {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + (int64_t)p * c));
+        sum[0] += f.x;
+        sum[1] += f.y;
+      }
     }
-    reinterpret_cast<float2*>(mean + img * c)[cp] = make_float2(s0 * inv, s1 * inv);
+#pragma unroll
+    for (int e = 0; e < 2 * V; ++e) part[g * c + u * 2 * V + e] = sum[e];
+  }
+  __syncthreads();
+  const float inv = 1.f / (float)hw;
+  for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+    float t = 0.f;
+    for (int g = 0; g < G; ++g) t += part[g * c + ch];
+    mean[(int64_t)img * c + ch] = t * inv;
   }
 }
 
-constexpr int kFcTI = 32, kFcTJ = 64, kFcTK = 32;
+// fc_kernel: a cluster of kFcSplit CTAs computes one 32-image x 256-class tile
+// of logits, CTA z of the cluster summing channels [z*kc, (z+1)*kc) (kc = C/8
+// rounded up to 4). Each thread keeps 4 images x 8 classes in registers over
+// 64-channel slices staged in shared memory; the partial tiles then meet over
+// distributed shared memory, CTA z adding images [4z, 4z+4) of the tile from
+// all eight partials in rank order (so the result does not depend on timing).
+constexpr int kFcImg = 32, kFcCls = 256, kFcKc = 64, kFcSplit = 8;
+constexpr int kFcSmem = (kFcKc * kFcImg + kFcKc * kFcCls) * 4;  // 72 KiB; the partial tile reuses it
 
-__global__ void __launch_bounds__(256) fc_kernel(const float* __restrict__ mean, const float* __restrict__ w,
-                                                 float* __restrict__ logits, int nimg, int c, int classes) {
-  __shared__ float sm[kFcTK][kFcTI + 1];
-  __shared__ float sw[kFcTK][kFcTJ];
-  const int i0 = blockIdx.x * kFcTI, j0 = blockIdx.y * kFcTJ;
-  const int tj = threadIdx.x % 16, ti = threadIdx.x / 16;  // 16 x 16 threads: 4 classes x 2 images each
-  float acc[2][4] = {};
-  for (int k0 = 0; k0 < c; k0 += kFcTK) {
-    for (int e = threadIdx.x; e < kFcTI * kFcTK; e += 256) {
-      const int ii = e / kFcTK, kk = e % kFcTK;
-      sm[kk][ii] = (i0 + ii < nimg && k0 + kk < c) ? mean[(int64_t)(i0 + ii) * c + k0 + kk] : 0.f;
-    }
-    for (int e = threadIdx.x; e < kFcTK * kFcTJ; e += 256) {
-      const int kk = e / kFcTJ, jj = e % kFcTJ;
-      sw[kk][jj] = (k0 + kk < c && j0 + jj < classes) ? w[(int64_t)(k0 + kk) * classes + j0 + jj] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int kk = 0; kk < kFcTK; ++kk) {
-      const float a0 = sm[kk][2 * ti], a1 = sm[kk][2 * ti + 1];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float b = sw[kk][tj + 16 * q];
-        acc[0][q] = fmaf(a0, b, acc[0][q]);
-        acc[1][q] = fmaf(a1, b, acc[1][q]);
+__global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
+    fc_kernel(const float* __restrict__ mean, const float* __restrict__ w, float* __restrict__ logits, int nimg,
+              int c, int classes, int vec) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) float fsm[];
+  float* sm = fsm;                   // [k][image]
+  float* sw = fsm + kFcKc * kFcImg;  // [k][class]
+  const int i0 = blockIdx.x * kFcImg, j0 = blockIdx.y * kFcCls;
+  const int z = (int)cluster.block_rank();
+  const int ig = threadIdx.x / 32, jg = threadIdx.x % 32;  // images 4ig..4ig+3; classes 4jg.., 128+4jg..
+  const int kc = (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
+  const int kbeg = min(c, z * kc), kend = min(c, kbeg + kc);
+  float acc[4][8] = {};
+  for (int k0 = kbeg; k0 < kend; k0 += kFcKc) {
+    const int kn = min(kFcKc, kend - k0);
+    if (vec) {  // kn, C and classes multiples of 4: whole float4s are in or out of range
+      for (int e = threadIdx.x; e < kFcImg * kFcKc / 4; e += 256) {
+        const int ii = e / (kFcKc / 4), kk = 4 * (e % (kFcKc / 4));
+        const float4 v = i0 + ii < nimg && kk < kn ? *reinterpret_cast<const float4*>(mean + (int64_t)(i0 + ii) * c + k0 + kk)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        sm[(kk + 0) * kFcImg + ii] = v.x;
+        sm[(kk + 1) * kFcImg + ii] = v.y;
+        sm[(kk + 2) * kFcImg + ii] = v.z;
+        sm[(kk + 3) * kFcImg + ii] = v.w;
+      }
+      for (int e = threadIdx.x; e < kFcKc * kFcCls / 4; e += 256) {
+        const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
+        const float4 v = kk < kn && j0 + jj < classes
+                             ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
+      }
+    } else {
+      for (int e = threadIdx.x; e < kFcImg * kFcKc; e += 256) {
+        const int ii = e / kFcKc, kk = e % kFcKc;
+        sm[kk * kFcImg + ii] = i0 + ii < nimg && kk < kn ? mean[(int64_t)(i0 + ii) * c + k0 + kk] : 0.f;
+      }
+      for (int e = threadIdx.x; e < kFcKc * kFcCls; e += 256) {
+        const int kk = e / kFcCls, jj = e % kFcCls;
+        sw[kk * kFcCls + jj] = kk < kn && j0 + jj < classes ? w[(int64_t)(k0 + kk) * classes + j0 + jj] : 0.f;
       }
     }
     __syncthreads();
-  }
-  for (int r = 0; r < 2; ++r) {
-    const int i = i0 + 2 * ti + r;
-    if (i >= nimg) continue;
-    for (int q = 0; q < 4; ++q) {
-      const int j = j0 + tj + 16 * q;
-      if (j < classes) logits[(int64_t)i * classes + j] = acc[r][q];
+#pragma unroll 4
+    for (int kk = 0; kk < kFcKc; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(sm + kk * kFcImg + 4 * ig);
+      const float4 b0 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 4 * jg);
+      const float4 b1 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 128 + 4 * jg);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[r][q] = fmaf(av[r], bv[q], acc[r][q]);
     }
+    __syncthreads();
   }
+  // the partial tile [image][class] into this CTA's shared memory
+  float* part = fsm;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float* row = part + (4 * ig + r) * kFcCls;
+    *reinterpret_cast<float4*>(row + 4 * jg) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    *reinterpret_cast<float4*>(row + 128 + 4 * jg) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+  }
+  cluster.sync();
+  for (int e = threadIdx.x; e < 4 * kFcCls; e += 256) {
+    const int ii = 4 * z + e / kFcCls, jj = e % kFcCls;
+    float sum = 0.f;
+    for (int rk = 0; rk < kFcSplit; ++rk) sum += cluster.map_shared_rank(part, rk)[ii * kFcCls + jj];
+    if (i0 + ii < nimg && j0 + jj < classes) logits[(int64_t)(i0 + ii) * classes + j0 + jj] = sum;
+  }
+  cluster.sync();  // no CTA leaves while another still reads its partial tile
 }
 
 // ── host side ────────────────────────────────────────────────────────────────
 // conv2d_bf16 arguments: out (B), in (B), w (B), H, W, Cin, Cout, k, stride,
-// pad, relu, in_wpad (i); ndrange = number of images. in_wpad: zero columns
-// the input buffer stores on each side of every row (its rows are W + 2*in_wpad
-// pixels long); the convolution's own padding is still `pad`.
+// pad, relu, in_wpad, out_wpad (i); ndrange = number of images. in_wpad: zero
+// columns the input buffer stores on each side of every row (its rows are
+// W + 2*in_wpad pixels long); the convolution's own padding is still `pad`.
+// out_wpad: the same for the output rows, which the kernel writes as zeros.
 static ConvShape conv_shape(const LaunchArgs& la) {
   ConvShape sh{};
   sh.n = (int)la.nd[0];
@@ -490,12 +869,14 @@ static ConvShape conv_shape(const LaunchArgs& la) {
   sh.k = la.a[7].i32;
   sh.stride = la.a[8].i32;
   sh.pad = la.a[9].i32;
-  sh.wpad = la.a.size() > 11 ? la.a[11].i32 : 0;
+  sh.wpad = la.a[11].i32;
+  sh.owp = la.a[12].i32;
   sh.ws = sh.w + 2 * sh.wpad;
   if (sh.stride > 0) {
     sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
     sh.wo = (sh.w + 2 * sh.pad - sh.k) / sh.stride + 1;
   }
+  sh.wso = sh.wo + 2 * sh.owp;
   sh.taps = sh.k * sh.k;
   sh.cpt = sh.cin / 8;
   sh.kblocks = (sh.taps * sh.cin + 63) / 64;
@@ -503,16 +884,23 @@ static ConvShape conv_shape(const LaunchArgs& la) {
   return sh;
 }
 
+static int conv_amode(ConvShape& sh);
+
 mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes) {
   if (la.ndim != 1) return fail(MTL_ERR_ARGUMENT, "conv2d: ndrange must be one-dimensional (the image count)");
   ConvShape sh = conv_shape(la);
   if (sh.n < 0 || sh.h <= 0 || sh.w <= 0 || sh.k <= 0 || sh.stride <= 0 || sh.pad < 0 || sh.cin <= 0 || sh.cout <= 0 ||
-      sh.wpad < 0)
-    return fail(MTL_ERR_ARGUMENT, "conv2d: sizes must be positive (paddings non-negative)");
+      sh.wpad < 0 || sh.owp < 0 || sh.owp > 64)
+    return fail(MTL_ERR_ARGUMENT, "conv2d: sizes must be positive (paddings non-negative, out_wpad at most 64)");
   if (sh.ho <= 0 || sh.wo <= 0) return fail(MTL_ERR_ARGUMENT, "conv2d: the filter does not fit the padded input");
-  if (sh.cin % 8) return fail(MTL_ERR_UNSUPPORTED, "conv2d: Cin must be a multiple of 8 (pad the channels), got %d", sh.cin);
+  const int am = conv_amode(sh);
+  if (sh.cin % 8 && !(sh.cin == 4 && (am == A_WINDOW4 || am == A_WINDOW4_RECT)))
+    return fail(MTL_ERR_UNSUPPORTED,
+                "conv2d: Cin must be a multiple of 8 (pad the channels), or 4 for an input stored with its padding "
+                "columns (at least 128 KiB), got %d",
+                sh.cin);
   if (sh.cout % 64) return fail(MTL_ERR_UNSUPPORTED, "conv2d: Cout must be a multiple of 64, got %d", sh.cout);
-  const uint64_t need[3] = {(uint64_t)sh.mtot * sh.cout * 2, (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2,
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2,
                             (uint64_t)sh.taps * sh.cin * sh.cout * 2};
   const char* what[3] = {"the output", "the input", "the weights"};
   for (int i = 0; i < 3; ++i) {
@@ -559,32 +947,37 @@ static mtl_status make_im2col_map(CUtensorMap* map, const void* in, const ConvSh
   int upper[2] = {sh.pad - (sh.k - 1) - sh.wpad, sh.pad - (sh.k - 1)};
   cuuint32_t estr[4] = {1, (cuuint32_t)sh.stride, (cuuint32_t)sh.stride, 1};
   if (window) {
-    // "Pixels" of 8 stored pixels (128 B) starting every `stride` stored
-    // pixels: pixel u covers stored columns stride*u .. stride*u + 7, the
-    // widened filter row of output column u.
-    dims[0] = 64;
+    // "Pixels" of 8 stored pixels (8*Cin elements: 128 B at Cin = 8, 64 B at
+    // Cin = 4) starting every `stride` stored pixels: pixel u covers stored
+    // columns stride*u .. stride*u + 7, the widened filter row of output column u.
+    dims[0] = (cuuint64_t)8 * sh.cin;
     dims[1] = (cuuint64_t)sh.wo;
     strides[0] = (cuuint64_t)sh.stride * sh.cin * 2;
     lower[0] = 0;
     upper[0] = 0;
     estr[1] = 1;
   }
+  const CUtensorMapSwizzle sw = !swizzle ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                : cpp * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(in), dims, strides, lower, upper, cpp, 128,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MTL_ERR_ARGUMENT, "conv2d: im2col tensor map rejected (CUresult %d)", (int)r);
   return MTL_OK;
 }
 
-// Weights [k][k][8][cout] read as {cout, ci, filter column, filter row} with
-// box {64, 8, 8, 1}: one filter row widened to 8 columns, the 8th (past k)
-// out of range and so zero.
+// Weights [k][k][Cin][cout] read as {cout, ci, filter column, filter row} with
+// box {64, Cin, 8, 8/Cin}: 64 K rows = one (Cin = 8) or two (Cin = 4) filter
+// rows widened to 8 columns; the 8th column and rows past k are out of range
+// and so zero.
 static mtl_status make_window_weight_map(CUtensorMap* map, const void* w, const ConvShape& sh) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[4] = {(cuuint64_t)sh.cout, 8, (cuuint64_t)sh.k, (cuuint64_t)sh.k};
-  cuuint64_t strides[3] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.cout * 8 * 2, (cuuint64_t)sh.cout * 8 * sh.k * 2};
-  cuuint32_t box[4] = {64, 8, 8, 1};
+  const cuuint64_t ci = (cuuint64_t)sh.cin;
+  cuuint64_t dims[4] = {(cuuint64_t)sh.cout, ci, (cuuint64_t)sh.k, (cuuint64_t)sh.k};
+  cuuint64_t strides[3] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.cout * ci * 2, (cuuint64_t)sh.cout * ci * sh.k * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)ci, 8, (cuuint32_t)(8 / ci)};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(w), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -600,10 +993,25 @@ static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, con
   cudaError_t e =
       cudaFuncSetAttribute(conv_bf16_kernel<BN, AM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   if (e != cudaSuccess) return e;
-  const int64_t tiles = ((sh.mtot + 127) / 128) * (sh.cout / BN);
+  const int64_t mtiles = is_rect(AM) ? (int64_t)sh.n * sh.tiles_x * sh.tiles_y : (sh.mtot + 127) / 128;
+  const int64_t tiles = mtiles * (sh.cout / BN);
   const int grid = (int)std::min<int64_t>(tiles, (int64_t)sm_count * Cfg::kCtasPerSm);
   conv_bf16_kernel<BN, AM><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(
       tw, ta, reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t launch_halo(const CUtensorMap& tw, const CUtensorMap& ta, void* out, const ConvShape& sh, int relu,
+                               int sm_count, cudaStream_t s) {
+  const uint32_t smem = halo_smem_bytes(sh, HaloCfg<BN>::kBBlock);
+  cudaError_t e = cudaFuncSetAttribute(conv_halo_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = (int64_t)sh.n * sh.halo_tiles * sh.nblk;
+  // whole column-block groups: CTA b serves column block b % nblk
+  int grid = (int)std::min<int64_t>(tiles, sm_count);
+  grid = std::max(sh.nblk, grid - grid % sh.nblk);
+  conv_halo_kernel<BN><<<grid, 192, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
   return cudaGetLastError();
 }
 
@@ -615,18 +1023,130 @@ static cudaError_t launch_conv_bn(int bn, const CUtensorMap& tw, const CUtensorM
                      : launch_conv<64, AM>(tw, ta, in, out, sh, relu, sm_count, s);
 }
 
-// Which A path a convolution takes. The im2col paths need the im2col corners
-// to fit the 4-D encoding ([-128, 127]) and, as a precaution, an input of at
-// least 128 KiB (CUTLASS patches im2col descriptors of smaller tensors on
-// drivers up to 13.1; those small inputs take the gather path instead).
-static int conv_amode(const ConvShape& sh) {
+// The rectangle th x tw (th * tw <= 128 output pixels) that wastes the fewest
+// MMA rows over an ho x wo image, the wider one on ties, with the TMA box
+// limits tw * sx <= 256 and th * sy <= 256 (sx, sy: traversal strides).
+// Returns the fraction of the tiles' 128 rows that hold output pixels.
+static double pick_rect(ConvShape& sh, int sx, int sy) {
+  double best = 0.0;
+  for (int tw = std::min(sh.wo, 128); tw >= 1; --tw) {
+    const int th = std::min(128 / tw, sh.ho);
+    if (tw * sx > 256 || th * sy > 256) continue;
+    const int tx = (sh.wo + tw - 1) / tw, ty = (sh.ho + th - 1) / th;
+    const double use = (double)sh.ho * sh.wo / ((double)tx * ty * 128.0);
+    if (use > best + 1e-9) {
+      best = use;
+      sh.tw = tw;
+      sh.th = th;
+      sh.tiles_x = tx;
+      sh.tiles_y = ty;
+    }
+  }
+  return best;
+}
+
+// The flat-halo plan (A_HALO) for a stride-1 convolution whose input stores
+// its padding columns: the widest BN dividing Cout whose resident weights
+// leave room for at least two halo stages in the 227 KiB of shared memory,
+// where the halo fits one TMA box (at most 256 rows) and the tiles' margin
+// positions waste under 15 % of the MMA rows. Returns BN, or 0.
+static int halo_plan(ConvShape& sh) {
+  if (sh.stride != 1 || sh.cin % 64 || sh.k % 2 == 0 || 2 * sh.pad != sh.k - 1 || sh.wpad != sh.pad) return 0;
+  if (sh.owp != 0 && sh.owp != sh.pad) return 0;
+  const int rows = 128 + 2 * (sh.pad * sh.ws + sh.pad);
+  if (rows > 256) return 0;
+  const int tiles = (sh.h * sh.ws + 127) / 128;
+  if ((double)sh.h * sh.w < 0.85 * tiles * 128.0) return 0;
+  const int stage = (rows * 128 + 1023) & ~1023;
+  const int kblocks = sh.taps * sh.cin / 64;
+  for (int bn = 256; bn >= 64; bn /= 2) {
+    if (sh.cout % bn) continue;
+    const int64_t avail = 232448 - 1024 - 256 - (int64_t)kblocks * 64 * bn * 2;
+    const int stages = (int)std::min<int64_t>(4, avail / stage);
+    if (stages < 2) continue;
+    sh.kblocks = kblocks;
+    sh.halo_rows = rows;
+    sh.halo_tiles = tiles;
+    sh.halo_stages = stages;
+    sh.halo_stage_bytes = stage;
+    sh.nblk = sh.cout / bn;
+    return bn;
+  }
+  return 0;
+}
+
+// Which A path a convolution takes (and, for the rectangle paths, its tile
+// shape in sh). Rectangles where they keep at least 85 % of the MMA rows busy
+// (wide outputs); flat 128-pixel im2col runs otherwise. The im2col paths need
+// the im2col corners to fit the 4-D encoding ([-128, 127]) and, as a
+// precaution, an input of at least 128 KiB (CUTLASS patches im2col
+// descriptors of smaller tensors on drivers up to 13.1; those small inputs
+// take the gather path instead).
+static int conv_amode(ConvShape& sh) {
   const uint64_t in_bytes = (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2;
   const bool corners_ok = sh.pad + sh.wpad <= 127 && sh.pad - (sh.k - 1) - sh.wpad >= -128;
   if (!corners_ok || in_bytes < (128u << 10) || sh.stride > 8) return A_GATHER;
-  if (sh.cin % 64 == 0) return A_IM2COL;
-  if (sh.cin == 8 && sh.k <= 8 && sh.wpad == sh.pad && sh.stride * (sh.wo - 1) + 8 <= sh.ws) return A_WINDOW;
+  {
+    ConvShape t = sh;
+    if (halo_plan(t)) {
+      sh = t;
+      return A_HALO;
+    }
+  }
+  if (sh.cin % 64 == 0) {
+    ConvShape t = sh;
+    if (pick_rect(t, sh.stride, sh.stride) >= 0.85) {
+      sh = t;
+      return A_RECT;
+    }
+    return A_IM2COL;
+  }
+  // windows: 16-byte steps between windows and rows (TMA strides)
+  const bool window = sh.k <= 8 && sh.wpad == sh.pad && sh.stride * (sh.wo - 1) + 8 <= sh.ws &&
+                      (sh.stride * sh.cin * 2) % 16 == 0 && ((int64_t)sh.ws * sh.cin * 2) % 16 == 0;
+  if (sh.cin == 8 && window) return A_WINDOW;
+  if (sh.cin == 4 && window) {
+    ConvShape t = sh;
+    if (pick_rect(t, 1, sh.stride) >= 0.85) {
+      sh = t;
+      return A_WINDOW4_RECT;
+    }
+    return A_WINDOW4;
+  }
   if (sh.cin == 8) return A_IM2COL_CHUNK;
   return A_GATHER;
+}
+
+// Tiled map for the rectangle paths. A_RECT: the NHWC input {C, stored W, H,
+// N} with box {64, tw*s, th*s, 1} and traversal strides {1, s, s, 1}, so one
+// load brings th x tw pixels x 64 channels of one filter tap (128-byte rows,
+// 128-byte swizzle). A_WINDOW4_RECT: the window view {8 pixels x Cin, wo
+// windows, H, N} (windows `stride` pixels apart) with box {8*Cin, tw, th*s, 1},
+// traversal {1, 1, s, 1}: th x tw windows of one filter row (64-byte rows,
+// 64-byte swizzle).
+static mtl_status make_rect_map(CUtensorMap* map, const void* in, const ConvShape& sh, bool window) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t px = (cuuint64_t)sh.cin * 2;  // bytes per stored pixel
+  cuuint64_t dims[4] = {(cuuint64_t)sh.cin, (cuuint64_t)sh.ws, (cuuint64_t)sh.h, (cuuint64_t)sh.n};
+  cuuint64_t strides[3] = {px, (cuuint64_t)sh.ws * px, (cuuint64_t)sh.h * sh.ws * px};
+  cuuint32_t box[4] = {64, (cuuint32_t)(sh.tw * sh.stride), (cuuint32_t)(sh.th * sh.stride), 1};
+  cuuint32_t estr[4] = {1, (cuuint32_t)sh.stride, (cuuint32_t)sh.stride, 1};
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (window) {
+    dims[0] = (cuuint64_t)8 * sh.cin;
+    dims[1] = (cuuint64_t)sh.wo;
+    strides[0] = (cuuint64_t)sh.stride * px;
+    box[0] = (cuuint32_t)(8 * sh.cin);
+    box[1] = (cuuint32_t)sh.tw;
+    estr[1] = 1;
+    sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  }
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(in), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTL_ERR_ARGUMENT, "conv2d: tiled activation map rejected (CUresult %d)", (int)r);
+  return MTL_OK;
 }
 
 mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
@@ -649,15 +1169,35 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
     if (mtl_status st = make_im2col_map(&ta, in, sh, 64, true)) return st;
   if (am == A_IM2COL_CHUNK)
     if (mtl_status st = make_im2col_map(&ta, in, sh, 8, false)) return st;
-  if (am == A_WINDOW) {
-    if (mtl_status st = make_im2col_map(&ta, in, sh, 64, true, true)) return st;
+  if (am == A_RECT)
+    if (mtl_status st = make_rect_map(&ta, in, sh, false)) return st;
+  if (am == A_WINDOW4_RECT)
+    if (mtl_status st = make_rect_map(&ta, in, sh, true)) return st;
+  if (am == A_WINDOW || am == A_WINDOW4)
+    if (mtl_status st = make_im2col_map(&ta, in, sh, 8 * sh.cin, true, true)) return st;
+  if (am == A_WINDOW || am == A_WINDOW4 || am == A_WINDOW4_RECT) {
     if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
-    sh.kblocks = sh.k;  // one K block per filter row
+    sh.kblocks = am == A_WINDOW ? sh.k : (sh.k + 1) / 2;  // one or two filter rows per K block
   }
   cudaStream_t s = (cudaStream_t)stream;
+  if (am == A_HALO) {
+    ConvShape hs = sh;
+    const int bn = halo_plan(hs);
+    if (mtl_status st = make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
+                                      (uint32_t)hs.halo_rows))
+      return st;
+    cudaError_t e = bn == 256   ? launch_halo<256>(tw, ta, out, hs, relu, la.sm_count, s)
+                    : bn == 128 ? launch_halo<128>(tw, ta, out, hs, relu, la.sm_count, s)
+                                : launch_halo<64>(tw, ta, out, hs, relu, la.sm_count, s);
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
   cudaError_t e = am == A_IM2COL         ? launch_conv_bn<A_IM2COL>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
                   : am == A_IM2COL_CHUNK ? launch_conv_bn<A_IM2COL_CHUNK>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
                   : am == A_WINDOW       ? launch_conv_bn<A_WINDOW>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
+                  : am == A_WINDOW4      ? launch_conv_bn<A_WINDOW4>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
+                  : am == A_RECT         ? launch_conv_bn<A_RECT>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
+                  : am == A_WINDOW4_RECT ? launch_conv_bn<A_WINDOW4_RECT>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
                                          : launch_conv_bn<A_GATHER>(BN, tw, ta, in, out, sh, relu, la.sm_count, s);
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
   return MTL_OK;
@@ -680,13 +1220,16 @@ mtl_status nhwc_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   const int h = la.a[3].i32, w = la.a[4].i32, wp = la.a[6].i32;
   const int64_t stored = la.nd[0] * h * (int64_t)(w + 2 * wp);
   if (stored == 0) return MTL_OK;
-  const int c = la.a[2].i32;
-  if (w % 8 == 0 && c <= 8 && la.a[5].i32 == 8 && (la.a[1].ptr & 15) == 0) {
+  const int c = la.a[2].i32, cp = la.a[5].i32;
+  if (w % 8 == 0 && c <= cp && (cp == 8 || cp == 4) && (la.a[1].ptr & 15) == 0 && (la.a[0].ptr & 15) == 0) {
     const int64_t rows = la.nd[0] * h, work = rows * (w / 8 + 1);
     const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)la.sm_count * 16);
-    nchw_to_nhwc8_vec_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr), reinterpret_cast<__nv_bfloat16*>(la.a[0].ptr), c, h, w,
-        wp, rows);
+    auto* src = reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr);
+    auto* dst = reinterpret_cast<__nv_bfloat16*>(la.a[0].ptr);
+    if (cp == 8)
+      nchw_to_nhwc_vec_kernel<8><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(src, dst, c, h, w, wp, rows);
+    else
+      nchw_to_nhwc_vec_kernel<4><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(src, dst, c, h, w, wp, rows);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "nchw_to_nhwc: %s", cudaGetErrorString(e));
   }
@@ -722,12 +1265,22 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
   if (n > (int64_t)1 << 24) return fail(MTL_ERR_UNSUPPORTED, "gap_fc: too many images");
   float* mean = reinterpret_cast<float*>(ws);
   cudaStream_t s = (cudaStream_t)stream;
-  const int64_t items = n * (c / 2);
-  const int64_t blocks = std::min<int64_t>((items + 255) / 256, (int64_t)la.sm_count * 32);
-  gap_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr), mean, (int)n, hw, c);
-  dim3 grid((unsigned)((n + kFcTI - 1) / kFcTI), (unsigned)((classes + kFcTJ - 1) / kFcTJ));
-  fc_kernel<<<grid, 256, 0, s>>>(mean, reinterpret_cast<const float*>(la.a[2].ptr), reinterpret_cast<float*>(la.a[0].ptr),
-                                 (int)n, c, classes);
+  const auto* act = reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr);
+  const bool v4 = c % 8 == 0 && (la.a[1].ptr & 15) == 0;
+  const int units = v4 ? c / 8 : c / 2;
+  const int groups = std::max(1, std::min(kGapMaxGroups, 256 / units));
+  const size_t gsm = (size_t)groups * c * 4;  // at most 8 x 1536 floats = 48 KiB
+  if (v4)
+    gap_kernel<4><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
+  else
+    gap_kernel<1><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
+  cudaFuncSetAttribute(fc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
+  // float4 loads need C, classes and each CTA's channel range (a multiple of 4
+  // by construction) to keep rows 16-byte aligned
+  const int vec = c % 4 == 0 && classes % 4 == 0 && (la.a[2].ptr & 15) == 0;
+  dim3 grid((unsigned)((n + kFcImg - 1) / kFcImg), (unsigned)((classes + kFcCls - 1) / kFcCls), kFcSplit);
+  fc_kernel<<<grid, 256, kFcSmem, s>>>(mean, reinterpret_cast<const float*>(la.a[2].ptr),
+                                       reinterpret_cast<float*>(la.a[0].ptr), (int)n, c, classes, vec);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
 }

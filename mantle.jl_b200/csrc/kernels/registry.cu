@@ -163,8 +163,8 @@ static KernelDesc g_kernels[] = {
     // batched bf16 GEMM, fp32 accumulate and output: C, A, B, M, N, K; ndrange = batch
     {"gemm_bf16", "BBBiii", false, 0b110, 0b001, gemm_check, nullptr, gemm_run, nullptr},
     // NHWC bf16 convolution (implicit GEMM): out, in, w (HWIO), H, W, Cin, Cout,
-    // k, stride, pad, relu, in_wpad; ndrange = images
-    {"conv2d_bf16", "BBBiiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
+    // k, stride, pad, relu, in_wpad, out_wpad; ndrange = images
+    {"conv2d_bf16", "BBBiiiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
     // NCHW -> NHWC with zero-padded channels and Wpad zero columns each side:
     // out, in, C, H, W, Cpad, Wpad; ndrange = images
     {"nchw_to_nhwc_bf16", "BBiiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},

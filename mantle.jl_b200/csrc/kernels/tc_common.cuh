@@ -90,10 +90,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // Shared-memory matrix descriptor (tcgen05): start address, leading and stride
-// byte offsets (all >> 4), version 1 at bit 46, 128-byte swizzle (2) at bit 61.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// byte offsets (all >> 4), version 1 at bit 46, layout at bit 61 (2 = 128-byte
+// swizzle, 4 = 64-byte swizzle, 0 = none).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint64_t layout = 2) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (layout << 61);
 }
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,

@@ -252,7 +252,7 @@ CNN_LAYERS = [("stem", 7, 3, 64, 2),
               ("s3c1", 3, 128, 256, 2), ("s3c2", 3, 256, 256, 1),
               ("s4c1", 3, 256, 512, 2), ("s4c2", 3, 512, 512, 1)]
 CNN_CLASSES = 1000
-STEM_CPAD = 8  # input channels padded 3 -> 8 (16-byte pixels)
+STEM_CPAD = 4  # input channels padded 3 -> 4 (8-byte pixels)
 STEM_WPAD = 3  # zero columns stored each side of the stem's input rows (its padding)
 
 
@@ -320,9 +320,10 @@ def cnn_input(batch_total: int, seed: int = 3, device: str = "cuda"):
 
 
 def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 1, **plan_kw) -> CnnWorkload:
-    """The forward pass as one graph: NCHW->NHWC (channels padded to 8, the
+    """The forward pass as one graph: NCHW->NHWC (channels padded to 4, the
     stem's 3 padding columns stored as zeros), nine conv+ReLU passes over
-    transients (aliased by the placer), then GAP+FC into the logits. With
+    transients (aliased by the placer; the input of each stride-1 conv stored
+    with its padding columns), then GAP+FC into the logits. With
     world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
     import torch
     device = f"cuda:{dev.ordinal}"
@@ -341,15 +342,20 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
     compute(g, "to_nhwc", lambda p: dispatch(p, kernels.nchw_to_nhwc_bf16, (
         use(p, cur, write=True), use(p, x, read=True), 3, h, w, STEM_CPAD, STEM_WPAD), per))
     cin, wpad = STEM_CPAD, STEM_WPAD
-    for name, k, _, cout, s in CNN_LAYERS:
+    for i, (name, k, _, cout, s) in enumerate(CNN_LAYERS):
         pad = k // 2
         ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
-        nxt = Transient.Buffer(g, np.uint16, per * ho * wo * cout)
+        # ahead of a stride-1 conv, store its padding columns (zeros, written by
+        # this conv's epilogue), which lets that conv read every filter tap as
+        # one shifted run of stored pixels
+        nxt_layer = CNN_LAYERS[i + 1] if i + 1 < len(CNN_LAYERS) else None
+        owp = nxt_layer[1] // 2 if nxt_layer is not None and nxt_layer[4] == 1 else 0
+        nxt = Transient.Buffer(g, np.uint16, per * ho * (wo + 2 * owp) * cout)
         compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad,
-                wpad=wpad: dispatch(p, kernels.conv2d_bf16, (use(p, dst, write=True), use(p, src, read=True),
-                                                             use(p, wt, read=True), h, w, cin, cout, k, s, pad, 1, wpad),
-                                    per))
-        cur, h, w, cin, wpad = nxt, ho, wo, cout, 0
+                wpad=wpad, owp=owp: dispatch(p, kernels.conv2d_bf16, (
+                    use(p, dst, write=True), use(p, src, read=True), use(p, wt, read=True),
+                    h, w, cin, cout, k, s, pad, 1, wpad, owp), per))
+        cur, h, w, cin, wpad = nxt, ho, wo, cout, owp
     compute(g, "gap_fc", lambda p: dispatch(p, kernels.gap_fc, (
         use(p, logits, write=True), use(p, cur, read=True), use(p, fc, read=True), h * w, cin, CNN_CLASSES), per))
     plan = Plan(g, **plan_kw)

@@ -59,8 +59,10 @@ def _rand_bits(rng, shape, scale=1.0, nonneg=False):
     return O.bf16_bits(np.abs(x) if nonneg else x)
 
 
-# Inputs under 128 KiB take the cp.async gather path; larger ones with Cin a
-# multiple of 64 the TMA im2col path, and with Cin = 8 the 8-channel im2col path.
+# Inputs under 128 KiB take the cp.async gather path. Larger ones with Cin a
+# multiple of 64 take rectangular tiles (one tiled TMA box per filter tap) when
+# a rectangle keeps at least 85 % of the 128 MMA rows busy, flat im2col runs
+# otherwise; with Cin = 8 the 8-channel im2col path.
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,h,w,cin,cout,k,s,relu", [
     (2, 14, 14, 64, 64, 3, 1, 1),     # gather; BN = 64, stride 1
@@ -68,8 +70,11 @@ def _rand_bits(rng, shape, scale=1.0, nonneg=False):
     (2, 7, 7, 256, 512, 3, 1, 0),     # gather; BN = 256, two column tiles, no ReLU
     (2, 30, 22, 8, 64, 7, 2, 1),      # gather; 8 channels, 7x7, K not a multiple of 64
     (1, 9, 9, 128, 256, 3, 2, 1),     # gather; fewer pixels than one tile
-    (4, 28, 28, 64, 64, 3, 1, 1),     # im2col; BN = 64
-    (2, 56, 56, 64, 128, 3, 2, 1),    # im2col; stride 2, BN = 128
+    (4, 28, 28, 64, 64, 3, 1, 1),     # rectangles 4 x 28; BN = 64
+    (2, 56, 56, 64, 128, 3, 2, 1),    # rectangles 4 x 28; stride 2, BN = 128
+    (2, 56, 56, 64, 64, 3, 1, 1),     # rectangles 2 x 56, two CTAs per SM
+    (8, 13, 35, 64, 64, 3, 1, 1),     # rectangles 7 x 18, ragged in both directions
+    (4, 26, 104, 128, 256, 3, 2, 1),  # rectangles 7 x 18 of a 13 x 52 output, stride 2, BN = 256
     (5, 15, 17, 128, 256, 3, 1, 1),   # im2col; tiles span rows and images, ragged last tile
     (6, 14, 14, 256, 512, 3, 2, 1),   # im2col; 7x7 outputs, BN = 256
     (3, 7, 7, 512, 512, 3, 1, 0),     # im2col; 7x7 in and out, no ReLU
@@ -87,55 +92,97 @@ def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     wtt = torch.from_numpy(wt.view(np.int16)).cuda()
     out = torch.full((n, ho, wo, cout), -1, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, relu, 0), n, stream=st)
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, relu, 0, 0), n, stream=st)
     torch.cuda.synchronize()
     ref, _ = O.conv_bf16(x, wt, s, pad, relu=bool(relu))
     close_layer(out.cpu().numpy().view(np.uint16), ref)
 
 
-# An input stored with its padding columns: the 8-channel window path when the
-# stored margin equals the padding (and the input is at least 128 KiB), the
-# gather path otherwise.
+# An input stored with its padding columns: the window paths when the stored
+# margin equals the padding (and the input is at least 128 KiB) — 8 channels
+# (128-byte windows) or 4 (64-byte windows, two filter rows per K block) —
+# the im2col or gather paths otherwise.
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,h,w,cout,k,s,pad,wpad", [
-    (2, 112, 96, 64, 7, 2, 3, 3),     # window: the stem's geometry
-    (3, 57, 121, 128, 7, 2, 3, 3),    # window; odd sizes, BN = 128
-    (2, 40, 40, 64, 5, 1, 2, 2),      # im2col-chunk: the 8-wide window would leave the stored row
-    (1, 20, 18, 64, 7, 2, 3, 3),      # gather (small input) with a margin
-    (2, 112, 96, 64, 7, 2, 3, 4),     # im2col-chunk path: margin wider than the padding
+@pytest.mark.parametrize("cin,n,h,w,cout,k,s,pad,wpad", [
+    (8, 2, 112, 96, 64, 7, 2, 3, 3),     # window: the stem's geometry
+    (8, 3, 57, 122, 128, 7, 2, 3, 3),    # window; odd height, BN = 128
+    (8, 6, 40, 40, 64, 5, 1, 2, 2),      # im2col-chunk: the 8-wide window would leave the stored row
+    (8, 1, 20, 18, 64, 7, 2, 3, 3),      # gather (small input) with a margin
+    (8, 2, 112, 96, 64, 7, 2, 3, 4),     # im2col-chunk path: margin wider than the padding
+    (4, 3, 112, 96, 64, 7, 2, 3, 3),     # 4-channel window rectangles 8 x 16: the stem's geometry
+    (4, 6, 61, 46, 128, 7, 2, 3, 3),     # 4-channel window rectangles 16 x 8, ragged; BN = 128
+    (4, 12, 31, 40, 64, 7, 2, 3, 3),     # 4-channel window, flat runs that span images
 ])
-def test_conv_with_stored_margin(dev, n, h, w, cout, k, s, pad, wpad):
+def test_conv_with_stored_margin(dev, cin, n, h, w, cout, k, s, pad, wpad):
     import torch
     rng = np.random.default_rng(11)
-    x = _rand_bits(rng, (n, h, w, 8), nonneg=True)
+    x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
     x[..., 3:] = 0  # padded channels, as the network stores them
-    wt = _rand_bits(rng, (k, k, 8, cout), scale=float(np.sqrt(2.0 / (k * k * 3))))
-    stored = np.zeros((n, h, w + 2 * wpad, 8), np.uint16)
+    wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * 3))))
+    stored = np.zeros((n, h, w + 2 * wpad, cin), np.uint16)
     stored[:, :, wpad:wpad + w] = x
     ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
     xt = torch.from_numpy(stored.view(np.int16)).cuda()
     wtt = torch.from_numpy(wt.view(np.int16)).cuda()
     out = torch.full((n, ho, wo, cout), -1, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, 8, cout, k, s, pad, 1, wpad), n, stream=st)
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, 1, wpad, 0), n, stream=st)
     torch.cuda.synchronize()
     ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
     close_layer(out.cpu().numpy().view(np.uint16), ref)
 
 
+# Stored margins on both sides: the input rows carry `wpad` zero columns and the
+# output rows `owp`, which the kernel writes as zeros. Stride-1 layers whose
+# input margin equals the padding take the flat-halo path (one TMA load per
+# channel block, taps as shifted views, weights resident in shared memory)
+# when the halo fits one box and wastes under 15 % of the MMA rows.
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,h,w,cin,cout,k,s,pad,wpad,owp", [
+    (4, 56, 56, 64, 64, 3, 1, 1, 1, 1),     # halo, BN = 64: the first stage's second conv
+    (3, 56, 56, 64, 64, 3, 1, 1, 1, 0),     # halo, output without margins
+    (4, 28, 28, 128, 128, 3, 1, 1, 1, 1),   # halo, two 64-wide column blocks (weights 2 x 144 KiB)
+    (2, 40, 40, 64, 128, 3, 1, 1, 1, 1),    # halo, BN = 128, three stages
+    (3, 37, 45, 64, 64, 3, 1, 1, 1, 1),     # halo, odd sizes, tiles end past the image
+    (2, 30, 30, 64, 64, 5, 1, 2, 2, 2),     # 5x5: the halo exceeds one box -> rectangles, 2-pixel margins
+    (2, 112, 112, 64, 64, 3, 2, 1, 0, 1),   # rectangles writing margins (the first stage's stride-2 conv)
+    (4, 28, 28, 128, 256, 3, 2, 1, 1, 1),   # flat im2col runs, margins in and out
+    (1, 9, 9, 64, 64, 3, 1, 1, 0, 1),       # gather (small input) writing margins
+])
+def test_conv_margins_and_halo(dev, n, h, w, cin, cout, k, s, pad, wpad, owp):
+    import torch
+    rng = np.random.default_rng(17)
+    x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
+    wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
+    stored = np.zeros((n, h, w + 2 * wpad, cin), np.uint16)
+    stored[:, :, wpad:wpad + w] = x
+    ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+    xt = torch.from_numpy(stored.view(np.int16)).cuda()
+    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
+    out = torch.full((n, ho, wo + 2 * owp, cout), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, 1, wpad, owp), n, stream=st)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
+    close_layer(got[:, :, owp:owp + wo], ref)
+    assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("w", [23, 24])  # scalar path, vector path (W a multiple of 8)
-def test_nchw_to_nhwc_with_margin(dev, w):
+@pytest.mark.parametrize("cp", [4, 8])
+def test_nchw_to_nhwc_with_margin(dev, w, cp):
     import torch
     rng = np.random.default_rng(12)
     x = _rand_bits(rng, (3, 3, 17, w))
     xt = torch.from_numpy(x.view(np.int16)).cuda()
-    out = torch.full((3, 17, w + 6, 8), -1, dtype=torch.int16, device="cuda")
+    out = torch.full((3, 17, w + 6, cp), -1, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    M.launch(M.kernels.nchw_to_nhwc_bf16, (out, xt, 3, 17, w, 8, 3), 3, stream=st)
+    M.launch(M.kernels.nchw_to_nhwc_bf16, (out, xt, 3, 17, w, cp, 3), 3, stream=st)
     torch.cuda.synchronize()
-    want = np.zeros((3, 17, w + 6, 8), np.uint16)
-    want[:, :, 3:3 + w] = O.nchw_to_nhwc(x, 8)
+    want = np.zeros((3, 17, w + 6, cp), np.uint16)
+    want[:, :, 3:3 + w] = O.nchw_to_nhwc(x, cp)
     assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
 
 
@@ -145,11 +192,11 @@ def test_conv_refusals(dev):
     t = torch.zeros(1 << 20, dtype=torch.int16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     with pytest.raises(M.MantleError, match="Cin must be a multiple of 8"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 3, 64, 3, 1, 1, 1, 0), 1, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 3, 64, 3, 1, 1, 1, 0, 0), 1, stream=st)
     with pytest.raises(M.MantleError, match="Cout must be a multiple of 64"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 8, 32, 3, 1, 1, 1, 0), 1, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 8, 8, 8, 32, 3, 1, 1, 1, 0, 0), 1, stream=st)
     with pytest.raises(M.MantleError, match="bytes"):
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 64, 64, 64, 64, 3, 1, 1, 1, 0), 8, stream=st)
+        M.launch(M.kernels.conv2d_bf16, (t, t, t, 64, 64, 64, 64, 3, 1, 1, 1, 0, 0), 8, stream=st)
 
 
 @pytest.mark.gpu
@@ -178,7 +225,12 @@ def test_cnn_full_batch_sampled_images(dev):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,hw,c,classes", [(37, 49, 512, 1000), (3, 5, 64, 10)])
+@pytest.mark.parametrize("n,hw,c,classes", [
+    (37, 49, 512, 1000),  # 16-byte loads in both kernels, ragged image tile
+    (3, 5, 64, 10),       # fewer pixels than pixel groups; scalar FC loads
+    (2, 3, 6, 12),        # 4-byte GAP loads (C not a multiple of 8)
+    (4, 9, 1536, 8),      # the widest C: one pixel group, threads loop over the channel units
+])
 def test_gap_fc_matches_oracle(dev, n, hw, c, classes):
     import torch
     rng = np.random.default_rng(13)
