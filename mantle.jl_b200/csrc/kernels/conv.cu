@@ -93,7 +93,9 @@ enum AMode {
   // pixels x 4 channels, tw windows, th rows} of the overlapping window view.
   A_WINDOW4_RECT = 6,
   // Stride 1 over a flat halo with resident weights: conv_halo_kernel.
-  A_HALO = 7
+  A_HALO = 7,
+  // stride * Cin * 2 == 16 over raw input rows: conv_rows_kernel.
+  A_ROWS = 8
 };
 __host__ __device__ constexpr bool is_rect(int am) { return am == A_RECT || am == A_WINDOW4_RECT; }
 
@@ -292,7 +294,10 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
             const uint32_t ao = AM == A_IM2COL_CHUNK                        ? kk * 256
                                 : (AM == A_WINDOW4 || AM == A_WINDOW4_RECT) ? (kk >> 1) * 512 + (kk & 1) * 2
                                                                              : kk * 2;
-            tc_mma(d, a0 + so + ao, b0 + so + kk * 128, Cfg::kIdesc, (kb | kk) != 0);
+            if (kk == 0)
+              tc_mma(d, a0 + so + ao, b0 + so, Cfg::kIdesc, kb != 0);
+            else
+              tc_mma_acc(d, a0 + so + ao, b0 + so + kk * 128, Cfg::kIdesc);
           }
           tc_commit(smem_u32(&empty[s]));
           if (++s == kConvStages) {
@@ -557,7 +562,7 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t adesc = smem_desc(smem_u32(astage), 16, 1024);
       const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
       const uint32_t bstep = (uint32_t)cblocks * (Cfg::kBBlock >> 4);  // next tap's weights
-      const uint32_t rowskip = (uint32_t)(sh.ws - sh.k) * 8;            // end of a filter row
+      const uint32_t wsrow = (uint32_t)sh.ws * 8;                         // one stored row of 128 B rows
       for (int64_t t = first; t < mtiles; t += step, ++i) {
         const int a = i & 1;
         if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) break;
@@ -571,18 +576,19 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_fence_after();
           const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
-          uint32_t ao = 0;                                // tap (r, c): r*ws + c rows of 128 B
-          uint32_t bo = (uint32_t)cb * (Cfg::kBBlock >> 4);  // weights of (tap, cb)
-          uint32_t acc = cb != 0;
-          for (int r = 0; r < sh.k; ++r) {
-            for (int c = 0; c < sh.k; ++c) {
+          const uint64_t bc = bdesc + (uint64_t)((uint32_t)cb * (Cfg::kBBlock >> 4));  // weights of (tap 0, cb)
+          // 3x3: all 36 MMAs unrolled, tap (r, c) at r*ws + c rows of 128 B
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) tc_mma(d, as + ao + kk * 2, bdesc + bo + kk * 128, Cfg::kIdesc, acc | kk);
-              acc = 1;
-              ao += 8;
-              bo += bstep;
+          for (int tap = 0; tap < 9; ++tap) {
+            const uint64_t a = as + (uint64_t)((uint32_t)(tap / 3) * wsrow + (tap % 3) * 8);
+            const uint64_t b = bc + (uint64_t)((uint32_t)tap * bstep);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              if (tap == 0 && kk == 0)
+                tc_mma(d, a, b, Cfg::kIdesc, cb != 0);
+              else
+                tc_mma_acc(d, a + kk * 2, b + kk * 128, Cfg::kIdesc);
             }
-            ao += rowskip;
           }
           tc_commit(smem_u32(&empty[s]));
           if (++s == S) {
@@ -644,6 +650,260 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols) : "memory");
+}
+
+// ── epilogue through shared memory and TMA stores ──
+// One warp's 32 accumulator rows (TMEM lane quarter) x BN columns: ReLU,
+// bf16, written as BN/64 chunks of 32 rows x 128 bytes in the 128-byte-swizzled
+// layout (16-byte piece j of row i at position j ^ (i & 7): conflict-free
+// shared stores) into `stage` (1024-byte aligned, BN/64 x 4 KiB), then lane 0
+// stores each chunk with one TMA store of box {64, 32, 1} at (c0 + 64*chunk,
+// c1, c2); rows past the map's second extent are clipped by the TMA. The
+// caller alternates two staging buffers per warp and calls
+// epi_stage_acquire() before reusing one.
+__device__ __forceinline__ void epi_stage_acquire(int lane) {
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+}
+
+template <int BN>
+__device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned char* stage, const CUtensorMap* tmO,
+                                              int c0, int c1, int c2, int lane) {
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + c * 32, r);
+    uint32_t pk[16];
+#pragma unroll
+    for (int v = 0; v < 16; ++v) {
+      float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+      if (relu) {
+        x0 = fmaxf(x0, 0.f);
+        x1 = fmaxf(x1, 0.f);
+      }
+      __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+      pk[v] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    unsigned char* row = stage + (c / 2) * 4096 + lane * 128;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int piece = (c % 2) * 4 + v;
+      *reinterpret_cast<uint4*>(row + ((piece ^ (lane & 7)) << 4)) =
+          make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int c = 0; c < BN / 64; ++c) tma_store_3d(tmO, smem_u32(stage + c * 4096), c0 + c * 64, c1, c2);
+    bulk_commit();
+  }
+}
+
+// ── strided convolution over raw input rows (A_ROWS) ──
+// For stride * Cin * 2 == 16 bytes (the 4-channel stem at stride 2) with the
+// input stored with `pad` zero columns each side: output pixel x of output row
+// oh reads, for filter row r, the 8 stored pixels s*x .. s*x + 7 of input row
+// s*oh - pad + r, i.e. the bytes 16*x .. 16*x + 8*Cin*2 - 1 of that stored row.
+// As a K-major matrix without swizzle (core matrices of 8 rows x 16 bytes)
+// that is row stride 16 B, K-chunk stride (LBO) 16 B and 8-row-group stride
+// (SBO) 128 B: the overlapping windows are read straight from the raw row, no
+// window copy. A tile is one output row (M = 128 >= Wo; rows past Wo read into
+// the next stored row or the stage's slack and are discarded); a stage holds
+// the s*(G-1) + k input rows of G consecutive output rows, brought by ONE bulk
+// copy (rows outside the image are not copied; their filter rows are skipped).
+// The weights of the CTA's 64-column block stay resident (k filter rows of
+// 8*Cin K rows, the 8th column zero). The epilogue goes through shared memory
+// and TMA stores.
+constexpr int kRowsG = 8;  // output rows per stage
+
+__host__ __device__ inline uint32_t rows_smem_bytes(const ConvShape& sh) {
+  // 1 KiB alignment slack, resident weights, stages, staging (4 warps x 2 x 4 KiB), barriers
+  return 1024 + (uint32_t)sh.kblocks * 8192 + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 32768 + 256;
+}
+
+template <int CIN, int KT>  // KT: the filter size when known at compile time (its interior rows fully unrolled), else 0
+__global__ void __launch_bounds__(192, 1)
+    conv_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmO,
+                     const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, const ConvShape sh,
+                     int relu) {
+  constexpr int BN = 64;
+  constexpr int KQ = CIN / 2;  // K16 steps per filter row (8 pixels x CIN channels)
+  constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false, true);
+  extern __shared__ unsigned char rsm_raw[];
+  unsigned char* bres =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(rsm_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* astage = bres + (size_t)sh.kblocks * 8192;
+  const int S = sh.halo_stages;
+  unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [4 warps][2][4 KiB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 32768);
+  uint64_t* full = bars;         // [S]
+  uint64_t* empty = bars + 4;    // [S], S <= 4
+  uint64_t* tfull = bars + 8;    // [2]
+  uint64_t* tempty = bars + 10;  // [2]
+  uint64_t* bfull = bars + 12;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nb = blockIdx.x % sh.nblk, n0 = nb * BN;
+  const int64_t first = blockIdx.x / sh.nblk, step = gridDim.x / sh.nblk;
+  const int groups = (sh.ho + kRowsG - 1) / kRowsG;
+  const int64_t units = (int64_t)sh.n * groups;
+  const uint32_t rowbytes = (uint32_t)sh.ws * CIN * 2;
+  const int hrows = sh.stride * (kRowsG - 1) + sh.k;  // input rows of a stage
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    mbar_init(smem_u32(bfull), 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // resident weights: K blocks of 64 rows (8/CIN filter rows of 8*CIN)
+      mbar_expect_tx(smem_u32(bfull), (uint32_t)sh.kblocks * 8192);
+      for (int kb = 0; kb < sh.kblocks; ++kb)
+        tma_load_4d(smem_u32(bres + (size_t)kb * 8192), &tmW, n0, 0, 0, kb * (8 / CIN), smem_u32(bfull));
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t u = first; u < units; u += step) {
+        const int img = (int)(u / groups);
+        const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+        const int r0 = oh0 * sh.stride - sh.pad;  // input row of stage row 0
+        const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
+        if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+        const uint32_t fb = smem_u32(&full[s]);
+        const uint32_t bytes = (uint32_t)(hi - lo) * rowbytes;
+        mbar_expect_tx(fb, bytes);
+        bulk_load(smem_u32(astage + (size_t)s * sh.halo_stage_bytes + (size_t)(lo - r0) * rowbytes),
+                  in + ((int64_t)img * sh.h + lo) * sh.ws * CIN, bytes, fb);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts)) {
+      tc_fence_after();
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      const uint64_t adesc = smem_desc_noswizzle(smem_u32(astage), 16, 128);
+      const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
+      bool ok = true;
+      for (int64_t u = first; u < units && ok; u += step) {
+        const int img = (int)(u / groups);
+        const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+        if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) break;
+        tc_fence_after();
+        const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
+        for (int t = 0; t < kRowsG && oh0 + t < sh.ho; ++t, ++i) {
+          const int a = i & 1;
+          if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(a * BN);
+          const int ir0 = (oh0 + t) * sh.stride - sh.pad;  // input row of filter row 0
+          // filter rows inside the image (the padding rows contribute nothing)
+          const int rlo = max(0, -ir0), rhi = min(sh.k, sh.h - ir0);
+          const uint64_t at = as + (uint64_t)(((uint32_t)(sh.stride * t) * rowbytes) >> 4);
+          const uint32_t arow = rowbytes >> 4;
+          constexpr uint32_t brow = 8 * CIN * 8;  // 8*CIN K rows of 128 B per filter row
+          if (KT > 0 && rlo == 0 && rhi == KT) {
+#pragma unroll
+            for (int r = 0; r < KT; ++r)
+#pragma unroll
+              for (int q = 0; q < KQ; ++q) {
+                if (r == 0 && q == 0)
+                  tc_mma(d, at, bdesc, kIdesc, 0);
+                else
+                  tc_mma_acc(d, at + r * arow + q * 2, bdesc + r * brow + q * 128, kIdesc);
+              }
+          } else {
+            uint32_t acc = 0;
+            for (int r = rlo; r < rhi; ++r) {
+#pragma unroll
+              for (int q = 0; q < KQ; ++q) {
+                tc_mma(d, at + r * arow + q * 2, bdesc + r * brow + q * 128, kIdesc, acc);
+                acc = 1;
+              }
+            }
+          }
+          tc_commit(smem_u32(&tfull[a]));
+        }
+        tc_commit(smem_u32(&empty[s]));
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ── epilogue: one output row per tile, through shared memory and TMA stores ──
+    const int q = warp & 3;
+    unsigned char* my_stage = staging + (warp - 2) * 8192;
+    int i = 0;
+    bool ok = true;
+    for (int64_t u = first; u < units && ok; u += step) {
+      const int img = (int)(u / groups);
+      const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+      for (int t = 0; t < kRowsG && oh0 + t < sh.ho; ++t, ++i) {
+        const int a = i & 1;
+        if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        unsigned char* buf = my_stage + (i & 1) * 4096;
+        epi_stage_acquire(lane);
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+        const int orow = img * sh.ho + oh0 + t;
+        epi_tma_store<BN>(tbase, relu, buf, &tmO, n0, q * 32, orow, lane);
+        const int x = q * 32 + lane;
+        if (sh.owp && (x == 0 || x == sh.wo - 1)) {  // zero this output row's margin pixels
+          __nv_bfloat16* p = out + ((int64_t)orow * sh.wso + sh.owp + x) * sh.cout + n0;
+          for (int e = 1; e <= sh.owp; ++e) {
+            uint4* z = reinterpret_cast<uint4*>(p + (int64_t)(x == 0 ? -e : e) * sh.cout);
+#pragma unroll
+            for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
 }
 
 // ── NCHW -> NHWC, channels zero-padded to cpad, wpad zero columns each side ──
@@ -894,7 +1154,7 @@ mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes) {
     return fail(MTL_ERR_ARGUMENT, "conv2d: sizes must be positive (paddings non-negative, out_wpad at most 64)");
   if (sh.ho <= 0 || sh.wo <= 0) return fail(MTL_ERR_ARGUMENT, "conv2d: the filter does not fit the padded input");
   const int am = conv_amode(sh);
-  if (sh.cin % 8 && !(sh.cin == 4 && (am == A_WINDOW4 || am == A_WINDOW4_RECT)))
+  if (sh.cin % 8 && !(sh.cin == 4 && (am == A_WINDOW4 || am == A_WINDOW4_RECT || am == A_ROWS)))
     return fail(MTL_ERR_UNSUPPORTED,
                 "conv2d: Cin must be a multiple of 8 (pad the channels), or 4 for an input stored with its padding "
                 "columns (at least 128 KiB), got %d",
@@ -1001,6 +1261,37 @@ static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, con
   return cudaGetLastError();
 }
 
+// The output as {Cout, Wo, N*Ho} (pixel stride Cout, row stride (Wo + 2*owp)
+// * Cout, starting after the left margin) for TMA stores of {64, 32, 1}.
+static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)sh.cout, (cuuint64_t)sh.wo, (cuuint64_t)sh.n * sh.ho};
+  cuuint64_t strides[2] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.wso * sh.cout * 2};
+  cuuint32_t box[3] = {64, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  void* base = reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)sh.owp * sh.cout;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTL_ERR_ARGUMENT, "conv2d: output tensor map rejected (CUresult %d)", (int)r);
+  return MTL_OK;
+}
+
+template <int CIN, int KT>
+static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, const void* in, void* out,
+                               const ConvShape& sh, int relu, int sm_count, cudaStream_t s) {
+  const uint32_t smem = rows_smem_bytes(sh);
+  cudaError_t e =
+      cudaFuncSetAttribute(conv_rows_kernel<CIN, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t units = (int64_t)sh.n * ((sh.ho + kRowsG - 1) / kRowsG) * sh.nblk;
+  int grid = (int)std::min<int64_t>(units, sm_count);
+  grid = std::max(sh.nblk, grid - grid % sh.nblk);
+  conv_rows_kernel<CIN, KT><<<grid, 192, smem, s>>>(tw, to, reinterpret_cast<const __nv_bfloat16*>(in),
+                                                    reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  return cudaGetLastError();
+}
+
 template <int BN>
 static cudaError_t launch_halo(const CUtensorMap& tw, const CUtensorMap& ta, void* out, const ConvShape& sh, int relu,
                                int sm_count, cudaStream_t s) {
@@ -1045,13 +1336,13 @@ static double pick_rect(ConvShape& sh, int sx, int sy) {
   return best;
 }
 
-// The flat-halo plan (A_HALO) for a stride-1 convolution whose input stores
-// its padding columns: the widest BN dividing Cout whose resident weights
+// The flat-halo plan (A_HALO) for a stride-1 3x3 convolution whose input
+// stores its padding column on each side: the widest BN dividing Cout whose resident weights
 // leave room for at least two halo stages in the 227 KiB of shared memory,
 // where the halo fits one TMA box (at most 256 rows) and the tiles' margin
 // positions waste under 15 % of the MMA rows. Returns BN, or 0.
 static int halo_plan(ConvShape& sh) {
-  if (sh.stride != 1 || sh.cin % 64 || sh.k % 2 == 0 || 2 * sh.pad != sh.k - 1 || sh.wpad != sh.pad) return 0;
+  if (sh.stride != 1 || sh.cin % 64 || sh.k != 3 || sh.pad != 1 || sh.wpad != 1) return 0;
   if (sh.owp != 0 && sh.owp != sh.pad) return 0;
   const int rows = 128 + 2 * (sh.pad * sh.ws + sh.pad);
   if (rows > 256) return 0;
@@ -1075,6 +1366,29 @@ static int halo_plan(ConvShape& sh) {
   return 0;
 }
 
+// The raw-row plan (A_ROWS): 4 channels at stride 2 (16 bytes per output
+// step), a filter row that fits the 8-pixel window, stored padding columns, one output
+// row per 128-row tile, the windows of valid outputs inside the stored row,
+// and resident weights plus two or more stages in shared memory.
+static bool rows_plan(ConvShape& sh) {
+  if (sh.cin != 4 || sh.stride != 2) return false;  // the 4-channel stride-2 stem
+  if (sh.k > 8 || sh.wpad != sh.pad || sh.wo > 128 || sh.stride * (sh.wo - 1) + 8 > sh.ws) return false;
+  const int64_t rowbytes = (int64_t)sh.ws * sh.cin * 2;
+  if (rowbytes % 16 || sh.cout % 64) return false;
+  const int hrows = sh.stride * (kRowsG - 1) + sh.k;
+  // the last stage row's windows of the 128 tile rows: 127 * 16 + 16 * Cin bytes
+  const int64_t stage = (hrows * rowbytes + 127 * 16 + 16 * sh.cin + 1023) & ~int64_t(1023);
+  const int kblocks = (sh.k * 8 * sh.cin + 63) / 64;
+  const int64_t avail = 232448 - 1024 - (int64_t)kblocks * 8192 - 32768 - 256;
+  const int stages = (int)std::min<int64_t>(4, avail / stage);
+  if (stages < 2) return false;
+  sh.kblocks = kblocks;
+  sh.halo_stages = stages;
+  sh.halo_stage_bytes = (int)stage;
+  sh.nblk = sh.cout / 64;
+  return true;
+}
+
 // Which A path a convolution takes (and, for the rectangle paths, its tile
 // shape in sh). Rectangles where they keep at least 85 % of the MMA rows busy
 // (wide outputs); flat 128-pixel im2col runs otherwise. The im2col paths need
@@ -1091,6 +1405,11 @@ static int conv_amode(ConvShape& sh) {
     if (halo_plan(t)) {
       sh = t;
       return A_HALO;
+    }
+    t = sh;
+    if (rows_plan(t)) {
+      sh = t;
+      return A_ROWS;
     }
   }
   if (sh.cin % 64 == 0) {
@@ -1180,6 +1499,15 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
     sh.kblocks = am == A_WINDOW ? sh.k : (sh.k + 1) / 2;  // one or two filter rows per K block
   }
   cudaStream_t s = (cudaStream_t)stream;
+  if (am == A_ROWS) {
+    CUtensorMap to;
+    if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
+    if (mtl_status st = make_out_map(&to, out, sh)) return st;
+    cudaError_t e = sh.k == 7 ? launch_rows<4, 7>(tw, to, in, out, sh, relu, la.sm_count, s)
+                              : launch_rows<4, 0>(tw, to, in, out, sh, relu, la.sm_count, s);
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
   if (am == A_HALO) {
     ConvShape hs = sh;
     const int bn = halo_plan(hs);

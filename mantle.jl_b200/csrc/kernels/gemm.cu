@@ -174,7 +174,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = smem_desc(b_addr + kk * 2048, kBK * 128, 1024);
-            tc_mma(d, ad, bd, kIdesc, (kb | kk) != 0);
+            if (kk == 0)
+              tc_mma(d, ad, bd, kIdesc, kb != 0);
+            else
+              tc_mma_acc(d, ad, bd, kIdesc);
           }
           tc_commit(smem_u32(&empty[s]));
           if (++s == kStages) {

@@ -41,20 +41,34 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait with a suspend-time hint: the thread sleeps in the barrier until the
+// phase completes or the hint (ns) runs out, instead of re-polling shared
+// memory. Polling warps take shared-memory cycles from the tensor core's
+// operand reads (an M=128, N=64 MMA reads 6 KiB of operands in 48 cycles, the
+// whole shared-memory bandwidth).
+constexpr uint32_t kSuspendHintNs = 1000000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase of `bar` with the given parity. Returns false when
 // the CTA is aborting (this wait ran out, or another role's did).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort, int* timeouts) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        atomicAdd(timeouts, 1);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      atomicAdd(timeouts, 1);
+      return false;
     }
   }
 }
@@ -74,6 +88,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The same, always accumulating. With N = 64 an MMA takes about 48 cycles of
+// tensor work; the single issuing thread keeps up only when little else runs
+// between MMAs (measured: a runtime accumulate flag and loop control per MMA
+// cost 71 cycles per MMA, fully unrolled issue with this form 51).
+__device__ __forceinline__ void tc_mma_acc(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, 1, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d), "l"(a),
+      "l"(b), "r"(idesc)
       : "memory");
 }
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
@@ -104,6 +128,32 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
 }
+
+// Plain bulk copy global -> shared (both 16-byte aligned, size a multiple of
+// 16), completing on the mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// TMA store of a 3-D box from shared memory (bulk-group completion): the
+// caller fences the async proxy first and waits with bulk_wait_read before
+// overwriting the shared-memory source.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most N committed bulk groups may still be reading their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Every committed bulk group complete (writes visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Shared-memory matrix descriptor without swizzling (K-major): 8-row x 16-byte
 // core matrices, `lbo` bytes between the 16-byte K chunks, `sbo` bytes between

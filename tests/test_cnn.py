@@ -98,10 +98,12 @@ def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     close_layer(out.cpu().numpy().view(np.uint16), ref)
 
 
-# An input stored with its padding columns: the window paths when the stored
-# margin equals the padding (and the input is at least 128 KiB) — 8 channels
-# (128-byte windows) or 4 (64-byte windows, two filter rows per K block) —
-# the im2col or gather paths otherwise.
+# An input stored with its padding columns: with 4 channels at stride 2 and
+# output rows up to 128 pixels, the raw-row path (each stage one bulk copy of
+# input rows, the stride-2 windows read in place by the descriptor); otherwise
+# the window paths when the stored margin equals the padding (and the input is
+# at least 128 KiB) — 8 channels (128-byte windows) or 4 (64-byte windows, two
+# filter rows per K block) — the im2col or gather paths otherwise.
 @pytest.mark.gpu
 @pytest.mark.parametrize("cin,n,h,w,cout,k,s,pad,wpad", [
     (8, 2, 112, 96, 64, 7, 2, 3, 3),     # window: the stem's geometry
@@ -109,9 +111,11 @@ def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     (8, 6, 40, 40, 64, 5, 1, 2, 2),      # im2col-chunk: the 8-wide window would leave the stored row
     (8, 1, 20, 18, 64, 7, 2, 3, 3),      # gather (small input) with a margin
     (8, 2, 112, 96, 64, 7, 2, 3, 4),     # im2col-chunk path: margin wider than the padding
-    (4, 3, 112, 96, 64, 7, 2, 3, 3),     # 4-channel window rectangles 8 x 16: the stem's geometry
-    (4, 6, 61, 46, 128, 7, 2, 3, 3),     # 4-channel window rectangles 16 x 8, ragged; BN = 128
-    (4, 12, 31, 40, 64, 7, 2, 3, 3),     # 4-channel window, flat runs that span images
+    (4, 3, 112, 96, 64, 7, 2, 3, 3),     # 4 channels, raw input rows: the stem's geometry
+    (4, 6, 61, 46, 128, 7, 2, 3, 3),     # raw rows, odd height (last stage partial), two column blocks
+    (4, 12, 31, 40, 64, 7, 2, 3, 3),     # raw rows, one stage per image
+    (4, 2, 40, 300, 64, 7, 2, 3, 3),     # 4-channel window rectangles 4 x 30: output rows wider than 128
+    (4, 11, 6, 258, 64, 7, 2, 3, 3),     # 4-channel window, flat runs (3 x 129 outputs: no rectangle fills 85 %)
 ])
 def test_conv_with_stored_margin(dev, cin, n, h, w, cout, k, s, pad, wpad):
     import torch
