@@ -723,8 +723,19 @@ __host__ __device__ inline uint32_t rows_smem_bytes(const ConvShape& sh) {
   return 1024 + (uint32_t)sh.kblocks * 8192 + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 32768 + 256;
 }
 
-template <int CIN, int KT>  // KT: the filter size when known at compile time (its interior rows fully unrolled), else 0
-__global__ void __launch_bounds__(192, 1)
+// With SRC_C > 0 the input is the network's NCHW tensor with SRC_C <= CIN
+// channels instead: the producer bulk-copies the stage's rows of each channel
+// plane into a raw buffer (two, alternating), and a converter warp writes the
+// stage's padded NHWC rows from them (margins and the padding channels zero),
+// fences the async proxy and signals the stage full: the NCHW -> NHWC pass
+// never touches HBM.
+__host__ __device__ inline uint32_t rows_raw_bytes(const ConvShape& sh, int src_c) {
+  const int hrows = sh.stride * (kRowsG - 1) + sh.k;
+  return ((uint32_t)hrows * sh.w * 2 * src_c + 1023) & ~1023u;
+}
+
+template <int CIN, int KT, int SRC_C>  // KT: the filter size when known at compile time (its interior rows fully unrolled), else 0
+__global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
     conv_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmO,
                      const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, const ConvShape sh,
                      int relu) {
@@ -737,13 +748,17 @@ __global__ void __launch_bounds__(192, 1)
   unsigned char* astage = bres + (size_t)sh.kblocks * 8192;
   const int S = sh.halo_stages;
   unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [4 warps][2][4 KiB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 32768);
+  unsigned char* raw = staging + 32768;                                 // SRC_C: [2][raw bytes]
+  const uint32_t raw_bytes = SRC_C ? rows_raw_bytes(sh, SRC_C) : 0;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + 2 * raw_bytes);
   uint64_t* full = bars;         // [S]
   uint64_t* empty = bars + 4;    // [S], S <= 4
   uint64_t* tfull = bars + 8;    // [2]
   uint64_t* tempty = bars + 10;  // [2]
   uint64_t* bfull = bars + 12;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* raw_full = bars + 13;   // [2]
+  uint64_t* raw_empty = bars + 15;  // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -764,6 +779,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(smem_u32(&tempty[a]), 4);
     }
     mbar_init(smem_u32(bfull), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&raw_full[b]), 1);
+      mbar_init(smem_u32(&raw_empty[b]), 1);
+    }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -792,6 +811,21 @@ __global__ void __launch_bounds__(192, 1)
         const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
         const int r0 = oh0 * sh.stride - sh.pad;  // input row of stage row 0
         const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
+        if (SRC_C) {
+          // the stage's rows of each channel plane into raw buffer s % 2 (s counts units here)
+          if (!wait_phase(smem_u32(&raw_empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+          const uint32_t fb = smem_u32(&raw_full[s]);
+          const uint32_t plane = (uint32_t)(hi - lo) * sh.w * 2;
+          mbar_expect_tx(fb, plane * SRC_C);
+          for (int c = 0; c < SRC_C; ++c)
+            bulk_load(smem_u32(raw + (size_t)s * raw_bytes + (size_t)c * hrows * sh.w * 2),
+                      in + (((int64_t)img * SRC_C + c) * sh.h + lo) * sh.w, plane, fb);
+          if (++s == 2) {
+            s = 0;
+            ph ^= 1;
+          }
+          continue;
+        }
         if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
         const uint32_t fb = smem_u32(&full[s]);
         const uint32_t bytes = (uint32_t)(hi - lo) * rowbytes;
@@ -862,7 +896,63 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (SRC_C && warp == 6) {
+    // ── converter: raw channel-plane rows -> the stage's padded NHWC rows ──
+    int s = 0, rb = 0;
+    uint32_t ph = 0, rph = 0;
+    for (int64_t u = first; u < units; u += step) {
+      const int img = (int)(u / groups);
+      const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+      const int r0 = oh0 * sh.stride - sh.pad;
+      const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
+      (void)img;
+      if (!wait_phase(smem_u32(&raw_full[rb]), rph, abort, &g_conv_timeouts)) break;
+      if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+      // lane m of a row converts image pixels 4m..4m+3: one 8-byte load per
+      // channel plane, four 8-byte pixel stores; lanes past the row zero the
+      // margin pixels
+      const unsigned char* src = raw + (size_t)rb * raw_bytes;
+      unsigned char* dst = astage + (size_t)s * sh.halo_stage_bytes + (size_t)(lo - r0) * rowbytes;
+      const int quads = sh.w / 4;
+      const size_t plane = (size_t)hrows * sh.w * 2;
+      for (int j = 0; j < hi - lo; ++j) {
+        const unsigned char* srow = src + (size_t)j * sh.w * 2;
+        unsigned char* drow = dst + (size_t)j * rowbytes;
+        for (int m = lane; m < quads; m += 32) {
+          uint2 pl[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            pl[c] = c < SRC_C ? *reinterpret_cast<const uint2*>(srow + c * plane + (size_t)m * 8) : make_uint2(0, 0);
+          // pixel i of the quad: channel c is the i-th bf16 of plane c's load
+          uint2 px[4];
+          px[0] = make_uint2(__byte_perm(pl[0].x, pl[1].x, 0x5410), __byte_perm(pl[2].x, pl[3].x, 0x5410));
+          px[1] = make_uint2(__byte_perm(pl[0].x, pl[1].x, 0x7632), __byte_perm(pl[2].x, pl[3].x, 0x7632));
+          px[2] = make_uint2(__byte_perm(pl[0].y, pl[1].y, 0x5410), __byte_perm(pl[2].y, pl[3].y, 0x5410));
+          px[3] = make_uint2(__byte_perm(pl[0].y, pl[1].y, 0x7632), __byte_perm(pl[2].y, pl[3].y, 0x7632));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint2*>(drow + (size_t)(sh.wpad + 4 * m + i) * 8) = px[i];
+        }
+        if (lane < 2 * sh.wpad) {  // margins: stored pixels 0..wpad-1 and wpad+w..ws-1
+          const int x = lane < sh.wpad ? lane : sh.w + lane;
+          *reinterpret_cast<uint2*>(drow + (size_t)x * 8) = make_uint2(0, 0);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&full[s]));
+        mbar_arrive(smem_u32(&raw_empty[rb]));
+      }
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+      if (++rb == 2) {
+        rb = 0;
+        rph ^= 1;
+      }
+    }
+  } else if (warp >= 2 && warp < 6) {
     // ── epilogue: one output row per tile, through shared memory and TMA stores ──
     const int q = warp & 3;
     unsigned char* my_stage = staging + (warp - 2) * 8192;
@@ -1277,18 +1367,18 @@ static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh)
   return MTL_OK;
 }
 
-template <int CIN, int KT>
+template <int CIN, int KT, int SRC_C>
 static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, const void* in, void* out,
                                const ConvShape& sh, int relu, int sm_count, cudaStream_t s) {
-  const uint32_t smem = rows_smem_bytes(sh);
+  const uint32_t smem = rows_smem_bytes(sh) + 2 * rows_raw_bytes(sh, SRC_C);
   cudaError_t e =
-      cudaFuncSetAttribute(conv_rows_kernel<CIN, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(conv_rows_kernel<CIN, KT, SRC_C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int64_t units = (int64_t)sh.n * ((sh.ho + kRowsG - 1) / kRowsG) * sh.nblk;
   int grid = (int)std::min<int64_t>(units, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_rows_kernel<CIN, KT><<<grid, 192, smem, s>>>(tw, to, reinterpret_cast<const __nv_bfloat16*>(in),
-                                                    reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  conv_rows_kernel<CIN, KT, SRC_C><<<grid, SRC_C ? 224 : 192, smem, s>>>(
+      tw, to, reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
   return cudaGetLastError();
 }
 
@@ -1370,7 +1460,7 @@ static int halo_plan(ConvShape& sh) {
 // step), a filter row that fits the 8-pixel window, stored padding columns, one output
 // row per 128-row tile, the windows of valid outputs inside the stored row,
 // and resident weights plus two or more stages in shared memory.
-static bool rows_plan(ConvShape& sh) {
+static bool rows_plan(ConvShape& sh, int src_c = 0) {
   if (sh.cin != 4 || sh.stride != 2) return false;  // the 4-channel stride-2 stem
   if (sh.k > 8 || sh.wpad != sh.pad || sh.wo > 128 || sh.stride * (sh.wo - 1) + 8 > sh.ws) return false;
   const int64_t rowbytes = (int64_t)sh.ws * sh.cin * 2;
@@ -1379,7 +1469,7 @@ static bool rows_plan(ConvShape& sh) {
   // the last stage row's windows of the 128 tile rows: 127 * 16 + 16 * Cin bytes
   const int64_t stage = (hrows * rowbytes + 127 * 16 + 16 * sh.cin + 1023) & ~int64_t(1023);
   const int kblocks = (sh.k * 8 * sh.cin + 63) / 64;
-  const int64_t avail = 232448 - 1024 - (int64_t)kblocks * 8192 - 32768 - 256;
+  const int64_t avail = 232448 - 1024 - (int64_t)kblocks * 8192 - 32768 - 256 - 2 * (int64_t)rows_raw_bytes(sh, src_c);
   const int stages = (int)std::min<int64_t>(4, avail / stage);
   if (stages < 2) return false;
   sh.kblocks = kblocks;
@@ -1503,8 +1593,8 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
     CUtensorMap to;
     if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
     if (mtl_status st = make_out_map(&to, out, sh)) return st;
-    cudaError_t e = sh.k == 7 ? launch_rows<4, 7>(tw, to, in, out, sh, relu, la.sm_count, s)
-                              : launch_rows<4, 0>(tw, to, in, out, sh, relu, la.sm_count, s);
+    cudaError_t e = sh.k == 7 ? launch_rows<4, 7, 0>(tw, to, in, out, sh, relu, la.sm_count, s)
+                              : launch_rows<4, 0, 0>(tw, to, in, out, sh, relu, la.sm_count, s);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }
@@ -1528,6 +1618,85 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
                   : am == A_WINDOW4_RECT ? launch_conv_bn<A_WINDOW4_RECT>(BN, tw, ta, in, out, sh, relu, la.sm_count, s)
                                          : launch_conv_bn<A_GATHER>(BN, tw, ta, in, out, sh, relu, la.sm_count, s);
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+  return MTL_OK;
+}
+
+// conv2d_nchw_bf16 arguments: out (B), in (B, NCHW bf16), w (B, HWIO with 4
+// input channels, those past C zero), H, W, C, Cout, k, stride, pad, relu,
+// out_wpad (i); ndrange = images. The first convolution of a network straight
+// from its NCHW input: the raw-row kernel with the NCHW -> NHWC conversion in
+// shared memory (C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of
+// at most 128 pixels, Cout a multiple of 64).
+static ConvShape nchw_conv_shape(const LaunchArgs& la) {
+  ConvShape sh{};
+  sh.n = (int)la.nd[0];
+  sh.h = la.a[3].i32;
+  sh.w = la.a[4].i32;
+  sh.cin = 4;
+  sh.cout = la.a[6].i32;
+  sh.k = la.a[7].i32;
+  sh.stride = la.a[8].i32;
+  sh.pad = la.a[9].i32;
+  sh.wpad = sh.pad;
+  sh.owp = la.a[11].i32;
+  sh.ws = sh.w + 2 * sh.wpad;
+  if (sh.stride > 0) {
+    sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
+    sh.wo = (sh.w + 2 * sh.pad - sh.k) / sh.stride + 1;
+  }
+  sh.wso = sh.wo + 2 * sh.owp;
+  sh.taps = sh.k * sh.k;
+  sh.cpt = 1;
+  sh.mtot = (int64_t)sh.n * sh.ho * sh.wo;
+  return sh;
+}
+
+mtl_status nchwconv_check(const LaunchArgs& la, const uint64_t* bytes) {
+  if (la.ndim != 1) return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: ndrange must be one-dimensional (the image count)");
+  ConvShape sh = nchw_conv_shape(la);
+  const int c = la.a[5].i32;
+  if (sh.n < 0 || sh.h <= 0 || sh.w <= 0 || sh.k <= 0 || sh.stride <= 0 || sh.pad < 0 || c <= 0 || sh.cout <= 0 ||
+      sh.owp < 0 || sh.owp > 64 || sh.ho <= 0 || sh.wo <= 0)
+    return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: bad sizes");
+  if (c > 4 || sh.stride != 2 || sh.w % 8 || sh.ws % 2 || sh.cout % 64 || !rows_plan(sh, c))
+    return fail(MTL_ERR_UNSUPPORTED,
+                "conv2d_nchw: needs C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of at most 128 pixels "
+                "and Cout a multiple of 64");
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * c * sh.h * sh.w * 2,
+                            (uint64_t)sh.taps * 4 * sh.cout * 2};
+  const char* what[3] = {"the output", "the input", "the weights"};
+  for (int i = 0; i < 3; ++i) {
+    if (bytes[i] && bytes[i] < need[i])
+      return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: %s has %llu bytes, the launch touches %llu", what[i],
+                  (unsigned long long)bytes[i], (unsigned long long)need[i]);
+    if (la.a[i].ptr & 15) return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: %s must be 16-byte aligned", what[i]);
+  }
+  return MTL_OK;
+}
+
+mtl_status nchwconv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  ConvShape sh = nchw_conv_shape(la);
+  if (sh.mtot == 0) return MTL_OK;
+  const int c = la.a[5].i32;
+  if (!rows_plan(sh, c)) return fail(MTL_ERR_UNSUPPORTED, "conv2d_nchw: shape not supported");
+  const int relu = la.a[10].i32 != 0;
+  void* out = reinterpret_cast<void*>(la.a[0].ptr);
+  const void* in = reinterpret_cast<const void*>(la.a[1].ptr);
+  CUtensorMap tw, to;
+  if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
+  if (mtl_status st = make_out_map(&to, out, sh)) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e;
+  if (c == 3)
+    e = sh.k == 7 ? launch_rows<4, 7, 3>(tw, to, in, out, sh, relu, la.sm_count, s)
+                  : launch_rows<4, 0, 3>(tw, to, in, out, sh, relu, la.sm_count, s);
+  else if (c == 4)
+    e = launch_rows<4, 0, 4>(tw, to, in, out, sh, relu, la.sm_count, s);
+  else if (c == 2)
+    e = launch_rows<4, 0, 2>(tw, to, in, out, sh, relu, la.sm_count, s);
+  else
+    e = launch_rows<4, 0, 1>(tw, to, in, out, sh, relu, la.sm_count, s);
+  if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d_nchw: %s", cudaGetErrorString(e));
   return MTL_OK;
 }
 

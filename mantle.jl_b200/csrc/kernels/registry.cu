@@ -20,6 +20,8 @@ mtl_status gemm_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gemm_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status conv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status nchwconv_check(const LaunchArgs& la, const uint64_t* bytes);
+mtl_status nchwconv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status nhwc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
@@ -165,6 +167,10 @@ static KernelDesc g_kernels[] = {
     // NHWC bf16 convolution (implicit GEMM): out, in, w (HWIO), H, W, Cin, Cout,
     // k, stride, pad, relu, in_wpad, out_wpad; ndrange = images
     {"conv2d_bf16", "BBBiiiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
+    // the first convolution straight from an NCHW input (C <= 4, stride 2):
+    // out, in, w (HWIO, 4 input channels), H, W, C, Cout, k, stride, pad,
+    // relu, out_wpad; ndrange = images
+    {"conv2d_nchw_bf16", "BBBiiiiiiiii", false, 0b110, 0b001, nchwconv_check, nullptr, nchwconv_run, nullptr},
     // NCHW -> NHWC with zero-padded channels and Wpad zero columns each side:
     // out, in, C, H, W, Cpad, Wpad; ndrange = images
     {"nchw_to_nhwc_bf16", "BBiiiii", false, 0b10, 0b01, nhwc_check, nullptr, nhwc_run, nullptr},

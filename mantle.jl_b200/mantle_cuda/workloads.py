@@ -252,8 +252,7 @@ CNN_LAYERS = [("stem", 7, 3, 64, 2),
               ("s3c1", 3, 128, 256, 2), ("s3c2", 3, 256, 256, 1),
               ("s4c1", 3, 256, 512, 2), ("s4c2", 3, 512, 512, 1)]
 CNN_CLASSES = 1000
-STEM_CPAD = 4  # input channels padded 3 -> 4 (8-byte pixels)
-STEM_WPAD = 3  # zero columns stored each side of the stem's input rows (its padding)
+STEM_CPAD = 4  # the stem's weights cover 4 input channels (the 4th zero): 8-byte pixels
 
 
 def cnn_macs_per_image(h: int = 224, w: int = 224) -> int:
@@ -320,10 +319,10 @@ def cnn_input(batch_total: int, seed: int = 3, device: str = "cuda"):
 
 
 def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 1, **plan_kw) -> CnnWorkload:
-    """The forward pass as one graph: NCHW->NHWC (channels padded to 4, the
-    stem's 3 padding columns stored as zeros), nine conv+ReLU passes over
-    transients (aliased by the placer; the input of each stride-1 conv stored
-    with its padding columns), then GAP+FC into the logits. With
+    """The forward pass as one graph: nine conv+ReLU passes over transients
+    (aliased by the placer; the stem reads the NCHW input and converts it to
+    padded NHWC rows in shared memory; the input of each stride-1 conv is
+    stored with its padding columns), then GAP+FC into the logits. With
     world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
     import torch
     device = f"cuda:{dev.ordinal}"
@@ -338,10 +337,7 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
     logits = Buffer(dev, np.float32, per * CNN_CLASSES)
     g = Graph(dev)
     h = w = 224
-    cur = Transient.Buffer(g, np.uint16, per * h * (w + 2 * STEM_WPAD) * STEM_CPAD)
-    compute(g, "to_nhwc", lambda p: dispatch(p, kernels.nchw_to_nhwc_bf16, (
-        use(p, cur, write=True), use(p, x, read=True), 3, h, w, STEM_CPAD, STEM_WPAD), per))
-    cin, wpad = STEM_CPAD, STEM_WPAD
+    cur, cin, wpad = x, 3, 0
     for i, (name, k, _, cout, s) in enumerate(CNN_LAYERS):
         pad = k // 2
         ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
@@ -351,10 +347,16 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
         nxt_layer = CNN_LAYERS[i + 1] if i + 1 < len(CNN_LAYERS) else None
         owp = nxt_layer[1] // 2 if nxt_layer is not None and nxt_layer[4] == 1 else 0
         nxt = Transient.Buffer(g, np.uint16, per * ho * (wo + 2 * owp) * cout)
-        compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad,
-                wpad=wpad, owp=owp: dispatch(p, kernels.conv2d_bf16, (
-                    use(p, dst, write=True), use(p, src, read=True), use(p, wt, read=True),
-                    h, w, cin, cout, k, s, pad, 1, wpad, owp), per))
+        if i == 0:  # the stem reads the NCHW input itself (converted in shared memory)
+            compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cout=cout, k=k, s=s, pad=pad,
+                    owp=owp: dispatch(p, kernels.conv2d_nchw_bf16, (
+                        use(p, dst, write=True), use(p, src, read=True), use(p, wt, read=True),
+                        h, w, 3, cout, k, s, pad, 1, owp), per))
+        else:
+            compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cin=cin, cout=cout, k=k, s=s, pad=pad,
+                    wpad=wpad, owp=owp: dispatch(p, kernels.conv2d_bf16, (
+                        use(p, dst, write=True), use(p, src, read=True), use(p, wt, read=True),
+                        h, w, cin, cout, k, s, pad, 1, wpad, owp), per))
         cur, h, w, cin, wpad = nxt, ho, wo, cout, owp
     compute(g, "gap_fc", lambda p: dispatch(p, kernels.gap_fc, (
         use(p, logits, write=True), use(p, cur, read=True), use(p, fc, read=True), h * w, cin, CNN_CLASSES), per))

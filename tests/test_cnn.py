@@ -173,6 +173,46 @@ def test_conv_margins_and_halo(dev, n, h, w, cin, cout, k, s, pad, wpad, owp):
     assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
 
 
+# The stem straight from an NCHW input: each stage's channel-plane rows are
+# bulk-copied to shared memory and converted there to padded NHWC rows.
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,c,h,w,cout,owp", [
+    (2, 3, 224, 224, 64, 0),   # the network's stem
+    (3, 3, 61, 96, 128, 1),    # odd height (a partial last stage), two column blocks, output margins
+    (5, 1, 40, 48, 64, 0),     # one channel
+    (4, 4, 33, 64, 64, 0),     # four channels (no padding channel)
+])
+def test_conv_nchw_matches_oracle(dev, n, c, h, w, cout, owp):
+    import torch
+    rng = np.random.default_rng(19)
+    k, s, pad = 7, 2, 3
+    x = _rand_bits(rng, (n, c, h, w), nonneg=True)
+    wt = _rand_bits(rng, (k, k, 4, cout), scale=float(np.sqrt(2.0 / (k * k * c))))
+    wt[:, :, c:] = 0
+    ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
+    out = torch.full((n, ho, wo + 2 * owp, cout), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.conv2d_nchw_bf16, (out, xt, wtt, h, w, c, cout, k, s, pad, 1, owp), n, stream=st)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    ref, _ = O.conv_bf16(O.nchw_to_nhwc(x, 4), wt, s, pad, relu=True)
+    close_layer(got[:, :, owp:owp + wo], ref)
+    assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
+
+
+@pytest.mark.gpu
+def test_conv_nchw_refusals(dev):
+    import torch
+    t = torch.zeros(1 << 20, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    with pytest.raises(M.MantleError, match="W a multiple of 8"):
+        M.launch(M.kernels.conv2d_nchw_bf16, (t, t, t, 16, 20, 3, 64, 7, 2, 3, 1, 0), 1, stream=st)
+    with pytest.raises(M.MantleError, match="C <= 4"):
+        M.launch(M.kernels.conv2d_nchw_bf16, (t, t, t, 16, 16, 5, 64, 7, 2, 3, 1, 0), 1, stream=st)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("w", [23, 24])  # scalar path, vector path (W a multiple of 8)
 @pytest.mark.parametrize("cp", [4, 8])
