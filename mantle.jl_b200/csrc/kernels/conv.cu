@@ -1144,7 +1144,10 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
   for (int k0 = kbeg; k0 < kend; k0 += kFcKc) {
     const int kn = min(kFcKc, kend - k0);
     if (vec) {  // kn, C and classes multiples of 4: whole float4s are in or out of range
-      for (int e = threadIdx.x; e < kFcImg * kFcKc / 4; e += 256) {
+      // fixed trip counts, fully unrolled: every load of the slice is in flight at once
+#pragma unroll
+      for (int it = 0; it < kFcImg * kFcKc / 4 / 256; ++it) {
+        const int e = threadIdx.x + it * 256;
         const int ii = e / (kFcKc / 4), kk = 4 * (e % (kFcKc / 4));
         const float4 v = i0 + ii < nimg && kk < kn ? *reinterpret_cast<const float4*>(mean + (int64_t)(i0 + ii) * c + k0 + kk)
                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1153,7 +1156,9 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
         sm[(kk + 2) * kFcImg + ii] = v.z;
         sm[(kk + 3) * kFcImg + ii] = v.w;
       }
-      for (int e = threadIdx.x; e < kFcKc * kFcCls / 4; e += 256) {
+#pragma unroll
+      for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
+        const int e = threadIdx.x + it * 256;
         const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
         const float4 v = kk < kn && j0 + jj < classes
                              ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
@@ -1194,10 +1199,22 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
     *reinterpret_cast<float4*>(row + 128 + 4 * jg) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
   }
   cluster.sync();
-  for (int e = threadIdx.x; e < 4 * kFcCls; e += 256) {
+  // all 32 remote loads of a thread in flight before the in-order sums
+  float pv[4][kFcSplit];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * 256;
+    const int ii = 4 * z + e / kFcCls, jj = e % kFcCls;
+#pragma unroll
+    for (int rk = 0; rk < kFcSplit; ++rk) pv[it][rk] = cluster.map_shared_rank(part, rk)[ii * kFcCls + jj];
+  }
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * 256;
     const int ii = 4 * z + e / kFcCls, jj = e % kFcCls;
     float sum = 0.f;
-    for (int rk = 0; rk < kFcSplit; ++rk) sum += cluster.map_shared_rank(part, rk)[ii * kFcCls + jj];
+#pragma unroll
+    for (int rk = 0; rk < kFcSplit; ++rk) sum += pv[it][rk];
     if (i0 + ii < nimg && j0 + jj < classes) logits[(int64_t)(i0 + ii) * classes + j0 + jj] = sum;
   }
   cluster.sync();  // no CTA leaves while another still reads its partial tile
