@@ -187,6 +187,33 @@ def pinned_like(a: np.ndarray) -> np.ndarray:
     return out
 
 
+def e2e_time(dev, ws, steps: int, uploads, run, downloads) -> dict:
+    """End-to-end seconds per step through the public API: every step uploads
+    `uploads` ((Buffer, pinned host array) pairs) from host memory, calls
+    `run()`, and downloads `downloads` ((Buffer, host array) pairs); wall
+    clock over the steps (max over ranks), after two untimed steps."""
+    import mantle_cuda as M
+
+    def one():
+        for buf, host in uploads:
+            M.check(M.lib().mtl_buffer_upload(buf.handle, host.ctypes.data, 0, host.nbytes))
+        run()
+        for buf, host in downloads:
+            M.check(M.lib().mtl_buffer_download(buf.handle, host.ctypes.data, 0, host.nbytes))
+
+    for _ in range(2):
+        one()
+    dev.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dev.synchronize()
+    sec = max_over_ranks(ws, (time.perf_counter() - t0) / steps)
+    return {"seconds": sec, "h2d_bytes_per_step": int(sum(h.nbytes for _, h in uploads)),
+            "d2h_bytes_per_step": int(sum(h.nbytes for _, h in downloads))}
+
+
 # ── CPU baseline (oracle) ───────────────────────────────────────────────────
 def cpu_scatter_step(inp: dict, nbins: int, threads: int, frac: float = 1.0):
     """One step of the workload on the CPU: two scatters + histogram + three
@@ -352,6 +379,13 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
     nbytes = w.bytes_unfused if args.unfused else w.bytes_compulsory
     value = ws * nbytes / (ms_step * 1e-3) / 1e9
     nk = w.plan.nkernels()
+    # end to end: x, y, z from pinned host memory, one replay, out back to the host
+    ups = [(getattr(w, k), pinned_like(w.inputs[k])) for k in ("x", "y", "z")]
+    out_host = np.empty(w.n, np.float32)
+    t = e2e_time(dev, ws, max(3, min(args.steps, 20)), ups, lambda: M.run(w.plan), [(w.out, out_host)])
+    e2e = {"value": round(ws * w.bytes_compulsory / t["seconds"] / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": t["h2d_bytes_per_step"], "d2h_bytes_per_step": t["d2h_bytes_per_step"],
+           "ms_per_step": round(t["seconds"] * 1e3, 3)}
     line = {
         "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
@@ -364,7 +398,7 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
         "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None},
-        "gpu_launches": nk * args.steps, "clocks": clk.summary(),
+        "e2e": e2e, "gpu_launches": nk * args.steps, "clocks": clk.summary(),
     }
     return line
 
@@ -401,6 +435,13 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
     tp = ROOT / "profiles" / "fft_traffic.json"
     if tp.exists():
         traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    # end to end: the input from pinned host memory, forward + inverse, the
+    # round trip back to the host
+    back_host = np.empty(w.inputs["x"].shape, w.inputs["x"].dtype)
+    t = e2e_time(dev, ws, 3, [(w.x, pinned_like(w.inputs["x"]))], lambda: M.run(w.plan), [(w.back, back_host)])
+    e2e = {"value": round(ws * w.bytes_step / t["seconds"] / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": t["h2d_bytes_per_step"], "d2h_bytes_per_step": t["d2h_bytes_per_step"],
+           "ms_per_step": round(t["seconds"] * 1e3, 3)}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -428,7 +469,7 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "algorithmic_bytes": algo, "peak_kind": f"{peak_kind} (burst copy)", "kernel_ms": round(k_ms, 4)},
-        "cpu_baseline": cpu, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
     }
 
 
@@ -461,6 +502,15 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
     tp = ROOT / "profiles" / "gemm_traffic.json"
     if tp.exists():
         roofline["traffic"] = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    # end to end: A and B (bf16 bits) from pinned host memory, the batch of
+    # GEMMs, C back to the host
+    A_host, B_host = w.host_operands()
+    C_host = np.empty(w.batch * w.M * w.N, np.float32)
+    t = e2e_time(dev, ws, 3, [(w.A, pinned_like(A_host.view(np.int16))), (w.B, pinned_like(B_host.view(np.int16)))],
+                 lambda: M.run(w.plan), [(w.C, C_host)])
+    e2e = {"value": round(ws * w.flops_step / t["seconds"] / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": t["h2d_bytes_per_step"], "d2h_bytes_per_step": t["d2h_bytes_per_step"],
+           "ms_per_step": round(t["seconds"] * 1e3, 3)}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         A, B = w.host_operands()
@@ -481,7 +531,7 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
         "config": {"workload": "dense GEMM C = A.B, bf16 in, fp32 accumulate and out", "M": w.M, "N": w.N, "K": w.K,
                    "batch": w.batch, "parallelism": f"{ws} independent batches",
                    "l2": "A and B 1 GiB each per step, above the 126 MB L2; no flush"},
-        "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": w.plan.nkernels() * args.steps,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps,
         "clocks": clk.summary(),
     }
 
@@ -521,6 +571,32 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     ms_step = max_over_ranks(ws, ms / args.steps)
     images_s = total / (ms_step * 1e-3)
     flops = 2 * total * (w.flops_step // (2 * w.batch))
+
+    # End to end through the public API: each step this rank's images (NCHW
+    # bf16) go from pinned host memory into the input buffer, the graph
+    # replays (and the logits are all-gathered when N > 1), and this rank's
+    # logits come back to the host.
+    x_bits, _, _ = w.host_params()
+    x_host = pinned_like(x_bits.view(np.int16))
+    logits_host = np.empty(w.batch * CNN_CLASSES, np.float32)
+
+    def e2e_step():
+        M.check(M.lib().mtl_buffer_upload(w.x.handle, x_host.ctypes.data, 0, x_host.nbytes))
+        step()
+        M.check(M.lib().mtl_buffer_download(w.logits.handle, logits_host.ctypes.data, 0, logits_host.nbytes))
+
+    for _ in range(2):
+        e2e_step()
+    dev.synchronize()
+    barrier(ws)
+    e2e_steps = max(3, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    dev.synchronize()
+    e2e_s = max_over_ranks(ws, (time.perf_counter() - t0) / e2e_steps)
+    e2e = {"value": round(total / e2e_s, 1), "unit": "images/s", "h2d_bytes_per_step": int(x_host.nbytes),
+           "d2h_bytes_per_step": int(logits_host.nbytes), "ms_per_step": round(e2e_s * 1e3, 3)}
     tflops = flops / (ms_step * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     per_gpu = tflops / ws
@@ -546,11 +622,12 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
                    "global_batch": total, "image": [3, 224, 224], "parallelism": f"batch split over {ws} GPUs"
                    + (", NCCL all-gather of the logits every step" if ws > 1 else ""),
                    "tflops": round(tflops, 1)},
-        "roofline": {"bound": "tensor", "kernel": "the whole forward graph (9 conv2d_bf16 + 2 small kernels)",
+        "roofline": {"bound": "tensor", "kernel": "the whole forward graph (conv2d_nchw_bf16 + 8 conv2d_bf16 + "
+                                                  "gap + fc)",
                      "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(per_gpu / peak, 4),
                      "traffic": None, "algorithmic_flops": flops // ws,
                      "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)"},
-        "cpu_baseline": cpu, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
     }
 
 
