@@ -43,12 +43,17 @@ def headers() -> list[Path]:
     return sorted(list(CSRC.rglob("*.hpp")) + list(CSRC.rglob("*.cuh")) + [ROOT / "include" / "mantle_cuda.h"])
 
 
+# Flags for single translation units. showcase.cu: no FMA contraction, so its
+# float arithmetic is the sequence of IEEE operations the C oracle performs.
+PER_FILE = {"showcase.cu": ["-fmad=false"]}
+
+
 def compile_one(src: Path, force: bool) -> Path:
     obj = OBJ / (src.relative_to(CSRC).as_posix().replace("/", "__") + ".o")
     newest_dep = max([src.stat().st_mtime] + [h.stat().st_mtime for h in headers()])
     if not force and obj.exists() and obj.stat().st_mtime >= newest_dep:
         return obj
-    cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH, *COMMON, *PER_FILE.get(src.name, []), "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
         cmd = [nvcc(), *COMMON, "-x", "c++", "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)

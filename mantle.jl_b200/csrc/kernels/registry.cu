@@ -21,6 +21,21 @@ mtl_status gemm_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* str
 mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status conv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status nchwconv_check(const LaunchArgs& la, const uint64_t* bytes);
+#define SC_DECL(k)                                               \
+  mtl_status k##_check(const LaunchArgs& la, const uint64_t* bytes); \
+  mtl_status k##_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+SC_DECL(sc_move_lights)
+SC_DECL(sc_cull)
+SC_DECL(sc_write_draw)
+SC_DECL(sc_tile_lights)
+SC_DECL(sc_ssao)
+SC_DECL(sc_ao_blur)
+SC_DECL(sc_shade)
+SC_DECL(sc_bright)
+SC_DECL(sc_blur)
+SC_DECL(sc_composite)
+#undef SC_DECL
+
 mtl_status nchwconv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status nhwc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
@@ -183,6 +198,21 @@ static KernelDesc g_kernels[] = {
     {"pack_bgra8", "BB", false, 0b10, 0b01, pack_check, nullptr, pack_run, nullptr},
     {"unpack_bgra8", "BBii", false, 0b10, 0b01, unpack_check, nullptr, unpack_run, nullptr},
     {"blur3x3", "BBii", false, 0b10, 0b01, blur_check, nullptr, blur_run, nullptr},
+    // the showcase's compute passes (bench/showcase.jl), headless; P = scene constants
+    {"sc_move_lights", "BBBBBBi", false, 0b0111110, 0b0000111, sc_move_lights_check, nullptr, sc_move_lights_run,
+     nullptr},
+    {"sc_cull", "BBBBi", false, 0b01110, 0b00011, sc_cull_check, nullptr, sc_cull_run, nullptr},
+    {"sc_write_draw", "BBi", false, 0b010, 0b001, sc_write_draw_check, nullptr, sc_write_draw_run, nullptr},
+    {"sc_tile_lights", "BBBBBiiiii", false, 0b0000011100, 0b0000000011, sc_tile_lights_check, nullptr,
+     sc_tile_lights_run, nullptr},
+    {"sc_ssao", "BBBBiii", false, 0b0001110, 0b0000001, sc_ssao_check, nullptr, sc_ssao_run, nullptr},
+    {"sc_ao_blur", "BBB", false, 0b110, 0b001, sc_ao_blur_check, nullptr, sc_ao_blur_run, nullptr},
+    {"sc_shade", "BBBBBBBBBBBBiii", false, 0b000111111111110, 0b000000000000001, sc_shade_check, nullptr,
+     sc_shade_run, nullptr},
+    {"sc_bright", "BBBiii", false, 0b000110, 0b000001, sc_bright_check, nullptr, sc_bright_run, nullptr},
+    {"sc_blur", "BBii", false, 0b0010, 0b0001, sc_blur_check, nullptr, sc_blur_run, nullptr},
+    {"sc_composite", "BBBBiii", false, 0b0001110, 0b0000001, sc_composite_check, nullptr, sc_composite_run,
+     nullptr},
 };
 #undef EW
 

@@ -460,3 +460,194 @@ def build_raster(dev, na: int = 200_000, nb: int = 100_000, seed: int = 0, stage
         src = dst
     plan = Plan(g, **plan_kw)
     return RasterWorkload(B, g, plan, inputs)
+
+
+# ── the showcase's compute passes (bench/showcase.jl), headless ─────────────
+# The reference fills its g-buffer and shadow map with raster passes (a graphics
+# stack this backend does not have). Here a seeded analytic scene — the floor
+# plane and spheres standing in for the crystals — is ray-cast on the host into
+# the same buffers: packed RGBA8 albedo+roughness, metal+emission, normal, and
+# depth in [0, 1] (1 = sky) as the reference's projection writes it.
+SC_PARAMS = 80
+SC_OFF = dict(vp=0, invvp=16, sunvp=32, eye=48, sun=52, suncol=56, fog=60, emit=61, stexel=62, sbias=63, aoamb=64,
+              aodirect=65, aoradius=66, aobias=67, threshold=68, exposure=69, bloom=70, aosharp=71, time=72)
+
+
+def _look(eye, f, r, u):
+    """The reference's view matrix (row-major here): rows r, u, -f with translation."""
+    v = np.eye(4)
+    v[0, :3], v[1, :3], v[2, :3] = r, u, -f
+    v[0, 3], v[1, 3], v[2, 3] = -r @ eye, -u @ eye, f @ eye
+    return v
+
+
+def showcase_camera(t: float, radius: float, height: float, w: int, h: int):
+    """camera (bench/showcase.jl:115-127): orbit around (0, 13, 0); Vulkan
+    clip (y down, depth 0..1); returns (vp row-major float64, eye)."""
+    eye = np.array([radius * np.cos(0.11 * t), height + 4.0 * np.sin(0.17 * t), radius * np.sin(0.11 * t)])
+    f = np.array([0.0, 13.0, 0.0]) - eye
+    f /= np.linalg.norm(f)
+    r = np.cross(f, [0.0, 1.0, 0.0])
+    r /= np.linalg.norm(r)
+    u = np.cross(r, f)
+    tn = np.tan(50.0 * np.pi / 360.0)
+    near, far = 0.5, 400.0
+    proj = np.zeros((4, 4))
+    proj[0, 0], proj[1, 1] = 1.0 / ((w / h) * tn), -1.0 / tn
+    proj[2, 2], proj[2, 3], proj[3, 2] = far / (near - far), near * far / (near - far), -1.0
+    return proj @ _look(eye, f, r, u), eye
+
+
+def showcase_sunmatrix(sundir, extent: float, depth: float):
+    """sunmatrix (bench/showcase.jl:132-144): orthographic box down the sun."""
+    sundir = np.asarray(sundir, np.float64)
+    f = -sundir / np.linalg.norm(sundir)
+    up = np.array([1.0, 0.0, 0.0]) if abs(f[1]) > 0.95 else np.array([0.0, 1.0, 0.0])
+    r = np.cross(f, up)
+    r /= np.linalg.norm(r)
+    u = np.cross(r, f)
+    eye = sundir / np.linalg.norm(sundir) * (0.5 * depth)
+    near, far = 1.0, depth
+    proj = np.eye(4)
+    proj[0, 0], proj[1, 1] = 1.0 / extent, -1.0 / extent
+    proj[2, 2], proj[2, 3] = -1.0 / (far - near), -near / (far - near)
+    return proj @ _look(eye, f, r, u)
+
+
+def _colmajor(m):
+    return np.asarray(m, np.float32).T.reshape(-1)
+
+
+def _raycast(origin, dirs, spheres):
+    """Nearest hit of rays (n, 3) against the plane y = 0 and spheres (m, 4):
+    (t, index) with index -1 for the floor, -2 for a miss."""
+    t = np.full(dirs.shape[0], np.inf)
+    idx = np.full(dirs.shape[0], -2, np.int64)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        tf = -origin[..., 1] / dirs[:, 1]
+    hit = (dirs[:, 1] < 0) & (tf > 0)
+    t[hit], idx[hit] = tf[hit], -1
+    for k, (cx, cy, cz, rad) in enumerate(spheres):
+        oc = origin - np.array([cx, cy, cz])
+        b = (oc * dirs).sum(-1)
+        c = (oc * oc).sum(-1) - rad * rad
+        disc = b * b - c
+        ok = disc > 0
+        tk = np.where(ok, -b - np.sqrt(np.where(ok, disc, 0.0)), np.inf)
+        better = ok & (tk > 1e-3) & (tk < t)
+        t[better], idx[better] = tk[better], k
+    return t, idx
+
+
+@dataclass
+class ShowcaseScene:
+    w: int
+    h: int
+    tile: int
+    pertile: int
+    nsample: int
+    shift: int
+    P: np.ndarray        # float32[80] scene constants
+    alb: np.ndarray      # (h, w) uint32
+    mat: np.ndarray
+    nrm: np.ndarray
+    dep: np.ndarray      # (h, w) float32
+    smap: np.ndarray     # (res, res) float32
+    home: np.ndarray     # (nlight, 4) light orbit centres and reach (sc_move_lights moves them)
+    lcol: np.ndarray     # (nlight, 4) colour and intensity
+    centers: np.ndarray  # (ninst, 4) instance bounding spheres; the last nlight stand for the lights
+    params: np.ndarray   # (ninst, 4) instance surface parameters
+
+    @property
+    def first(self) -> int:
+        return self.centers.shape[0] - self.home.shape[0]
+
+
+def showcase_scene(w: int = 1600, h: int = 900, seed: int = 9, smap_res: int = 2048, nlight: int = 44,
+                   nspheres: int = 90, ninst: int = 5044, t: float = 3.0) -> ShowcaseScene:
+    """A seeded scene at the reference's settings (bench/showcase.jl:28-45,
+    647-676): 16-pixel tiles with up to 32 lights, 12 occlusion samples, bloom
+    at a quarter of each axis, the sun at normalize(-0.62, 0.22, 0.35)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    vp, eye = showcase_camera(t, 62.0, 14.0, w, h)
+    inv = np.linalg.inv(vp)
+    sun = np.array([-0.62, 0.22, 0.35])
+    sun /= np.linalg.norm(sun)
+    extent, sdepth = 150.0, 520.0
+    sunvp = showcase_sunmatrix(np.array([-0.62, 0.045, 0.35]), extent, sdepth)
+    # spheres: a ring of large ones around a plaza and smaller ones beyond
+    ang = rng.uniform(0, 2 * np.pi, nspheres)
+    dist = np.where(np.arange(nspheres) < 26, rng.uniform(46, 64, nspheres), rng.uniform(60, 140, nspheres))
+    rad = np.where(np.arange(nspheres) < 26, rng.uniform(4, 9, nspheres), rng.uniform(1, 4, nspheres))
+    spheres = np.stack([dist * np.cos(ang), rad * rng.uniform(0.3, 1.0, nspheres), dist * np.sin(ang), rad], 1)
+    col = rng.uniform(0.2, 0.7, (nspheres, 3))
+    rough = rng.uniform(0.08, 0.5, nspheres) ** 2 + 0.04
+    metal = np.where(rng.uniform(size=nspheres) < 0.4, 0.9, 0.05)
+    emit = np.where(rng.uniform(size=nspheres) < 0.1, rng.uniform(0.3, 1.0, nspheres), 0.0)
+
+    # primary rays through pixel centres
+    py, px = np.mgrid[0:h, 0:w].astype(np.float64)
+    nx, ny = 2 * (px + 0.5) / w - 1, 2 * (py + 0.5) / h - 1
+    pts = np.stack([nx, ny], -1).reshape(-1, 2)
+    near = np.c_[pts, np.zeros(len(pts)), np.ones(len(pts))] @ inv.T
+    far = np.c_[pts, np.ones(len(pts)), np.ones(len(pts))] @ inv.T
+    near, far = near[:, :3] / near[:, 3:], far[:, :3] / far[:, 3:]
+    dirs = far - near
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    tt, idx = _raycast(near, dirs, spheres)
+    world = near + dirs * np.where(np.isfinite(tt), tt, 0)[:, None]
+    clip = np.c_[world, np.ones(len(world))] @ vp.T
+    dep = np.where(idx > -2, clip[:, 2] / clip[:, 3], 1.0).astype(np.float32)
+    dep = np.where(dep < 1.0, dep, np.float32(1.0)).astype(np.float32)
+    n = np.zeros_like(world)
+    n[idx == -1] = [0.0, 1.0, 0.0]
+    sp = idx >= 0
+    n[sp] = (world[sp] - spheres[idx[sp], :3]) / spheres[idx[sp], 3:4]
+    q8 = lambda x: np.clip(np.rint(np.asarray(x) * 255.0), 0, 255).astype(np.uint32)  # noqa: E731
+    alb_rgb = np.where(sp[:, None], col[np.maximum(idx, 0)], [0.045, 0.047, 0.056])
+    alb_r = np.where(sp, rough[np.maximum(idx, 0)], 0.13)
+    met = np.where(sp, metal[np.maximum(idx, 0)], 0.30)
+    emi = np.where(sp, emit[np.maximum(idx, 0)], 0.0)
+    alb = q8(alb_rgb[:, 0]) | q8(alb_rgb[:, 1]) << 8 | q8(alb_rgb[:, 2]) << 16 | q8(alb_r) << 24
+    mat = q8(met) | q8(emi) << 8 | np.uint32(255) << 24
+    nrm = q8(0.5 * n[:, 0] + 0.5) | q8(0.5 * n[:, 1] + 0.5) << 8 | q8(0.5 * n[:, 2] + 0.5) << 16 | np.uint32(255) << 24
+
+    # the shadow map: depth (the sun's clip z) of the nearest surface per texel
+    ty, tx = np.mgrid[0:smap_res, 0:smap_res].astype(np.float64)
+    sx, sy = 2 * (tx + 0.5) / smap_res - 1, 2 * (ty + 0.5) / smap_res - 1
+    sinv = np.linalg.inv(sunvp)
+    spts = np.stack([sx, sy], -1).reshape(-1, 2)
+    o = np.c_[spts, np.zeros(len(spts)), np.ones(len(spts))] @ sinv.T
+    e = np.c_[spts, np.ones(len(spts)), np.ones(len(spts))] @ sinv.T
+    o, e = o[:, :3] / o[:, 3:], e[:, :3] / e[:, 3:]
+    sd = e - o
+    sl = np.linalg.norm(sd, axis=1, keepdims=True)
+    st, sidx = _raycast(o, sd / sl, spheres)
+    sw = o + sd / sl * np.where(np.isfinite(st), st, 0)[:, None]
+    sz = (np.c_[sw, np.ones(len(sw))] @ sunvp.T)[:, 2]
+    smap = np.where(sidx > -2, sz, 1.0).astype(np.float32).reshape(smap_res, smap_res)
+
+    # lights (bench/showcase.jl:659-664) and instances
+    a = rng.uniform(0, 2 * np.pi, nlight)
+    r = 12 + 62 * rng.uniform(size=nlight)
+    home = np.stack([r * np.cos(a), 2 + 17 * rng.uniform(size=nlight) ** 1.6, r * np.sin(a),
+                     24 + 22 * rng.uniform(size=nlight)], 1).astype(np.float32)
+    hue = 6 * rng.uniform(size=nlight)
+    i6, fr = np.floor(hue).astype(int), hue - np.floor(hue)
+    tints = np.array([[1, f, 0] if i == 0 else [1 - f, 1, 0] if i == 1 else [0, 1, f] if i == 2 else
+                      [0, 1 - f, 1] if i == 3 else [f, 0, 1] if i == 4 else [1, 0, 1 - f] for i, f in zip(i6, fr)])
+    lcol = np.c_[0.1 + 0.9 * tints, np.full(nlight, 5.5)].astype(np.float32)
+    centers = np.c_[rng.uniform(-230, 230, ninst), rng.uniform(0, 40, ninst), rng.uniform(-230, 230, ninst),
+                    rng.uniform(1, 20, ninst)].astype(np.float32)
+    params = np.zeros((ninst, 4), np.float32)
+
+    P = np.zeros(SC_PARAMS, np.float32)
+    P[0:16], P[16:32], P[32:48] = _colmajor(vp), _colmajor(inv), _colmajor(sunvp)
+    P[48:51], P[52:55] = eye, sun
+    P[56:60] = [1.0, 0.55, 0.28, 6.5]
+    smap_texel = 2 * extent / smap_res
+    for k, v in dict(fog=0.0035, emit=9.0, stexel=smap_texel, sbias=0.004, aoamb=2.6, aodirect=0.6, aoradius=4.5,
+                     aobias=0.05, threshold=1.6, exposure=0.85, bloom=0.30, aosharp=900.0, time=t).items():
+        P[SC_OFF[k]] = v
+    return ShowcaseScene(w, h, 16, 32, 12, 4, P, alb.reshape(h, w), mat.reshape(h, w), nrm.reshape(h, w),
+                         dep.reshape(h, w), smap, home, lcol, centers, params)

@@ -13,14 +13,14 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-SRC = HERE / "mantle_oracle.c"
+SRCS = [HERE / "mantle_oracle.c", HERE / "showcase_oracle.c"]
 OUT = HERE / "liboracle.so"
 
 
 def build(force: bool = False) -> Path:
-    if not force and OUT.exists() and OUT.stat().st_mtime >= SRC.stat().st_mtime:
+    if not force and OUT.exists() and all(OUT.stat().st_mtime >= s.stat().st_mtime for s in SRCS):
         return OUT
-    cmd = ["gcc", "-O2", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared", "-o", str(OUT), str(SRC), "-lm"]
+    cmd = ["gcc", "-O2", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared", "-o", str(OUT), *map(str, SRCS), "-lm"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed: {' '.join(cmd)}\n{r.stderr}")

@@ -676,6 +676,17 @@ def lib():
         h.oracle_pack_bgra8.argtypes = [u8p, f32p, C.c_int64]
         h.oracle_unpack_bgra8.argtypes = [f32p, u8p, C.c_int, C.c_int]
         h.oracle_blur3x3.argtypes = [f32p, f32p, C.c_int, C.c_int]
+        I = C.c_int  # noqa: E741
+        h.oracle_sc_move_lights.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, I, I]
+        h.oracle_sc_cull.argtypes = [u8p, f32p, f32p, I]
+        h.oracle_sc_tile_lights.argtypes = [u32p, u32p, f32p, f32p, f32p, I, I, I, I, I]
+        h.oracle_sc_shade.argtypes = [f32p, u32p, u32p, u32p, f32p, f32p, f32p, u32p, u32p, f32p, f32p, f32p,
+                                      I, I, I, I, I]
+        h.oracle_sc_ssao.argtypes = [f32p, f32p, u32p, f32p, I, I, I]
+        h.oracle_sc_ao_blur.argtypes = [f32p, f32p, f32p, I, I]
+        h.oracle_sc_bright.argtypes = [f32p, f32p, f32p, I, I, I]
+        h.oracle_sc_blur.argtypes = [f32p, f32p, I, I, I, I]
+        h.oracle_sc_composite.argtypes = [f32p, f32p, f32p, f32p, I, I, I, I, I]
         h.oracle_max_threads.restype = C.c_int
         _lib = h
     return _lib
@@ -850,3 +861,87 @@ def uniform(seed: int, n: int, lo: float, hi: float, stream: int = 0) -> np.ndar
 def integers(seed: int, n: int, hi: int, stream: int = 0) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64([seed, stream]))
     return rng.integers(0, hi, n, dtype=np.int32)
+
+
+# ── the showcase's compute passes (showcase_oracle.c) ───────────────────────
+# Arrays: images [H][W] (float4 images as (H, W, 4) float32), packed RGBA8
+# g-buffer channels uint32, lights and instances (n, 4) float32, P the scene
+# constants (float32[80], offsets as in showcase_oracle.c).
+def _f(a):
+    return _p(np.ascontiguousarray(a, np.float32), C.c_float)
+
+
+def _u(a):
+    return _p(np.ascontiguousarray(a, np.uint32), C.c_uint32)
+
+
+def sc_move_lights(centers, params, home, lcol, P, first):
+    """-> (pos, centers', params') after moving the lights (showcase.jl:214-229)."""
+    n = home.shape[0]
+    pos = np.zeros((n, 4), np.float32)
+    c = np.array(centers, np.float32, copy=True)
+    q = np.array(params, np.float32, copy=True)
+    lib().oracle_sc_move_lights(_p(pos, C.c_float), _p(c, C.c_float), _p(q, C.c_float), _f(home), _f(lcol), _f(P),
+                                first, n)
+    return pos, c, q
+
+
+def sc_cull(centers, M):
+    """Boolean mask of the instances inside the frustum of the 16-float column-major M."""
+    keep = np.zeros(centers.shape[0], np.uint8)
+    lib().oracle_sc_cull(_p(keep, C.c_uint8), _f(centers), _f(M), centers.shape[0])
+    return keep.astype(bool)
+
+
+def sc_tile_lights(dep, lpos, P, tile, pertile):
+    h, w = dep.shape
+    ntx, nty = -(-w // tile), -(-h // tile)
+    tl = np.zeros(ntx * nty * pertile, np.uint32)
+    tc = np.zeros(ntx * nty, np.uint32)
+    lib().oracle_sc_tile_lights(_p(tl, C.c_uint32), _p(tc, C.c_uint32), _f(dep), _f(lpos), _f(P), w, h, tile,
+                                lpos.shape[0], pertile)
+    return tl, tc
+
+
+def sc_ssao(dep, nrm, P, nsample):
+    h, w = dep.shape
+    ao = np.zeros((-(-h // 2), -(-w // 2), 2), np.float32)
+    lib().oracle_sc_ssao(_p(ao, C.c_float), _f(dep), _u(nrm), _f(P), w, h, nsample)
+    return ao
+
+
+def sc_ao_blur(src, P):
+    aoh, aow = src.shape[:2]
+    dst = np.zeros((aoh, aow), np.float32)
+    lib().oracle_sc_ao_blur(_p(dst, C.c_float), _f(src), _f(P), aow, aoh)
+    return dst
+
+
+def sc_shade(alb, mat, nrm, dep, lpos, lcol, tl, tc, smap, aomap, P, tile, pertile):
+    h, w = dep.shape
+    hdr = np.zeros((h, w, 4), np.float32)
+    lib().oracle_sc_shade(_p(hdr, C.c_float), _u(alb), _u(mat), _u(nrm), _f(dep), _f(lpos), _f(lcol), _u(tl), _u(tc),
+                          _f(smap), _f(aomap), _f(P), w, h, tile, pertile, smap.shape[0])
+    return hdr
+
+
+def sc_bright(hdr, P, shift):
+    h, w = hdr.shape[:2]
+    dst = np.zeros((-(-h // shift), -(-w // shift), 4), np.float32)
+    lib().oracle_sc_bright(_p(dst, C.c_float), _f(hdr), _f(P), w, h, shift)
+    return dst
+
+
+def sc_blur(src, dx, dy):
+    bh, bw = src.shape[:2]
+    dst = np.zeros_like(src, dtype=np.float32)
+    lib().oracle_sc_blur(_p(dst, C.c_float), _f(src), bw, bh, dx, dy)
+    return dst
+
+
+def sc_composite(hdr, bloom, P, shift):
+    h, w = hdr.shape[:2]
+    bh, bw = bloom.shape[:2]
+    out = np.zeros((h, w, 4), np.float32)
+    lib().oracle_sc_composite(_p(out, C.c_float), _f(hdr), _f(bloom), _f(P), w, h, bw, bh, shift)
+    return out

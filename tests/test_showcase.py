@@ -1,0 +1,232 @@
+"""The showcase's compute passes (bench/showcase.jl): the C oracle against
+numpy restatements on the CPU, each CUDA kernel against the oracle on the GPU,
+and the passes as one graph.
+
+Tolerances. Both sides perform the same IEEE single-precision +, -, *, / and
+sqrt in the same order (the CUDA file is compiled without FMA contraction, the
+oracle without contraction), so kernels without transcendental functions match
+bit for bit. expf, powf, sinf and cosf may round differently in the last place
+on the GPU: kernels that use them are held to 1e-5 relative (plus 1e-6
+absolute). Where such a difference can move a sample across a pixel or a
+comparison (occlusion samples, shadow-map taps), a few pixels can take the
+other branch: those kernels require 99.5 % of pixels within the tolerance.
+"""
+import numpy as np
+import pytest
+
+import mantle_cuda as M
+from mantle_cuda.workloads import SC_OFF, showcase_scene
+from oracle import oracle as O
+
+W, H, SMAP = 320, 184, 512  # 184 rows: the last tile row is partial
+
+
+@pytest.fixture(scope="module")
+def scene():
+    return showcase_scene(W, H, seed=9, smap_res=SMAP)
+
+
+def _close(got, want, rel=1e-5, absol=1e-6, frac=1.0):
+    ok = np.abs(got.astype(np.float64) - want) <= absol + rel * np.abs(want)
+    assert ok.mean() >= frac, f"{(~ok).sum()} of {ok.size} outside tolerance, worst {np.abs(got - want).max()}"
+
+
+# ── CPU: the oracle against plain numpy restatements ───────────────────────
+def test_scene_is_plausible(scene):
+    d = scene.dep
+    assert 0.2 < (d < 1).mean() < 0.9 and d.min() > 0 and d.max() == 1.0
+    n = np.stack([((scene.nrm >> s) & 255) / 255.0 * 2 - 1 for s in (0, 8, 16)], -1)[d < 1]
+    assert np.abs(np.linalg.norm(n, axis=-1) - 1).max() < 0.02
+    assert (scene.smap < 1).any() and (scene.smap == 1).any()
+
+
+def test_oracle_blur_bright_composite_against_numpy():
+    rng = np.random.default_rng(3)
+    src = rng.uniform(0, 4, (13, 21, 4)).astype(np.float32)
+    # 13 taps, weights exp(-k^2/16), clamp to edge, along x
+    g = np.exp(-np.arange(-6, 7, dtype=np.float64) ** 2 / 16)
+    idx = np.clip(np.arange(21)[:, None] + np.arange(-6, 7)[None], 0, 20)
+    want = (src[:, idx, :3] * g[None, None, :, None]).sum(2) / g.sum()
+    assert np.abs(O.sc_blur(src, 1, 0)[..., :3] - want).max() < 1e-5 * np.abs(want).max()
+    P = np.zeros(80, np.float32)
+    P[SC_OFF["threshold"]], P[SC_OFF["bloom"]], P[SC_OFF["exposure"]] = 1.6, 0.3, 0.85
+    br = O.sc_bright(src, P, 4)
+    m = src[..., :3].max(-1)
+    keep = np.where(m > 1.6, (m - 1.6) / m, 0.0)[..., None] * src[..., :3]
+    want = np.zeros((4, 6, 3))
+    for iy in range(4):
+        for ix in range(6):
+            for dy in (0, 2):
+                for dx in (0, 2):
+                    want[iy, ix] += keep[min(4 * iy + dy, 12), min(4 * ix + dx, 20)]
+    assert np.abs(br[..., :3] - want * 0.25).max() < 1e-5 * max(1.0, np.abs(want).max())
+    out = O.sc_composite(src, br, P, 4)
+    assert out.shape == (13, 21, 4) and np.all((out[..., :3] >= 0) & (out[..., :3] < 1))
+    # a constant bloom composites to the Reinhard of (hdr + 0.3 c) * 0.85
+    flat = np.full((4, 6, 4), 0.5, np.float32)
+    v = (src[..., :3].astype(np.float64) + 0.15) * 0.85
+    assert np.abs(O.sc_composite(src, flat, P, 4)[..., :3] - v / (1 + v)).max() < 1e-6
+
+
+def test_oracle_tiles_and_cull_against_python(scene):
+    lpos, _, _ = O.sc_move_lights(scene.centers, scene.params, scene.home, scene.lcol, scene.P, scene.first)
+    tl, tc = O.sc_tile_lights(scene.dep, lpos, scene.P, 16, 32)
+    inv = scene.P[16:32].reshape(4, 4).T.astype(np.float64)
+    ntx = -(-W // 16)
+    for ti in (0, 7, 77, ntx * 11 + 3, len(tc) - 1):  # includes a partial last-row tile
+        tx, ty = ti % ntx, ti // ntx
+        blk = scene.dep[ty * 16:(ty + 1) * 16, tx * 16:(tx + 1) * 16]
+        cov = blk[blk < 1]
+        if cov.size == 0:
+            assert tc[ti] == 0
+            continue
+        x0, y0, x1, y1 = tx * 16, ty * 16, min(tx * 16 + 16, W), min(ty * 16 + 16, H)
+        corners = [inv @ [2 * x / W - 1, 2 * y / H - 1, d, 1] for x in (x0, x1) for y in (y0, y1)
+                   for d in (cov.min(), cov.max())]
+        pts = np.array([c[:3] / c[3] for c in corners])
+        lo, hi = pts.min(0), pts.max(0)
+        gap = np.maximum(0, np.maximum(lo - lpos[:, :3], lpos[:, :3] - hi))
+        want = (np.nonzero((gap ** 2).sum(1) <= lpos[:, 3] ** 2 * (1 + 1e-5))[0] + 1)[:32]
+        got = tl[ti * 32:ti * 32 + tc[ti]]
+        assert set(got) <= set(want) and len(set(want) - set(got)) <= 1  # float64 vs float32 at the boundary
+    vp = scene.P[0:16]
+    keep = O.sc_cull(scene.centers, vp)
+    m = vp.reshape(4, 4).T.astype(np.float64)
+    planes = [m[3] + m[0], m[3] - m[0], m[3] + m[1], m[3] - m[1], m[2], m[3] - m[2]]
+    c = scene.centers.astype(np.float64)
+    want = np.ones(len(c), bool)
+    for p in planes:
+        p = p / np.linalg.norm(p[:3])
+        want &= c[:, :3] @ p[:3] + p[3] >= -c[:, 3]
+    assert (keep != want).sum() <= 2 and 0 < keep.sum() < len(keep)
+
+
+# ── GPU: each kernel against the oracle ─────────────────────────────────────
+def _dev(a):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        return torch.from_numpy(a.view(np.int32)).cuda()
+    return torch.from_numpy(a).cuda()
+
+
+def _host(t, dtype=None):
+    a = t.cpu().numpy()
+    return a.view(dtype) if dtype is not None else a
+
+
+@pytest.fixture(scope="module")
+def chain(scene):
+    """The oracle's pass outputs, each computed from the previous oracle outputs."""
+    s = scene
+    lpos, centers, params = O.sc_move_lights(s.centers, s.params, s.home, s.lcol, s.P, s.first)
+    tl, tc = O.sc_tile_lights(s.dep, lpos, s.P, s.tile, s.pertile)
+    ao = O.sc_ssao(s.dep, s.nrm, s.P, s.nsample)
+    aomap = O.sc_ao_blur(ao, s.P)
+    hdr = O.sc_shade(s.alb, s.mat, s.nrm, s.dep, lpos, s.lcol, tl, tc, s.smap, aomap, s.P, s.tile, s.pertile)
+    bloom_a = O.sc_bright(hdr, s.P, s.shift)
+    bloom_b = O.sc_blur(bloom_a, 1, 0)
+    bloom_c = O.sc_blur(bloom_b, 0, 1)
+    out = O.sc_composite(hdr, bloom_c, s.P, s.shift)
+    return dict(lpos=lpos, centers=centers, params=params, tl=tl, tc=tc, ao=ao, aomap=aomap, hdr=hdr,
+                bloom_a=bloom_a, bloom_b=bloom_b, bloom_c=bloom_c, out=out)
+
+
+@pytest.mark.gpu
+def test_move_lights_and_cull(dev, scene, chain):
+    import torch
+    s = scene
+    st = torch.cuda.current_stream().cuda_stream
+    pos = _dev(np.zeros_like(s.home))
+    centers, params = _dev(s.centers), _dev(s.params)
+    M.launch(M.kernels.sc_move_lights, (pos, centers, params, _dev(s.home), _dev(s.lcol), _dev(s.P), s.first),
+             s.home.shape[0], stream=st)
+    _close(_host(pos), chain["lpos"])
+    _close(_host(centers), chain["centers"])
+    assert np.array_equal(_host(params), chain["params"])
+    # cull against the camera and against the sun, then the draw commands
+    n = s.centers.shape[0]
+    for off in (0, 32):
+        visible = _dev(np.full(n, 7, np.uint32))
+        counter = _dev(np.zeros(1, np.uint32))
+        M.launch(M.kernels.sc_cull, (visible, counter, _dev(s.centers), _dev(s.P), off), n, stream=st)
+        cnt = int(_host(counter, np.uint32)[0])
+        want = np.nonzero(O.sc_cull(s.centers, s.P[off:off + 16]))[0] + 1
+        assert cnt == len(want) and np.array_equal(np.sort(_host(visible, np.uint32)[:cnt]), want)
+        cmd = _dev(np.zeros(4, np.uint32))
+        M.launch(M.kernels.sc_write_draw, (cmd, counter, 72), 1, stream=st)
+        assert list(_host(cmd, np.uint32)) == [72 * cnt, 1, 0, 0]
+    # a counter that was not cleared: survivors past the list are dropped, never written beyond it
+    visible = _dev(np.zeros(n + 4, np.uint32))
+    counter = _dev(np.array([n - 3], np.uint32))
+    M.launch(M.kernels.sc_cull, (visible, counter, _dev(s.centers), _dev(s.P), 0), n, stream=st)
+    assert not _host(visible, np.uint32)[n:].any()
+
+
+@pytest.mark.gpu
+def test_tile_lights_exact(dev, scene, chain):
+    import torch
+    s = scene
+    ntx, nty = -(-W // s.tile), -(-H // s.tile)
+    tl = _dev(np.zeros(ntx * nty * s.pertile, np.uint32))
+    tc = _dev(np.zeros(ntx * nty, np.uint32))
+    M.launch(M.kernels.sc_tile_lights, (tl, tc, _dev(s.dep), _dev(chain["lpos"]), _dev(s.P), W, H, s.tile,
+                                        chain["lpos"].shape[0], s.pertile), (ntx, nty),
+             stream=torch.cuda.current_stream().cuda_stream)
+    got_c = _host(tc, np.uint32)
+    assert np.array_equal(got_c, chain["tc"]) and got_c.max() > 1
+    got_l = _host(tl, np.uint32).reshape(-1, s.pertile)
+    want_l = chain["tl"].reshape(-1, s.pertile)
+    for t in range(len(got_c)):
+        assert np.array_equal(got_l[t, :got_c[t]], want_l[t, :got_c[t]])
+
+
+@pytest.mark.gpu
+def test_ssao_and_ao_blur(dev, scene, chain):
+    import torch
+    s = scene
+    st = torch.cuda.current_stream().cuda_stream
+    aow, aoh = -(-W // 2), -(-H // 2)
+    ao = _dev(np.zeros((aoh, aow, 2), np.float32))
+    M.launch(M.kernels.sc_ssao, (ao, _dev(s.dep), _dev(s.nrm), _dev(s.P), W, H, s.nsample), (aow, aoh), stream=st)
+    got = _host(ao)
+    assert np.array_equal(got[..., 1], chain["ao"][..., 1])
+    assert (chain["ao"][..., 0] > 0).mean() > 0.05  # the scene occludes somewhere
+    _close(got[..., 0], chain["ao"][..., 0], rel=1e-5, absol=1e-6, frac=0.995)
+    blurred = _dev(np.zeros((aoh, aow), np.float32))
+    M.launch(M.kernels.sc_ao_blur, (blurred, _dev(chain["ao"]), _dev(s.P)), (aow, aoh), stream=st)
+    _close(_host(blurred), chain["aomap"], rel=1e-5, absol=1e-6)
+
+
+@pytest.mark.gpu
+def test_shade(dev, scene, chain):
+    import torch
+    s = scene
+    hdr = _dev(np.zeros((H, W, 4), np.float32))
+    args = (hdr, _dev(s.alb), _dev(s.mat), _dev(s.nrm), _dev(s.dep), _dev(chain["lpos"]), _dev(s.lcol),
+            _dev(chain["tl"]), _dev(chain["tc"]), _dev(s.smap), _dev(chain["aomap"]), _dev(s.P), s.tile, s.pertile,
+            SMAP)
+    M.launch(M.kernels.sc_shade, args, (W, H), stream=torch.cuda.current_stream().cuda_stream)
+    got = _host(hdr)
+    assert np.all(got[..., 3] == 1.0) and np.isfinite(got).all()
+    _close(got[..., :3], chain["hdr"][..., :3], rel=1e-5, absol=1e-6, frac=0.995)
+
+
+@pytest.mark.gpu
+def test_bright_blur_composite(dev, scene, chain):
+    import torch
+    s = scene
+    st = torch.cuda.current_stream().cuda_stream
+    bw, bh = -(-W // s.shift), -(-H // s.shift)
+    a = _dev(np.zeros((bh, bw, 4), np.float32))
+    M.launch(M.kernels.sc_bright, (a, _dev(chain["hdr"]), _dev(s.P), W, H, s.shift), (bw, bh), stream=st)
+    assert np.array_equal(_host(a), chain["bloom_a"])  # no transcendental function: bit for bit
+    b = _dev(np.zeros((bh, bw, 4), np.float32))
+    M.launch(M.kernels.sc_blur, (b, _dev(chain["bloom_a"]), 1, 0), (bw, bh), stream=st)
+    _close(_host(b), chain["bloom_b"])
+    out = _dev(np.zeros((H, W, 4), np.float32))
+    M.launch(M.kernels.sc_composite, (out, _dev(chain["hdr"]), _dev(chain["bloom_c"]), _dev(s.P), bw, bh, s.shift),
+             (W, H), stream=st)
+    assert np.array_equal(_host(out), chain["out"])
+    with pytest.raises(M.MantleError, match="overlap"):
+        M.launch(M.kernels.sc_blur, (b, b, 1, 0), (bw, bh), stream=st)
