@@ -651,3 +651,91 @@ def showcase_scene(w: int = 1600, h: int = 900, seed: int = 9, smap_res: int = 2
         P[SC_OFF[k]] = v
     return ShowcaseScene(w, h, 16, 32, 12, 4, P, alb.reshape(h, w), mat.reshape(h, w), nrm.reshape(h, w),
                          dep.reshape(h, w), smap, home, lcol, centers, params)
+
+
+@dataclass
+class ShowcaseWorkload:
+    scene: ShowcaseScene
+    bufs: dict
+    graph: Graph
+    plan: Plan
+
+    @property
+    def nlight(self) -> int:
+        return self.scene.home.shape[0]
+
+
+def build_showcase(dev, scene: ShowcaseScene, **plan_kw) -> ShowcaseWorkload:
+    """The showcase's compute passes as one graph, in the reference's order
+    (bench/showcase.jl:700-790): clear the two counters, move the lights, cull
+    against the camera and the sun, write both draw commands, then tiles, SSAO,
+    the AO blur, lighting, bright pass, the separable bloom blur and the
+    composite. The g-buffer and the shadow map are persistent inputs (their
+    raster passes are not built); the tile lists, occlusion, HDR and bloom
+    images are transients, placed and aliased by the planner. Scene constants
+    live in the persistent buffer `P` (update it per frame)."""
+    s = scene
+    w, h, tile, pertile, shift = s.w, s.h, s.tile, s.pertile, s.shift
+    ntx, nty = -(-w // tile), -(-h // tile)
+    aow, aoh = -(-w // 2), -(-h // 2)
+    bw, bh = -(-w // shift), -(-h // shift)
+    ninst, nlight = s.centers.shape[0], s.home.shape[0]
+    B = {k: Buffer(dev, np.ascontiguousarray(v)) for k, v in dict(
+        P=s.P, alb=s.alb.reshape(-1), mat=s.mat.reshape(-1), nrm=s.nrm.reshape(-1), dep=s.dep.reshape(-1),
+        smap=s.smap.reshape(-1), home=s.home.reshape(-1), lcol=s.lcol.reshape(-1),
+        centers=s.centers.reshape(-1), params=s.params.reshape(-1)).items()}
+    B["lpos"] = Buffer(dev, np.float32, 4 * nlight)
+    for k in ("visible", "sunvisible"):
+        B[k] = Buffer(dev, np.ones(ninst, np.uint32))
+    for k in ("counter", "suncounter"):
+        B[k] = Buffer(dev, np.zeros(1, np.uint32))
+    for k in ("drawcmd", "sundrawcmd"):
+        B[k] = Buffer(dev, np.zeros(4, np.uint32))
+    B["out"] = Buffer(dev, np.float32, 4 * w * h)
+    g = Graph(dev)
+    tl = Transient.Buffer(g, np.uint32, ntx * nty * pertile)
+    tc = Transient.Buffer(g, np.uint32, ntx * nty)
+    aoraw = Transient.Buffer(g, np.float32, 2 * aow * aoh)
+    aomap = Transient.Buffer(g, np.float32, aow * aoh)
+    hdr = Transient.Buffer(g, np.float32, 4 * w * h)
+    bloom_a = Transient.Buffer(g, np.float32, 4 * bw * bh)
+    bloom_b = Transient.Buffer(g, np.float32, 4 * bw * bh)
+    R = lambda p, b: use(p, b, read=True)  # noqa: E731
+    W = lambda p, b: use(p, b, write=True)  # noqa: E731
+    RW = lambda p, b: use(p, b, read=True, write=True)  # noqa: E731
+
+    def clear(p):
+        dispatch(p, kernels.fill_span, (W(p, B["counter"]), 0, 0.0), 1)
+        dispatch(p, kernels.fill_span, (W(p, B["suncounter"]), 0, 0.0), 1)
+
+    def draw_count(p):
+        dispatch(p, kernels.sc_write_draw, (W(p, B["drawcmd"]), R(p, B["counter"]), 72), 1)
+        dispatch(p, kernels.sc_write_draw, (W(p, B["sundrawcmd"]), R(p, B["suncounter"]), 72), 1)
+
+    compute(g, "clear count", clear)
+    compute(g, "lights", lambda p: dispatch(p, kernels.sc_move_lights, (
+        W(p, B["lpos"]), RW(p, B["centers"]), RW(p, B["params"]), R(p, B["home"]), R(p, B["lcol"]), R(p, B["P"]),
+        ninst - nlight), nlight))
+    compute(g, "cull", lambda p: dispatch(p, kernels.sc_cull, (
+        W(p, B["visible"]), RW(p, B["counter"]), R(p, B["centers"]), R(p, B["P"]), 0), ninst))
+    compute(g, "sun cull", lambda p: dispatch(p, kernels.sc_cull, (
+        W(p, B["sunvisible"]), RW(p, B["suncounter"]), R(p, B["centers"]), R(p, B["P"]), 32), ninst))
+    compute(g, "draw count", draw_count)
+    compute(g, "tiles", lambda p: dispatch(p, kernels.sc_tile_lights, (
+        W(p, tl), W(p, tc), R(p, B["dep"]), R(p, B["lpos"]), R(p, B["P"]), w, h, tile, nlight, pertile),
+        (ntx, nty)))
+    compute(g, "ssao", lambda p: dispatch(p, kernels.sc_ssao, (
+        W(p, aoraw), R(p, B["dep"]), R(p, B["nrm"]), R(p, B["P"]), w, h, s.nsample), (aow, aoh)))
+    compute(g, "ao blur", lambda p: dispatch(p, kernels.sc_ao_blur, (W(p, aomap), R(p, aoraw), R(p, B["P"])),
+                                             (aow, aoh)))
+    compute(g, "light", lambda p: dispatch(p, kernels.sc_shade, (
+        W(p, hdr), R(p, B["alb"]), R(p, B["mat"]), R(p, B["nrm"]), R(p, B["dep"]), R(p, B["lpos"]),
+        R(p, B["lcol"]), R(p, tl), R(p, tc), R(p, B["smap"]), R(p, aomap), R(p, B["P"]), tile, pertile,
+        s.smap.shape[0]), (w, h)))
+    compute(g, "bright", lambda p: dispatch(p, kernels.sc_bright, (W(p, bloom_a), R(p, hdr), R(p, B["P"]), w, h,
+                                                                   shift), (bw, bh)))
+    compute(g, "blur x", lambda p: dispatch(p, kernels.sc_blur, (W(p, bloom_b), R(p, bloom_a), 1, 0), (bw, bh)))
+    compute(g, "blur y", lambda p: dispatch(p, kernels.sc_blur, (W(p, bloom_a), R(p, bloom_b), 0, 1), (bw, bh)))
+    compute(g, "composite", lambda p: dispatch(p, kernels.sc_composite, (
+        W(p, B["out"]), R(p, hdr), R(p, bloom_a), R(p, B["P"]), bw, bh, shift), (w, h)))
+    return ShowcaseWorkload(scene, B, g, Plan(g, **plan_kw))

@@ -230,3 +230,21 @@ def test_bright_blur_composite(dev, scene, chain):
     assert np.array_equal(_host(out), chain["out"])
     with pytest.raises(M.MantleError, match="overlap"):
         M.launch(M.kernels.sc_blur, (b, b, 1, 0), (bw, bh), stream=st)
+
+
+@pytest.mark.gpu
+def test_showcase_graph(dev, scene, chain):
+    """The thirteen compute passes as one planned graph, replayed twice (the
+    lights' instance slots are rewritten in place each frame)."""
+    from mantle_cuda.workloads import build_showcase
+    w = build_showcase(dev, scene)
+    M.run(w.plan)
+    M.run(w.plan)
+    dev.synchronize()
+    out = w.bufs["out"].array()
+    _close(out.reshape(H, W, 4), chain["out"], rel=1e-5, absol=1e-6, frac=0.995)
+    assert w.bufs["counter"].array()[0] == O.sc_cull(chain["centers"], scene.P[0:16]).sum()
+    # transients: tile lists, occlusion (raw and blurred), HDR and two bloom
+    # images; the planner lets images whose lifetimes do not overlap share bytes
+    hdr_bytes = 16 * W * H
+    assert 0 < M.peakbytes(w.plan) < 1.6 * hdr_bytes
