@@ -631,6 +631,77 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     }
 
 
+def bench_showcase(args, ws, rank, local, peaks, peak_kind):
+    """The showcase's thirteen compute passes at the reference's size (1600 x
+    900, 44 lights, 5044 instances, a 2048^2 shadow map) as one replayed graph
+    per frame; each rank renders its own frame (weak scaling, no collective)."""
+    import mantle_cuda as M
+    from mantle_cuda.workloads import build_showcase, showcase_scene
+    from oracle import oracle as O
+
+    dev = M.Device(local)
+    sc = showcase_scene(1600, 900, seed=9 + rank, smap_res=2048)
+    w = build_showcase(dev, sc)
+    for _ in range(args.warmup):
+        M.run(w.plan)
+    dev.synchronize()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = device_time_ms(dev.stream, lambda: M.run(w.plan), args.steps)
+    ms_step = max_over_ranks(ws, ms / args.steps)
+    npx = sc.w * sc.h
+    # compulsory image bytes of a frame: depth for the tiles; depth + normal at
+    # the occlusion samples' centres and its half-resolution output, read and
+    # blurred; the four g-buffer channels, the occlusion map and the HDR write
+    # of lighting; the four bright taps per bloom pixel and the bloom chain;
+    # HDR + bloom read and the output write of the composite
+    bw, bh = -(-sc.w // sc.shift), -(-sc.h // sc.shift)
+    aon = -(-sc.w // 2) * -(-sc.h // 2)
+    algo = (4 * npx + 8 * aon + 8 * aon + 12 * aon + (16 + 4 + 4 * aon / npx) * npx + 16 * npx
+            + 4 * 16 * bw * bh + 16 * bw * bh + 4 * 32 * bw * bh + 32 * npx)
+    achieved = algo / (ms_step * 1e-3) / 1e9
+    # end to end: the frame's scene constants in, the composited image out
+    out_host = np.empty(4 * npx, np.float32)
+    t = e2e_time(dev, ws, max(3, min(args.steps, 20)), [(w.bufs["P"], pinned_like(sc.P))], lambda: M.run(w.plan),
+                 [(w.bufs["out"], out_host)])
+    e2e = {"value": round(ws / t["seconds"], 1), "unit": "frames/s", "h2d_bytes_per_step": t["h2d_bytes_per_step"],
+           "d2h_bytes_per_step": t["d2h_bytes_per_step"], "ms_per_step": round(t["seconds"] * 1e3, 3)}
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        threads = O.max_threads()
+        t0, frames = time.perf_counter(), 0
+        while time.perf_counter() - t0 < args.cpu_seconds or frames == 0:
+            lpos, _, _ = O.sc_move_lights(sc.centers, sc.params, sc.home, sc.lcol, sc.P, sc.first)
+            O.sc_cull(sc.centers, sc.P[0:16])
+            O.sc_cull(sc.centers, sc.P[32:48])
+            tl, tc = O.sc_tile_lights(sc.dep, lpos, sc.P, sc.tile, sc.pertile)
+            ao = O.sc_ao_blur(O.sc_ssao(sc.dep, sc.nrm, sc.P, sc.nsample), sc.P)
+            hdr = O.sc_shade(sc.alb, sc.mat, sc.nrm, sc.dep, lpos, sc.lcol, tl, tc, sc.smap, ao, sc.P, sc.tile,
+                             sc.pertile)
+            bloom = O.sc_blur(O.sc_blur(O.sc_bright(hdr, sc.P, sc.shift), 1, 0), 0, 1)
+            O.sc_composite(hdr, bloom, sc.P, sc.shift)
+            frames += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(frames / dt, 3), "unit": "frames/s", "cores": threads, "kind": "port",
+               "sample": f"{frames} frames of the thirteen passes through the oracle (shading and occlusion on "
+                         f"OpenMP, the rest one thread) in {dt:.1f} s"}
+    return {
+        "metric": BASELINE_METRIC, "value": round(ws * 1e3 / ms_step, 1), "unit": "frames/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded analytic scene (floor + spheres) ray-cast into the g-buffer and shadow map",
+        "config": {"workload": "showcase compute passes (bench/showcase.jl): lights, cull x2, draw count, tiles, "
+                               "SSAO, AO blur, GGX lighting, bright, blur x/y, composite",
+                   "resolution": [sc.w, sc.h], "lights": sc.home.shape[0], "instances": sc.centers.shape[0],
+                   "shadow_map": sc.smap.shape[0], "parallelism": f"{ws} independent frames",
+                   "l2": "a frame's images (~70 MB) fit the L2; frames replay back to back (no flush)"},
+        "roofline": {"bound": "hbm", "kernel": "the whole frame (13 passes)", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": None, "algorithmic_bytes": int(algo), "peak_kind": f"{peak_kind} (burst copy)"},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
+    }
+
+
 def profile_case(args, local):
     """Only the dominant kernel of a workload, three launches, for an ncu capture
     (`-k regex:<kernel> -c 3`); prints nothing but "ok"."""
@@ -715,7 +786,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm", "cnn"], default="scatter")
+    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm", "cnn", "showcase"], default="scatter")
     ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -747,6 +818,8 @@ def main():
             line = bench_gemm(args, ws, rank, local, peaks, peak_kind)
         elif args.workload == "cnn":
             line = bench_cnn(args, ws, rank, local, peaks, peak_kind)
+        elif args.workload == "showcase":
+            line = bench_showcase(args, ws, rank, local, peaks, peak_kind)
         else:
             line = bench_scatter(args, ws, rank, local, peaks, peak_kind)
         if rank == 0:

@@ -123,7 +123,8 @@ __device__ v3 ggx(v3 n, v3 v, v3 l, v3 albedo, float rough, float metal) {
   const float k = a * 0.5f;
   const float G = (ndl / (ndl * (1.f - k) + k)) * (ndv / (ndv * (1.f - k) + k));
   const v3 f0 = mk(0.04f, 0.04f, 0.04f) + (albedo - mk(0.04f, 0.04f, 0.04f)) * metal;
-  const float fr = powf(1.f - vdh, 5.f);
+  const float om = 1.f - vdh;
+  const float fr = om * om * om * om * om;  // (1 - v.h)^5 as four products, left to right
   const v3 F = f0 + (mk(1.f, 1.f, 1.f) - f0) * fr;
   const v3 spec = F * (D * G / fmaxf(1e-4f, 4.f * ndl * ndv));
   const v3 kd = (mk(1.f, 1.f, 1.f) - F) * (1.f - metal);
@@ -337,7 +338,8 @@ __global__ void __launch_bounds__(256) sc_shade_kernel(
   const v3 world = unproject(P + SC_INVVP, (float)px + 0.5f, (float)py + 0.5f, fminf(d, 0.999999f), w, h);
   const v3 eyep = mk(P[SC_EYE], P[SC_EYE + 1], P[SC_EYE + 2]);
   const v3 ray = unit(world - eyep);
-  v3 out = sky(ray, sundir, sunrgb);
+  const v3 skyc = sky(ray, sundir, sunrgb);  // the background, and the fog's colour below
+  v3 out = skyc;
   if (d < 1.f) {
     const uint32_t a = alb[i], m = mat[i];
     const v3 albedo = mk(unpack8(a, 0), unpack8(a, 8), unpack8(a, 16));
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(256) sc_shade_kernel(
     const v3 de = world - eyep;
     const float dist = sqrtf(de.x * de.x + de.y * de.y + de.z * de.z);
     const float f = 1.f - expf(-dist * P[SC_FOG]);
-    out = acc + (sky(ray, sundir, sunrgb) - acc) * f;
+    out = acc + (skyc - acc) * f;
   }
   hdr[i] = make_float4(out.x, out.y, out.z, 1.f);
 }

@@ -520,23 +520,33 @@ def _colmajor(m):
 
 def _raycast(origin, dirs, spheres):
     """Nearest hit of rays (n, 3) against the plane y = 0 and spheres (m, 4):
-    (t, index) with index -1 for the floor, -2 for a miss."""
-    t = np.full(dirs.shape[0], np.inf)
-    idx = np.full(dirs.shape[0], -2, np.int64)
-    with np.errstate(divide="ignore", invalid="ignore"):
-        tf = -origin[..., 1] / dirs[:, 1]
-    hit = (dirs[:, 1] < 0) & (tf > 0)
-    t[hit], idx[hit] = tf[hit], -1
-    for k, (cx, cy, cz, rad) in enumerate(spheres):
-        oc = origin - np.array([cx, cy, cz])
-        b = (oc * dirs).sum(-1)
-        c = (oc * oc).sum(-1) - rad * rad
-        disc = b * b - c
-        ok = disc > 0
-        tk = np.where(ok, -b - np.sqrt(np.where(ok, disc, 0.0)), np.inf)
-        better = ok & (tk > 1e-3) & (tk < t)
-        t[better], idx[better] = tk[better], k
-    return t, idx
+    (t, index) with index -1 for the floor, -2 for a miss. float64, in chunks,
+    on the GPU when there is one."""
+    import torch
+    dv = "cuda" if torch.cuda.is_available() else "cpu"
+    sp = torch.as_tensor(np.asarray(spheres, np.float64), device=dv)
+    o_all = torch.as_tensor(np.broadcast_to(origin, dirs.shape).copy(), device=dv)
+    d_all = torch.as_tensor(dirs, device=dv)
+    t_out = np.empty(dirs.shape[0])
+    i_out = np.empty(dirs.shape[0], np.int64)
+    for a in range(0, dirs.shape[0], 1 << 18):
+        o, d = o_all[a:a + (1 << 18)], d_all[a:a + (1 << 18)]
+        tf = -o[:, 1] / d[:, 1]
+        floor = (d[:, 1] < 0) & (tf > 0)
+        t = torch.where(floor, tf, torch.full_like(tf, float("inf")))
+        idx = torch.where(floor, torch.full_like(tf, -1, dtype=torch.int64), torch.full_like(tf, -2, dtype=torch.int64))
+        oc = o[:, None, :] - sp[None, :, :3]                       # (n, m, 3)
+        b = (oc * d[:, None, :]).sum(-1)
+        disc = b * b - ((oc * oc).sum(-1) - sp[None, :, 3] ** 2)
+        ts = torch.where(disc > 0, -b - torch.sqrt(disc.clamp(min=0)), torch.full_like(b, float("inf")))
+        ts = torch.where(ts > 1e-3, ts, torch.full_like(ts, float("inf")))
+        tmin, k = ts.min(1)
+        better = tmin < t
+        t = torch.where(better, tmin, t)
+        idx = torch.where(better, k, idx)
+        t_out[a:a + len(d)] = t.cpu().numpy()
+        i_out[a:a + len(d)] = idx.cpu().numpy()
+    return t_out, i_out
 
 
 @dataclass

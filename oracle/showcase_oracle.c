@@ -82,7 +82,8 @@ static V3 ggx(V3 n, V3 v, V3 l, V3 albedo, float rough, float metal) {
   const float k = a * 0.5f;
   const float G = (ndl / (ndl * (1.f - k) + k)) * (ndv / (ndv * (1.f - k) + k));
   const V3 f0 = add(V(0.04f, 0.04f, 0.04f), scl(sub(albedo, V(0.04f, 0.04f, 0.04f)), metal));
-  const float fr = powf(1.f - vdh, 5.f);
+  const float om = 1.f - vdh;
+  const float fr = om * om * om * om * om;  // (1 - v.h)^5 as four products, left to right
   const V3 F = add(f0, scl(sub(V(1.f, 1.f, 1.f), f0), fr));
   const V3 spec = scl(F, D * G / fmaxf(1e-4f, 4.f * ndl * ndv));
   const V3 kd = scl(sub(V(1.f, 1.f, 1.f), F), 1.f - metal);
@@ -199,7 +200,8 @@ void oracle_sc_shade(float* hdr, const uint32_t* alb, const uint32_t* mat, const
       const float d = dep[i];
       const V3 world = unproject(P + SC_INVVP, (float)px + 0.5f, (float)py + 0.5f, fminf(d, 0.999999f), w, h);
       const V3 ray = nrmz(sub(world, eyep));
-      V3 out = sky(ray, sundir, sunrgb);
+      const V3 skyc = sky(ray, sundir, sunrgb);
+      V3 out = skyc;
       if (d < 1.f) {
         const uint32_t a = alb[i], m = mat[i];
         const V3 albedo = V(unpack8(a, 0), unpack8(a, 8), unpack8(a, 16));
@@ -243,7 +245,7 @@ void oracle_sc_shade(float* hdr, const uint32_t* alb, const uint32_t* mat, const
         const V3 de = sub(world, eyep);
         const float dist = sqrtf(de.x * de.x + de.y * de.y + de.z * de.z);
         const float f = 1.f - expf(-dist * P[SC_FOG]);
-        out = add(acc, scl(sub(sky(ray, sundir, sunrgb), acc), f));
+        out = add(acc, scl(sub(skyc, acc), f));
       }
       float* o = hdr + 4 * i;
       o[0] = out.x, o[1] = out.y, o[2] = out.z, o[3] = 1.f;
