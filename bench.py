@@ -727,7 +727,12 @@ def profile_case(args, local):
             M.run(w.plan)
     elif args.profile == "cnn":
         from mantle_cuda.workloads import build_cnn
-        w = build_cnn(dev, batch=64)
+        w = build_cnn(dev, batch=args.profile_batch)
+        for _ in range(3):
+            M.run(w.plan)
+    elif args.profile == "showcase":
+        from mantle_cuda.workloads import build_showcase, showcase_scene
+        w = build_showcase(dev, showcase_scene(1600, 900, seed=9, smap_res=2048))
         for _ in range(3):
             M.run(w.plan)
     elif args.profile == "fft":
@@ -790,7 +795,8 @@ def main():
     ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--profile", choices=["scatter", "fft", "gemm", "cnn"], default=None,
+    ap.add_argument("--profile-batch", type=int, default=64, help="--profile cnn: the batch (default 64)")
+    ap.add_argument("--profile", choices=["scatter", "fft", "gemm", "cnn", "showcase"], default=None,
                     help="launch only the workload's dominant kernel three times (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
