@@ -248,6 +248,9 @@ __global__ void __launch_bounds__(256) sc_tile_lights_kernel(uint32_t* __restric
   const int ti = ty * ntx + tx;
   const int x0 = tx * tile, y0 = ty * tile;
   const int x1 = min(x0 + tile, w), y1 = min(y0 + tile, h);
+  // this thread's light, loaded early so its latency overlaps the depth pass
+  float4 mylight = make_float4(0.f, 0.f, 0.f, -1.f);
+  if (threadIdx.x < nlight) mylight = lpos[threadIdx.x];
   float dmin = 1.f, dmax = 0.f;
   for (int e = threadIdx.x; e < tile * tile; e += blockDim.x) {
     const int px = x0 + e % tile, py = y0 + e / tile;
@@ -269,23 +272,31 @@ __global__ void __launch_bounds__(256) sc_tile_lights_kernel(uint32_t* __restric
     smax[warp] = dmax;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int k = 1; k < nwarp; ++k) {
+  if (warp == 0) {
+    // every lane of warp 0 folds the per-warp ranges; lanes 0-7 then unproject
+    // one corner each and the box is their min / max (fminf / fmaxf are exact,
+    // so the order of folding does not matter)
+    dmin = 1.f;
+    dmax = 0.f;
+    for (int k = 0; k < nwarp; ++k) {
       dmin = fminf(dmin, smin[k]);
       dmax = fmaxf(dmax, smax[k]);
     }
-    smin[0] = dmin;
-    smax[0] = dmax;
-    if (dmax > 0.f) {
-      const float* inv = P + SC_INVVP;
-      v3 lo = mk(1e30f, 1e30f, 1e30f), hi = mk(-1e30f, -1e30f, -1e30f);
-      for (int c = 0; c < 8; ++c) {
-        const v3 p = unproject(inv, (float)((c & 1) == 0 ? x0 : x1), (float)((c & 2) == 0 ? y0 : y1),
-                               (c & 4) == 0 ? dmin : dmax, w, h);
-        lo = mk(fminf(lo.x, p.x), fminf(lo.y, p.y), fminf(lo.z, p.z));
-        hi = mk(fmaxf(hi.x, p.x), fmaxf(hi.y, p.y), fmaxf(hi.z, p.z));
+    const int c = lane & 7;
+    const v3 p = unproject(P + SC_INVVP, (float)((c & 1) == 0 ? x0 : x1), (float)((c & 2) == 0 ? y0 : y1),
+                           (c & 4) == 0 ? dmin : dmax, w, h);
+    float lo[3] = {p.x, p.y, p.z}, hi[3] = {p.x, p.y, p.z};
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        lo[j] = fminf(lo[j], __shfl_xor_sync(0xffffffffu, lo[j], o));
+        hi[j] = fmaxf(hi[j], __shfl_xor_sync(0xffffffffu, hi[j], o));
       }
-      box[0] = lo.x, box[1] = lo.y, box[2] = lo.z, box[3] = hi.x, box[4] = hi.y, box[5] = hi.z;
+    __syncwarp();
+    if (lane == 0) {
+      smin[0] = dmin;
+      smax[0] = dmax;
+      box[0] = lo[0], box[1] = lo[1], box[2] = lo[2], box[3] = hi[0], box[4] = hi[1], box[5] = hi[2];
     }
   }
   __syncthreads();
@@ -298,7 +309,7 @@ __global__ void __launch_bounds__(256) sc_tile_lights_kernel(uint32_t* __restric
     const int l = l0 + threadIdx.x;
     bool hit = false;
     if (l < nlight) {
-      const float4 lp = lpos[l];
+      const float4 lp = l0 == 0 ? mylight : lpos[l];
       const float dx = fmaxf(0.f, fmaxf(box[0] - lp.x, lp.x - box[3]));
       const float dy = fmaxf(0.f, fmaxf(box[1] - lp.y, lp.y - box[4]));
       const float dz = fmaxf(0.f, fmaxf(box[2] - lp.z, lp.z - box[5]));
