@@ -465,7 +465,10 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
 template <int BN>
 struct HaloCfg {
   static constexpr uint32_t kBBlock = 64 * BN * 2;  // one K block of weights
-  static constexpr uint32_t kTmemCols = 2 * BN;
+  // two issuing threads (warps 1 and 6) take alternate tiles, each with two
+  // accumulators: four in TMEM
+  static constexpr uint32_t kTmemCols = 4 * BN;
+  static_assert(4 * BN <= 512, "four accumulators must fit the 512 TMEM columns");
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false, true);
 };
 
@@ -474,7 +477,7 @@ __host__ __device__ inline uint32_t halo_smem_bytes(const ConvShape& sh, uint32_
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                      __nv_bfloat16* __restrict__ out, const ConvShape sh, int relu) {
   using Cfg = HaloCfg<BN>;
@@ -486,10 +489,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(astage + (size_t)S * sh.halo_stage_bytes);
   uint64_t* full = bars;           // [S]
   uint64_t* empty = bars + 4;      // [S], S <= 4
-  uint64_t* tfull = bars + 8;      // [2]
-  uint64_t* tempty = bars + 10;    // [2]
-  uint64_t* bfull = bars + 12;     // resident weights landed
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* tfull = bars + 8;      // [4] accumulator ready
+  uint64_t* tempty = bars + 12;    // [4] accumulator drained
+  uint64_t* bfull = bars + 16;     // resident weights landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(smem_u32(&full[i]), 1);
       mbar_init(smem_u32(&empty[i]), 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 4; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 4);
     }
@@ -551,26 +554,30 @@ __global__ void __launch_bounds__(192, 1)
       }
     p_done:;
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 6) {
+    // Issuer j takes tiles i = j, j + 2, ... (the CTA's i-th tile is first +
+    // i * step): one thread issuing N = 64 MMAs leaves the tensor core idle
+    // between them, two keep it fed. Tile i's channel block cb sits in stage
+    // (i * cblocks + cb) mod S of the producer's ring; its accumulator is i mod 4.
+    const int j = warp == 1 ? 0 : 1;
     if (lane == 0 && wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts)) {
       tc_fence_after();
-      int s = 0;
-      uint32_t ph = 0;
-      int i = 0;
       // descriptors as offsets in 16-byte units from stage 0 / weight block 0
       // (two adds per MMA; see conv_bf16_kernel)
       const uint64_t adesc = smem_desc(smem_u32(astage), 16, 1024);
       const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
       const uint32_t bstep = (uint32_t)cblocks * (Cfg::kBBlock >> 4);  // next tap's weights
       const uint32_t wsrow = (uint32_t)sh.ws * 8;                         // one stored row of 128 B rows
-      for (int64_t t = first; t < mtiles; t += step, ++i) {
-        const int a = i & 1;
-        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) break;
+      for (int i = j; first + (int64_t)i * step < mtiles; i += 2) {
+        const int a = i & 3;
+        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 2) & 1) ^ 1, abort, &g_conv_timeouts)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * BN);
         bool ok = true;
         for (int cb = 0; cb < cblocks; ++cb) {
-          if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) {
+          const int g = i * cblocks + cb;
+          const int s = g % S;
+          if (!wait_phase(smem_u32(&full[s]), (uint32_t)((g / S) & 1), abort, &g_conv_timeouts)) {
             ok = false;
             break;
           }
@@ -591,10 +598,6 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
           tc_commit(smem_u32(&empty[s]));
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
-          }
         }
         if (!ok) break;
         tc_commit(smem_u32(&tfull[a]));
@@ -605,8 +608,8 @@ __global__ void __launch_bounds__(192, 1)
     int i = 0;
     const int hws = sh.h * sh.ws;
     for (int64_t t = first; t < mtiles; t += step, ++i) {
-      const int a = i & 1;
-      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) break;
+      const int a = i & 3;
+      if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
       const int img = (int)(t / sh.halo_tiles);
       const int pos = (int)(t - (int64_t)img * sh.halo_tiles) * 128 + q * 32 + lane;  // stored position
@@ -1409,7 +1412,7 @@ static cudaError_t launch_halo(const CUtensorMap& tw, const CUtensorMap& ta, voi
   // whole column-block groups: CTA b serves column block b % nblk
   int grid = (int)std::min<int64_t>(tiles, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_halo_kernel<BN><<<grid, 192, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  conv_halo_kernel<BN><<<grid, 224, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
   return cudaGetLastError();
 }
 
@@ -1457,7 +1460,7 @@ static int halo_plan(ConvShape& sh) {
   if ((double)sh.h * sh.w < 0.85 * tiles * 128.0) return 0;
   const int stage = (rows * 128 + 1023) & ~1023;
   const int kblocks = sh.taps * sh.cin / 64;
-  for (int bn = 256; bn >= 64; bn /= 2) {
+  for (int bn = 128; bn >= 64; bn /= 2) {  // four accumulators of 4 * bn <= 512 TMEM columns
     if (sh.cout % bn) continue;
     const int64_t avail = 232448 - 1024 - 256 - (int64_t)kblocks * 64 * bn * 2;
     const int stages = (int)std::min<int64_t>(4, avail / stage);
@@ -1621,9 +1624,8 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
     if (mtl_status st = make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
                                       (uint32_t)hs.halo_rows))
       return st;
-    cudaError_t e = bn == 256   ? launch_halo<256>(tw, ta, out, hs, relu, la.sm_count, s)
-                    : bn == 128 ? launch_halo<128>(tw, ta, out, hs, relu, la.sm_count, s)
-                                : launch_halo<64>(tw, ta, out, hs, relu, la.sm_count, s);
+    cudaError_t e = bn == 128 ? launch_halo<128>(tw, ta, out, hs, relu, la.sm_count, s)
+                              : launch_halo<64>(tw, ta, out, hs, relu, la.sm_count, s);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }
