@@ -737,8 +737,13 @@ __host__ __device__ inline uint32_t rows_raw_bytes(const ConvShape& sh, int src_
   return ((uint32_t)hrows * sh.w * 2 * src_c + 1023) & ~1023u;
 }
 
+// Two MMA-issuing warps (1 and kRowsIssuer2) take alternate output rows of
+// each stage, each with two of the four TMEM accumulators.
+template <int SRC_C>
+constexpr int rows_threads() { return SRC_C ? 256 : 224; }
+
 template <int CIN, int KT, int SRC_C>  // KT: the filter size when known at compile time (its interior rows fully unrolled), else 0
-__global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
+__global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
     conv_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmO,
                      const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, const ConvShape sh,
                      int relu) {
@@ -755,13 +760,13 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
   const uint32_t raw_bytes = SRC_C ? rows_raw_bytes(sh, SRC_C) : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + 2 * raw_bytes);
   uint64_t* full = bars;         // [S]
-  uint64_t* empty = bars + 4;    // [S], S <= 4
-  uint64_t* tfull = bars + 8;    // [2]
-  uint64_t* tempty = bars + 10;  // [2]
-  uint64_t* bfull = bars + 12;
-  uint64_t* raw_full = bars + 13;   // [2]
-  uint64_t* raw_empty = bars + 15;  // [2]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* empty = bars + 4;    // [S], S <= 4; both issuers release a stage
+  uint64_t* tfull = bars + 8;    // [4]
+  uint64_t* tempty = bars + 12;  // [4]
+  uint64_t* bfull = bars + 16;
+  uint64_t* raw_full = bars + 17;   // [2]
+  uint64_t* raw_empty = bars + 19;  // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -775,9 +780,9 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(smem_u32(&full[i]), 1);
-      mbar_init(smem_u32(&empty[i]), 1);
+      mbar_init(smem_u32(&empty[i]), 2);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 4; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 4);
     }
@@ -792,7 +797,7 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                 "r"(2 * BN)
+                 "r"(4 * BN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -841,12 +846,15 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == (SRC_C ? 7 : 6)) {
+    // issuer j: rows t = j, j + 2, ... of every stage; its c-th tile uses
+    // accumulator j + 2 * (c & 1)
+    const int j = warp == 1 ? 0 : 1;
     if (lane == 0 && wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts)) {
       tc_fence_after();
       int s = 0;
       uint32_t ph = 0;
-      int i = 0;
+      int c = 0;
       const uint64_t adesc = smem_desc_noswizzle(smem_u32(astage), 16, 128);
       const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
       bool ok = true;
@@ -856,9 +864,10 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
         if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) break;
         tc_fence_after();
         const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
-        for (int t = 0; t < kRowsG && oh0 + t < sh.ho; ++t, ++i) {
-          const int a = i & 1;
-          if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) {
+        bool issued = false;
+        for (int t = j; t < kRowsG && oh0 + t < sh.ho; t += 2, ++c) {
+          const int a = j + 2 * (c & 1);
+          if (!wait_phase(smem_u32(&tempty[a]), ((c >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) {
             ok = false;
             break;
           }
@@ -891,8 +900,15 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
             }
           }
           tc_commit(smem_u32(&tfull[a]));
+          issued = true;
         }
-        tc_commit(smem_u32(&empty[s]));
+        if (!ok) break;
+        // both issuers release the stage; one with no row here (a short last
+        // stage) has nothing in flight on it
+        if (issued)
+          tc_commit(smem_u32(&empty[s]));
+        else
+          mbar_arrive(smem_u32(&empty[s]));
         if (++s == S) {
           s = 0;
           ph ^= 1;
@@ -960,13 +976,15 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
     const int q = warp & 3;
     unsigned char* my_stage = staging + (warp - 2) * 8192;
     int i = 0;
+    int cnt[2] = {0, 0};  // tiles seen per issuer
     bool ok = true;
     for (int64_t u = first; u < units && ok; u += step) {
       const int img = (int)(u / groups);
       const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
       for (int t = 0; t < kRowsG && oh0 + t < sh.ho; ++t, ++i) {
-        const int a = i & 1;
-        if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) {
+        const int j = t & 1, c = cnt[j]++;
+        const int a = j + 2 * (c & 1);
+        if (!wait_phase(smem_u32(&tfull[a]), (c >> 1) & 1, abort, &g_conv_timeouts)) {
           ok = false;
           break;
         }
@@ -996,7 +1014,7 @@ __global__ void __launch_bounds__(SRC_C ? 224 : 192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * BN) : "memory");
 }
 
 // ── NCHW -> NHWC, channels zero-padded to cpad, wpad zero columns each side ──
@@ -1397,7 +1415,7 @@ static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, con
   const int64_t units = (int64_t)sh.n * ((sh.ho + kRowsG - 1) / kRowsG) * sh.nblk;
   int grid = (int)std::min<int64_t>(units, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_rows_kernel<CIN, KT, SRC_C><<<grid, SRC_C ? 224 : 192, smem, s>>>(
+  conv_rows_kernel<CIN, KT, SRC_C><<<grid, rows_threads<SRC_C>(), smem, s>>>(
       tw, to, reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
   return cudaGetLastError();
 }
