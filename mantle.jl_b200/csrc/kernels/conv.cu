@@ -48,6 +48,11 @@ struct ConvShape {
   int tw, th, tiles_x, tiles_y;
   int wpad, ws;   // zero columns stored on each side of every input row; stored width w + 2*wpad
   int owp, wso;   // the same for the output rows (written as zeros); stored output width wo + 2*owp
+  // Phase planes: a tensor stored as four planes [n][row parity][column
+  // parity][H/2][W/2 + 1][C], column 0 of every plane row zero (a stride-2
+  // layer reads each filter tap as a shifted run of one plane). in_phase: the
+  // input is stored so (pq = W/2 + 1); out_phase: write the output so.
+  int in_phase, out_phase, pq;
   // A_HALO: halo rows per channel block, tiles per image, A stages and their
   // bytes, column blocks (Cout / BN)
   int halo_rows, halo_tiles, halo_stages, halo_stage_bytes, nblk;
@@ -476,7 +481,17 @@ __host__ __device__ inline uint32_t halo_smem_bytes(const ConvShape& sh, uint32_
   return 1024 + (uint32_t)sh.kblocks * bblock + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 256;
 }
 
-template <int BN>
+// Taps of phase plane p = 2 * row parity + column parity for a 3x3 stride-2
+// filter with padding 1: row parity 0 holds filter row 1, parity 1 rows 0 and
+// 2 (row 0 one plane row up); columns likewise (column 0 one plane column
+// left, into the zero column 0).
+__host__ __device__ constexpr int ph_ntaps(int p) { return ((p >> 1) ? 2 : 1) * ((p & 1) ? 2 : 1); }
+__host__ __device__ constexpr int ph_tap_r(int p, int t) {
+  return (p >> 1) ? ((t / ((p & 1) ? 2 : 1)) ? 2 : 0) : 1;
+}
+__host__ __device__ constexpr int ph_tap_c(int p, int t) { return (p & 1) ? ((t % 2) ? 2 : 0) : 1; }
+
+template <int BN, bool PH>
 __global__ void __launch_bounds__(224, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                      __nv_bfloat16* __restrict__ out, const ConvShape sh, int relu) {
@@ -487,20 +502,27 @@ __global__ void __launch_bounds__(224, 1)
   unsigned char* astage = bres + (size_t)sh.kblocks * Cfg::kBBlock;
   const int S = sh.halo_stages;
   uint64_t* bars = reinterpret_cast<uint64_t*>(astage + (size_t)S * sh.halo_stage_bytes);
-  uint64_t* full = bars;           // [S]
-  uint64_t* empty = bars + 4;      // [S], S <= 4
-  uint64_t* tfull = bars + 8;      // [4] accumulator ready
-  uint64_t* tempty = bars + 12;    // [4] accumulator drained
-  uint64_t* bfull = bars + 16;     // resident weights landed
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* full = bars;           // [S], S <= 8
+  uint64_t* empty = bars + 8;      // [S]
+  uint64_t* tfull = bars + 16;     // [4] accumulator ready
+  uint64_t* tempty = bars + 20;    // [4] accumulator drained
+  uint64_t* bfull = bars + 24;     // resident weights landed
+  uint64_t* idle = bars + 25;      // [2] an issuer's MMAs all done (drain before exit)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 27);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* prog = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2] loads each issuer has waited for
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int cblocks = sh.cin / 64;
   const int nb = blockIdx.x % sh.nblk, n0 = nb * BN;
   const int64_t first = blockIdx.x / sh.nblk, step = gridDim.x / sh.nblk;
   const int64_t mtiles = (int64_t)sh.n * sh.halo_tiles;
-  const int halo0 = sh.pad * sh.ws + sh.pad;
+  // positions per row of the tiled grid and the halo's lead: stored input rows
+  // (stride 1: the taps' shifts are -pad*ws - pad .. +pad*ws + pad), or phase
+  // planes (stride 2: shifts -pq - 1 .. 0)
+  const int pitch = PH ? sh.pq : sh.ws;
+  const int halo0 = PH ? sh.pq + 1 : sh.pad * sh.ws + sh.pad;
+  constexpr int kLoads = PH ? 4 : 1;  // stages per (tile, channel block)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -512,7 +534,10 @@ __global__ void __launch_bounds__(224, 1)
       mbar_init(smem_u32(&tempty[a]), 4);
     }
     mbar_init(smem_u32(bfull), 1);
+    mbar_init(smem_u32(&idle[0]), 1);
+    mbar_init(smem_u32(&idle[1]), 1);
     *abort = 0;
+    prog[0] = prog[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -538,28 +563,50 @@ __global__ void __launch_bounds__(224, 1)
                       smem_u32(bfull));
       int s = 0;
       uint32_t ph = 0;
+      int64_t loads = 0;
       for (int64_t t = first; t < mtiles; t += step) {
         const int img = (int)(t / sh.halo_tiles);
         const int q0 = (int)(t - (int64_t)img * sh.halo_tiles) * 128;
-        for (int cb = 0; cb < cblocks; ++cb) {
-          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto p_done;
-          const uint32_t fb = smem_u32(&full[s]);
-          mbar_expect_tx(fb, (uint32_t)sh.halo_rows * 128);
-          tma_load_3d(smem_u32(astage + (size_t)s * sh.halo_stage_bytes), &tmA, cb * 64, q0 - halo0, img, fb);
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
+        for (int cb = 0; cb < cblocks; ++cb)
+          for (int p = 0; p < kLoads; ++p) {
+            if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto p_done;
+            const uint32_t fb = smem_u32(&full[s]);
+            mbar_expect_tx(fb, (uint32_t)sh.halo_rows * 128);
+            tma_load_3d(smem_u32(astage + (size_t)s * sh.halo_stage_bytes), &tmA, cb * 64, q0 - halo0,
+                        PH ? img * 4 + p : img, fb);
+            ++loads;
+            if (++s == S) {
+              s = 0;
+              ph ^= 1;
+            }
           }
-        }
       }
-    p_done:;
+    p_done:
+      // no load may still be landing when the CTA leaves (an aborted run):
+      // wait for the last phase armed on each stage used
+      for (int u = 0; u < S && u < loads; ++u) {
+        const int64_t g = loads - 1 - u;  // the last load into stage g % S
+        drain_phase(smem_u32(&full[g % S]), (uint32_t)((g / S) & 1));
+      }
+      drain_phase(smem_u32(bfull), 0);
     }
   } else if (warp == 1 || warp == 6) {
     // Issuer j takes tiles i = j, j + 2, ... (the CTA's i-th tile is first +
     // i * step): one thread issuing N = 64 MMAs leaves the tensor core idle
-    // between them, two keep it fed. Tile i's channel block cb sits in stage
-    // (i * cblocks + cb) mod S of the producer's ring; its accumulator is i mod 4.
+    // between them, two keep it fed. The g-th load of the producer sits in
+    // stage g mod S; tile i's accumulator is i mod 4. Both issuers wait on the
+    // same stages, so before waiting for load g an issuer makes sure load g - S
+    // (the stage's previous phase) has been waited for: when that was the
+    // other issuer's, it checks the other's progress (a parity wait on a stage
+    // two phases behind would pass at once).
     const int j = warp == 1 ? 0 : 1;
+    const int per_tile = cblocks * kLoads;
+    // Load k of a tile (k < S) follows load k - S of the tile ceil((S - k) /
+    // per_tile) back: the other issuer's when that is odd (bit k of `cross`;
+    // loads k >= S follow one of the same tile).
+    uint32_t cross = 0;
+    for (int k = 0; k < S && k < per_tile; ++k)
+      if (((S - k + per_tile - 1) / per_tile) & 1) cross |= 1u << k;
     if (lane == 0 && wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts)) {
       tc_fence_after();
       // descriptors as offsets in 16-byte units from stage 0 / weight block 0
@@ -567,65 +614,126 @@ __global__ void __launch_bounds__(224, 1)
       const uint64_t adesc = smem_desc(smem_u32(astage), 16, 1024);
       const uint64_t bdesc = smem_desc(smem_u32(bres), 64 * 128, 1024);
       const uint32_t bstep = (uint32_t)cblocks * (Cfg::kBBlock >> 4);  // next tap's weights
-      const uint32_t wsrow = (uint32_t)sh.ws * 8;                         // one stored row of 128 B rows
+      const uint32_t prow = (uint32_t)pitch * 8;                          // one grid row of 128 B rows
       for (int i = j; first + (int64_t)i * step < mtiles; i += 2) {
         const int a = i & 3;
         if (!wait_phase(smem_u32(&tempty[a]), ((i >> 2) & 1) ^ 1, abort, &g_conv_timeouts)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * BN);
         bool ok = true;
-        for (int cb = 0; cb < cblocks; ++cb) {
-          const int g = i * cblocks + cb;
-          const int s = g % S;
-          if (!wait_phase(smem_u32(&full[s]), (uint32_t)((g / S) & 1), abort, &g_conv_timeouts)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
+        for (int cb = 0; cb < cblocks && ok; ++cb) {
           const uint64_t bc = bdesc + (uint64_t)((uint32_t)cb * (Cfg::kBBlock >> 4));  // weights of (tap 0, cb)
-          // 3x3: all 36 MMAs unrolled, tap (r, c) at r*ws + c rows of 128 B
 #pragma unroll
-          for (int tap = 0; tap < 9; ++tap) {
-            const uint64_t a = as + (uint64_t)((uint32_t)(tap / 3) * wsrow + (tap % 3) * 8);
-            const uint64_t b = bc + (uint64_t)((uint32_t)tap * bstep);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              if (tap == 0 && kk == 0)
-                tc_mma(d, a, b, Cfg::kIdesc, cb != 0);
-              else
-                tc_mma_acc(d, a + kk * 2, b + kk * 128, Cfg::kIdesc);
+          for (int p = 0; p < kLoads; ++p) {
+            const int k = cb * kLoads + p;
+            const int g = i * per_tile + k;
+            const int s = g % S;
+            if (k < S && ((cross >> k) & 1) && g >= S &&
+                !wait_progress(&prog[1 - j], g - S + 1, abort, &g_conv_timeouts)) {
+              ok = false;
+              break;
             }
+            if (!wait_phase(smem_u32(&full[s]), (uint32_t)((g / S) & 1), abort, &g_conv_timeouts)) {
+              ok = false;
+              break;
+            }
+            prog[j] = g + 1;
+            tc_fence_after();
+            const uint64_t as = adesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
+            if (!PH) {
+              // 3x3 stride 1: all 36 MMAs unrolled, tap (r, c) at r*ws + c rows of 128 B
+#pragma unroll
+              for (int tap = 0; tap < 9; ++tap) {
+                const uint64_t at = as + (uint64_t)((uint32_t)(tap / 3) * prow + (tap % 3) * 8);
+                const uint64_t b = bc + (uint64_t)((uint32_t)tap * bstep);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  if (tap == 0 && kk == 0)
+                    tc_mma(d, at, b, Cfg::kIdesc, cb != 0);
+                  else
+                    tc_mma_acc(d, at + kk * 2, b + kk * 128, Cfg::kIdesc);
+                }
+              }
+            } else {
+              // plane p's taps: filter row 0 starts one plane row earlier, filter
+              // column 0 one plane column earlier (rows pq + 1 of halo lead)
+#pragma unroll
+              for (int t = 0; t < ph_ntaps(p); ++t) {
+                const int r = ph_tap_r(p, t), c = ph_tap_c(p, t);
+                const uint32_t start = (uint32_t)(r == 0 ? 0 : pitch) + (c == 0 ? 0u : 1u);  // rows of 128 B
+                const uint64_t at = as + (uint64_t)(start * 8);
+                const uint64_t b = bc + (uint64_t)((uint32_t)(r * 3 + c) * bstep);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  if (p == 0 && t == 0 && kk == 0)
+                    tc_mma(d, at, b, Cfg::kIdesc, cb != 0);
+                  else
+                    tc_mma_acc(d, at + kk * 2, b + kk * 128, Cfg::kIdesc);
+                }
+              }
+            }
+            tc_commit(smem_u32(&empty[s]));
           }
-          tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
         tc_commit(smem_u32(&tfull[a]));
       }
     }
+    if (lane == 0) {
+      // every MMA this thread issued has finished before TMEM is freed
+      tc_commit(smem_u32(&idle[j]));
+      drain_phase(smem_u32(&idle[j]), 0);
+    }
+    __syncwarp();
   } else if (warp < 6) {
     const int q = warp & 3;
     int i = 0;
-    const int hws = sh.h * sh.ws;
+    const int grid_pos = sh.ho * pitch;  // positions of one image's grid
     for (int64_t t = first; t < mtiles; t += step, ++i) {
       const int a = i & 3;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
       const int img = (int)(t / sh.halo_tiles);
-      const int pos = (int)(t - (int64_t)img * sh.halo_tiles) * 128 + q * 32 + lane;  // stored position
-      const int y = pos / sh.ws, xs = pos - (pos / sh.ws) * sh.ws;
-      const bool inner = xs >= sh.pad && xs < sh.pad + sh.w;
-      // with stored output margins every position of the image is written
-      // (zeros at the margins); without, only the output pixels
-      const bool store = pos < hws && (sh.owp ? true : inner);
-      const int64_t dpos = sh.owp ? (int64_t)img * hws + pos : ((int64_t)img * sh.h + y) * sh.w + xs - sh.pad;
-      __nv_bfloat16* orow = out + dpos * sh.cout + n0;
+      const int pos = (int)(t - (int64_t)img * sh.halo_tiles) * 128 + q * 32 + lane;  // grid position
+      const int y = pos / pitch, xg = pos - (pos / pitch) * pitch;
+      // the output column of this grid position, and whether it is one
+      const int xo = PH ? xg - 1 : xg - sh.pad;
+      const bool inner = pos < grid_pos && xo >= 0 && xo < sh.wo;
+      // Where the row goes (-1: nowhere) and whether it is a margin (zeros):
+      //   phase-plane output: the output pixel's plane row, plus (for xo < 2)
+      //     the plane row's zero column 0;
+      //   stride 1 with margins == padding: every grid position of the image
+      //     (its stored position), zeros at the margins;
+      //   otherwise the output pixel with `owp` margins, the first and last
+      //     pixel of a row also zeroing that row's margins.
+      int64_t dpos = -1, zpos = -1, zpos2 = -1;
+      if (sh.out_phase) {
+        if (inner) {
+          const int hh = sh.ho / 2, wq = sh.wo / 2 + 1;
+          const int64_t prow_base = (((int64_t)img * 2 + (y & 1)) * 2 + (xo & 1)) * hh + (y >> 1);
+          dpos = prow_base * wq + (xo >> 1) + 1;
+          if (xo < 2) zpos = prow_base * wq;
+        }
+      } else if (!PH && sh.owp) {
+        if (pos < grid_pos) {
+          if (inner)
+            dpos = (int64_t)img * grid_pos + pos;
+          else
+            zpos = (int64_t)img * grid_pos + pos;
+        }
+      } else if (inner) {
+        const int64_t rowb = ((int64_t)img * sh.ho + y) * sh.wso;
+        dpos = rowb + sh.owp + xo;
+        if (sh.owp && xo == 0) zpos = rowb;              // one margin pixel: owp is 1 here
+        if (sh.owp && xo == sh.wo - 1) zpos2 = rowb + sh.owp + sh.wo;
+      }
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+      __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
-        if (store) {
+        if (dpos >= 0) {
           uint32_t pk[16];
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
@@ -634,14 +742,22 @@ __global__ void __launch_bounds__(224, 1)
               x0 = fmaxf(x0, 0.f);
               x1 = fmaxf(x1, 0.f);
             }
-            if (!inner) x0 = x1 = 0.f;
             __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
             pk[v] = *reinterpret_cast<uint32_t*>(&h);
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          uint4* dst = reinterpret_cast<uint4*>(drow + c * 32);
 #pragma unroll
           for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
+      }
+      // margin pixels: zeros over this column block
+#pragma unroll 1
+      for (int zz = 0; zz < 2; ++zz) {
+        const int64_t zp = zz ? zpos2 : zpos;
+        if (zp < 0) continue;
+        uint4* z = reinterpret_cast<uint4*>(out + zp * sh.cout + n0);
+#pragma unroll
+        for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -664,6 +780,10 @@ __global__ void __launch_bounds__(224, 1)
 // c1, c2); rows past the map's second extent are clipped by the TMA. The
 // caller alternates two staging buffers per warp and calls
 // epi_stage_acquire() before reusing one.
+// Phase-plane output (c1 < 0): the 32 rows are 32 consecutive pixels of one
+// output row; the even ones go to staging rows 0..15, the odd ones to 16..31,
+// and two TMA stores of box {64, 16, 1, 1} put them into the row's two
+// column-parity planes at (c0 + 64*chunk, pc1, pc2, pc3) and (.., pc3 + 1).
 __device__ __forceinline__ void epi_stage_acquire(int lane) {
   if (lane == 0) bulk_wait_read<1>();
   __syncwarp();
@@ -671,7 +791,9 @@ __device__ __forceinline__ void epi_stage_acquire(int lane) {
 
 template <int BN>
 __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned char* stage, const CUtensorMap* tmO,
-                                              int c0, int c1, int c2, int lane) {
+                                              int c0, int c1, int c2, int lane, int pc1 = 0, int pc2 = 0,
+                                              int pc3 = 0) {
+  const int srow = c1 >= 0 ? lane : (lane & 1) * 16 + (lane >> 1);
 #pragma unroll
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -687,19 +809,27 @@ __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned
       __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
       pk[v] = *reinterpret_cast<uint32_t*>(&h);
     }
-    unsigned char* row = stage + (c / 2) * 4096 + lane * 128;
+    unsigned char* row = stage + (c / 2) * 4096 + srow * 128;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const int piece = (c % 2) * 4 + v;
-      *reinterpret_cast<uint4*>(row + ((piece ^ (lane & 7)) << 4)) =
+      *reinterpret_cast<uint4*>(row + ((piece ^ (srow & 7)) << 4)) =
           make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
     }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
   if (lane == 0) {
+    if (c1 >= 0) {
 #pragma unroll
-    for (int c = 0; c < BN / 64; ++c) tma_store_3d(tmO, smem_u32(stage + c * 4096), c0 + c * 64, c1, c2);
+      for (int c = 0; c < BN / 64; ++c) tma_store_3d(tmO, smem_u32(stage + c * 4096), c0 + c * 64, c1, c2);
+    } else {
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          tma_store_4d(tmO, smem_u32(stage + c * 4096 + h * 2048), c0 + c * 64, pc1, pc2, pc3 + h);
+    }
     bulk_commit();
   }
 }
@@ -993,8 +1123,19 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
         epi_stage_acquire(lane);
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
         const int orow = img * sh.ho + oh0 + t;
-        epi_tma_store<BN>(tbase, relu, buf, &tmO, n0, q * 32, orow, lane);
         const int x = q * 32 + lane;
+        // phase-plane output: row y = oh0 + t's even and odd pixels go to
+        // planes (y & 1, 0) and (y & 1, 1), plane row y / 2, from column 1;
+        // x = 0 and x = 1 zero those plane rows' column 0
+        const int y = oh0 + t, pl = img * 4 + (y & 1) * 2;
+        epi_tma_store<BN>(tbase, relu, buf, &tmO, n0, sh.out_phase ? -1 : q * 32, orow, lane, 1 + q * 16, y >> 1,
+                          pl);
+        if (sh.out_phase && x < 2) {
+          uint4* z = reinterpret_cast<uint4*>(
+              out + (((int64_t)(pl + x) * (sh.ho / 2) + (y >> 1)) * (sh.wo / 2 + 1)) * sh.cout + n0);
+#pragma unroll
+          for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
+        }
         if (sh.owp && (x == 0 || x == sh.wo - 1)) {  // zero this output row's margin pixels
           __nv_bfloat16* p = out + ((int64_t)orow * sh.wso + sh.owp + x) * sh.cout + n0;
           for (int e = 1; e <= sh.owp; ++e) {
@@ -1247,6 +1388,9 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
 // columns the input buffer stores on each side of every row (its rows are
 // W + 2*in_wpad pixels long); the convolution's own padding is still `pad`.
 // out_wpad: the same for the output rows, which the kernel writes as zeros.
+// in_wpad = -1: the input is stored as phase planes (see ConvShape; a 3x3
+// stride-2 convolution with padding 1 over even H and W); out_wpad = -1: the
+// output is written so (even Ho and Wo).
 static ConvShape conv_shape(const LaunchArgs& la) {
   ConvShape sh{};
   sh.n = (int)la.nd[0];
@@ -1259,7 +1403,16 @@ static ConvShape conv_shape(const LaunchArgs& la) {
   sh.pad = la.a[9].i32;
   sh.wpad = la.a[11].i32;
   sh.owp = la.a[12].i32;
+  if (sh.wpad == -1) {
+    sh.in_phase = 1;
+    sh.wpad = 0;
+  }
+  if (sh.owp == -1) {
+    sh.out_phase = 1;
+    sh.owp = 0;
+  }
   sh.ws = sh.w + 2 * sh.wpad;
+  sh.pq = sh.w / 2 + 1;
   if (sh.stride > 0) {
     sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
     sh.wo = (sh.w + 2 * sh.pad - sh.k) / sh.stride + 1;
@@ -1282,13 +1435,21 @@ mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes) {
     return fail(MTL_ERR_ARGUMENT, "conv2d: sizes must be positive (paddings non-negative, out_wpad at most 64)");
   if (sh.ho <= 0 || sh.wo <= 0) return fail(MTL_ERR_ARGUMENT, "conv2d: the filter does not fit the padded input");
   const int am = conv_amode(sh);
+  if (sh.in_phase && am != A_HALO)
+    return fail(MTL_ERR_UNSUPPORTED,
+                "conv2d: a phase-plane input (in_wpad = -1) needs a 3x3 stride-2 convolution with padding 1, even H "
+                "and W, Cin a multiple of 64, W/2 + 1 <= 127, out_wpad in {-1, 0, 1}");
+  if (sh.out_phase && (am != A_HALO && am != A_ROWS || sh.ho % 2 || sh.wo % 2))
+    return fail(MTL_ERR_UNSUPPORTED,
+                "conv2d: a phase-plane output (out_wpad = -1) needs even Ho and Wo and the halo or raw-row path");
   if (sh.cin % 8 && !(sh.cin == 4 && (am == A_WINDOW4 || am == A_WINDOW4_RECT || am == A_ROWS)))
     return fail(MTL_ERR_UNSUPPORTED,
                 "conv2d: Cin must be a multiple of 8 (pad the channels), or 4 for an input stored with its padding "
                 "columns (at least 128 KiB), got %d",
                 sh.cin);
   if (sh.cout % 64) return fail(MTL_ERR_UNSUPPORTED, "conv2d: Cout must be a multiple of 64, got %d", sh.cout);
-  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2,
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * (sh.out_phase ? sh.wo + 2 : sh.wso) * sh.cout * 2,
+                            (uint64_t)sh.n * sh.h * (sh.in_phase ? sh.w + 2 : sh.ws) * sh.cin * 2,
                             (uint64_t)sh.taps * sh.cin * sh.cout * 2};
   const char* what[3] = {"the output", "the input", "the weights"};
   for (int i = 0; i < 3; ++i) {
@@ -1391,9 +1552,23 @@ static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, con
 
 // The output as {Cout, Wo, N*Ho} (pixel stride Cout, row stride (Wo + 2*owp)
 // * Cout, starting after the left margin) for TMA stores of {64, 32, 1}.
+// Phase-plane output: {Cout, Wo/2 + 1, Ho/2, N*4} with box {64, 16, 1, 1}.
 static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
+  if (sh.out_phase) {
+    const cuuint64_t wq = (cuuint64_t)sh.wo / 2 + 1, hh = (cuuint64_t)sh.ho / 2, px = (cuuint64_t)sh.cout * 2;
+    cuuint64_t dims[4] = {(cuuint64_t)sh.cout, wq, hh, (cuuint64_t)sh.n * 4};
+    cuuint64_t strides[3] = {px, wq * px, hh * wq * px};
+    cuuint32_t box[4] = {64, 16, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, out, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(MTL_ERR_ARGUMENT, "conv2d: phase-plane output tensor map rejected (CUresult %d)", (int)r);
+    return MTL_OK;
+  }
   cuuint64_t dims[3] = {(cuuint64_t)sh.cout, (cuuint64_t)sh.wo, (cuuint64_t)sh.n * sh.ho};
   cuuint64_t strides[2] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.wso * sh.cout * 2};
   cuuint32_t box[3] = {64, 32, 1};
@@ -1420,17 +1595,17 @@ static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, con
   return cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, bool PH>
 static cudaError_t launch_halo(const CUtensorMap& tw, const CUtensorMap& ta, void* out, const ConvShape& sh, int relu,
                                int sm_count, cudaStream_t s) {
   const uint32_t smem = halo_smem_bytes(sh, HaloCfg<BN>::kBBlock);
-  cudaError_t e = cudaFuncSetAttribute(conv_halo_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(conv_halo_kernel<BN, PH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int64_t tiles = (int64_t)sh.n * sh.halo_tiles * sh.nblk;
   // whole column-block groups: CTA b serves column block b % nblk
   int grid = (int)std::min<int64_t>(tiles, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_halo_kernel<BN><<<grid, 224, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  conv_halo_kernel<BN, PH><<<grid, 224, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
   return cudaGetLastError();
 }
 
@@ -1464,24 +1639,37 @@ static double pick_rect(ConvShape& sh, int sx, int sy) {
   return best;
 }
 
-// The flat-halo plan (A_HALO) for a stride-1 3x3 convolution whose input
-// stores its padding column on each side: the widest BN dividing Cout whose resident weights
-// leave room for at least two halo stages in the 227 KiB of shared memory,
-// where the halo fits one TMA box (at most 256 rows) and the tiles' margin
-// positions waste under 15 % of the MMA rows. Returns BN, or 0.
+// The flat-halo plan (A_HALO) for a 3x3 convolution with padding 1 and Cin a
+// multiple of 64: at stride 1 over an input that stores its padding column on
+// each side (the tiles' margin positions must waste under 15 % of the MMA
+// rows), or at stride 2 over phase planes (any waste: no other path reads
+// them). The widest BN dividing Cout whose resident weights leave room for at
+// least two halo stages in the 227 KiB of shared memory, where the halo fits
+// one TMA box (at most 256 rows). Returns BN, or 0.
 static int halo_plan(ConvShape& sh) {
-  if (sh.stride != 1 || sh.cin % 64 || sh.k != 3 || sh.pad != 1 || sh.wpad != 1) return 0;
-  if (sh.owp != 0 && sh.owp != sh.pad) return 0;
-  const int rows = 128 + 2 * (sh.pad * sh.ws + sh.pad);
+  if (sh.cin % 64 || sh.k != 3 || sh.pad != 1) return 0;
+  if (sh.out_phase && (sh.ho % 2 || sh.wo % 2)) return 0;
+  int rows, tiles, max_stages;
+  if (sh.in_phase) {
+    if (sh.stride != 2 || sh.h % 2 || sh.w % 2 || sh.owp > 1) return 0;
+    rows = 128 + sh.pq + 1;
+    tiles = (sh.ho * sh.pq + 127) / 128;
+    max_stages = 8;  // four loads (planes) per tile and channel block
+  } else {
+    if (sh.stride != 1 || sh.wpad != 1) return 0;
+    if (sh.owp != 0 && sh.owp != sh.pad) return 0;
+    rows = 128 + 2 * (sh.pad * sh.ws + sh.pad);
+    tiles = (sh.h * sh.ws + 127) / 128;
+    if ((double)sh.h * sh.w < 0.85 * tiles * 128.0) return 0;
+    max_stages = 4;
+  }
   if (rows > 256) return 0;
-  const int tiles = (sh.h * sh.ws + 127) / 128;
-  if ((double)sh.h * sh.w < 0.85 * tiles * 128.0) return 0;
   const int stage = (rows * 128 + 1023) & ~1023;
   const int kblocks = sh.taps * sh.cin / 64;
   for (int bn = 128; bn >= 64; bn /= 2) {  // four accumulators of 4 * bn <= 512 TMEM columns
     if (sh.cout % bn) continue;
     const int64_t avail = 232448 - 1024 - 256 - (int64_t)kblocks * 64 * bn * 2;
-    const int stages = (int)std::min<int64_t>(4, avail / stage);
+    const int stages = (int)std::min<int64_t>(max_stages, avail / stage);
     if (stages < 2) continue;
     sh.kblocks = kblocks;
     sh.halo_rows = rows;
@@ -1525,6 +1713,12 @@ static bool rows_plan(ConvShape& sh, int src_c = 0) {
 // descriptors of smaller tensors on drivers up to 13.1; those small inputs
 // take the gather path instead).
 static int conv_amode(ConvShape& sh) {
+  if (sh.in_phase) {  // phase planes: the stride-2 halo or nothing
+    ConvShape t = sh;
+    if (!halo_plan(t)) return -1;
+    sh = t;
+    return A_HALO;
+  }
   const uint64_t in_bytes = (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2;
   const bool corners_ok = sh.pad + sh.wpad <= 127 && sh.pad - (sh.k - 1) - sh.wpad >= -128;
   if (!corners_ok || in_bytes < (128u << 10) || sh.stride > 8) return A_GATHER;
@@ -1639,11 +1833,16 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   if (am == A_HALO) {
     ConvShape hs = sh;
     const int bn = halo_plan(hs);
-    if (mtl_status st = make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
-                                      (uint32_t)hs.halo_rows))
-      return st;
-    cudaError_t e = bn == 128 ? launch_halo<128>(tw, ta, out, hs, relu, la.sm_count, s)
-                              : launch_halo<64>(tw, ta, out, hs, relu, la.sm_count, s);
+    // stored rows {Cin, H * stored W, N}, or the planes {Cin, H/2 * (W/2 + 1), N * 4}
+    const mtl_status st = sh.in_phase ? make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)(sh.h / 2) * sh.pq,
+                                                      (uint64_t)sh.n * 4, (uint32_t)hs.halo_rows)
+                                      : make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
+                                                      (uint32_t)hs.halo_rows);
+    if (st) return st;
+    cudaError_t e = sh.in_phase ? (bn == 128 ? launch_halo<128, true>(tw, ta, out, hs, relu, la.sm_count, s)
+                                             : launch_halo<64, true>(tw, ta, out, hs, relu, la.sm_count, s))
+                                : (bn == 128 ? launch_halo<128, false>(tw, ta, out, hs, relu, la.sm_count, s)
+                                             : launch_halo<64, false>(tw, ta, out, hs, relu, la.sm_count, s));
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }
@@ -1663,7 +1862,8 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
 // out_wpad (i); ndrange = images. The first convolution of a network straight
 // from its NCHW input: the raw-row kernel with the NCHW -> NHWC conversion in
 // shared memory (C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of
-// at most 128 pixels, Cout a multiple of 64).
+// at most 128 pixels, Cout a multiple of 64). out_wpad = -1 writes the output
+// as phase planes.
 static ConvShape nchw_conv_shape(const LaunchArgs& la) {
   ConvShape sh{};
   sh.n = (int)la.nd[0];
@@ -1676,6 +1876,10 @@ static ConvShape nchw_conv_shape(const LaunchArgs& la) {
   sh.pad = la.a[9].i32;
   sh.wpad = sh.pad;
   sh.owp = la.a[11].i32;
+  if (sh.owp == -1) {  // phase-plane output
+    sh.out_phase = 1;
+    sh.owp = 0;
+  }
   sh.ws = sh.w + 2 * sh.wpad;
   if (sh.stride > 0) {
     sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
@@ -1695,11 +1899,12 @@ mtl_status nchwconv_check(const LaunchArgs& la, const uint64_t* bytes) {
   if (sh.n < 0 || sh.h <= 0 || sh.w <= 0 || sh.k <= 0 || sh.stride <= 0 || sh.pad < 0 || c <= 0 || sh.cout <= 0 ||
       sh.owp < 0 || sh.owp > 64 || sh.ho <= 0 || sh.wo <= 0)
     return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: bad sizes");
-  if (c > 4 || sh.stride != 2 || sh.w % 8 || sh.ws % 2 || sh.cout % 64 || !rows_plan(sh, c))
+  if (c > 4 || sh.stride != 2 || sh.w % 8 || sh.ws % 2 || sh.cout % 64 || !rows_plan(sh, c) ||
+      (sh.out_phase && (sh.ho % 2 || sh.wo % 2)))
     return fail(MTL_ERR_UNSUPPORTED,
                 "conv2d_nchw: needs C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of at most 128 pixels "
-                "and Cout a multiple of 64");
-  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * c * sh.h * sh.w * 2,
+                "and Cout a multiple of 64 (and even Ho and Wo for a phase-plane output)");
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * (sh.out_phase ? sh.wo + 2 : sh.wso) * sh.cout * 2, (uint64_t)sh.n * c * sh.h * sh.w * 2,
                             (uint64_t)sh.taps * 4 * sh.cout * 2};
   const char* what[3] = {"the output", "the input", "the weights"};
   for (int i = 0; i < 3; ++i) {

@@ -72,6 +72,30 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
     }
   }
 }
+// Wait, bounded, for an operation this CTA started itself (a load landing, its
+// MMAs finishing) before leaving; used on exit paths, so it ignores `abort`.
+__device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait_sleep(bar, parity))
+    if (globaltimer() - t0 > kWaitLimitNs) return;
+}
+// Bounded wait until another role's progress counter (in shared memory)
+// reaches `target`.
+__device__ __forceinline__ bool wait_progress(volatile int* counter, int target, volatile int* abort, int* timeouts) {
+  if (*counter >= target) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    __nanosleep(64);
+    if (*counter >= target) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      atomicAdd(timeouts, 1);
+      return false;
+    }
+  }
+}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
                                             uint32_t bar) {
   asm volatile(
@@ -144,6 +168,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
