@@ -48,11 +48,9 @@ struct ConvShape {
   int tw, th, tiles_x, tiles_y;
   int wpad, ws;   // zero columns stored on each side of every input row; stored width w + 2*wpad
   int owp, wso;   // the same for the output rows (written as zeros); stored output width wo + 2*owp
-  // Phase planes: a tensor stored as four planes [n][row parity][column
-  // parity][H/2][W/2 + 1][C], column 0 of every plane row zero (a stride-2
-  // layer reads each filter tap as a shifted run of one plane). in_phase: the
-  // input is stored so (pq = W/2 + 1); out_phase: write the output so.
-  int in_phase, out_phase, pq;
+  // Stride-2 halo (A_HALO at stride 2): positions per frame row pq = Wo + 1,
+  // output rows per tile ph_rows, bytes of one plane frame ph_box_bytes
+  int pq, ph_rows, ph_box_bytes;
   // A_HALO: halo rows per channel block, tiles per image, A stages and their
   // bytes, column blocks (Cout / BN)
   int halo_rows, halo_tiles, halo_stages, halo_stage_bytes, nblk;
@@ -467,6 +465,18 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
 // (taps * Cin/64 K blocks of 64 x BN). Roles as in conv_bf16_kernel: warp 0
 // loads, warp 1 issues tcgen05.mma into two TMEM accumulators, warps 2-5 read
 // them back.
+//
+// Stride 2 (3x3, padding 1) over the plain NHWC input: the input splits into
+// four parity planes (row parity pr, column parity pc), each a tensor map
+// over the same memory with pixel stride 2 and row stride 2 (no copy). Output
+// pixel (y, x) reads, for tap (r, c), plane row y - 1 (r = 0, odd rows), y
+// (r = 1, even rows; r = 2, odd rows) and plane column x - 1 (c = 0, odd
+// columns), x (c = 1, even; c = 2, odd). A tile is ph_rows output rows; per
+// plane and 64-channel block one TMA load brings the frame of plane rows
+// y0 - 1 .. y0 + ph_rows and columns -1 .. Wo - 1 (pq = Wo + 1 positions per
+// row; row -1 and column -1 lie outside the input: zeros, the padding). MMA
+// row m is output (y0 + m / pq, m % pq) (m % pq == Wo: no pixel), and tap (r,
+// c) reads frame position m + (r != 0) * pq + (c != 0): again one shifted run.
 template <int BN>
 struct HaloCfg {
   static constexpr uint32_t kBBlock = 64 * BN * 2;  // one K block of weights
@@ -491,9 +501,15 @@ __host__ __device__ constexpr int ph_tap_r(int p, int t) {
 }
 __host__ __device__ constexpr int ph_tap_c(int p, int t) { return (p & 1) ? ((t % 2) ? 2 : 0) : 1; }
 
+// The A-operand maps of a halo convolution: [0] the stored rows (stride 1),
+// or the four parity planes pr * 2 + pc (stride 2).
+struct HaloMaps {
+  CUtensorMap m[4];
+};
+
 template <int BN, bool PH>
 __global__ void __launch_bounds__(224, 1)
-    conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ HaloMaps tmA,
                      __nv_bfloat16* __restrict__ out, const ConvShape sh, int relu) {
   using Cfg = HaloCfg<BN>;
   extern __shared__ unsigned char hsm_raw[];
@@ -517,12 +533,13 @@ __global__ void __launch_bounds__(224, 1)
   const int nb = blockIdx.x % sh.nblk, n0 = nb * BN;
   const int64_t first = blockIdx.x / sh.nblk, step = gridDim.x / sh.nblk;
   const int64_t mtiles = (int64_t)sh.n * sh.halo_tiles;
-  // positions per row of the tiled grid and the halo's lead: stored input rows
-  // (stride 1: the taps' shifts are -pad*ws - pad .. +pad*ws + pad), or phase
-  // planes (stride 2: shifts -pq - 1 .. 0)
+  // positions per row of the tiled grid: stored input rows (stride 1; the
+  // halo run starts pad*ws + pad positions before the tile), or frame rows
+  // (stride 2)
   const int pitch = PH ? sh.pq : sh.ws;
-  const int halo0 = PH ? sh.pq + 1 : sh.pad * sh.ws + sh.pad;
-  constexpr int kLoads = PH ? 4 : 1;  // stages per (tile, channel block)
+  const int halo0 = sh.pad * sh.ws + sh.pad;
+  constexpr int kLoads = PH ? 4 : 1;  // stages per (tile, channel block): the planes
+  const uint32_t load_bytes = PH ? (uint32_t)sh.ph_box_bytes : (uint32_t)sh.halo_rows * 128;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -566,14 +583,17 @@ __global__ void __launch_bounds__(224, 1)
       int64_t loads = 0;
       for (int64_t t = first; t < mtiles; t += step) {
         const int img = (int)(t / sh.halo_tiles);
-        const int q0 = (int)(t - (int64_t)img * sh.halo_tiles) * 128;
+        const int tt = (int)(t - (int64_t)img * sh.halo_tiles);
         for (int cb = 0; cb < cblocks; ++cb)
           for (int p = 0; p < kLoads; ++p) {
             if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto p_done;
             const uint32_t fb = smem_u32(&full[s]);
-            mbar_expect_tx(fb, (uint32_t)sh.halo_rows * 128);
-            tma_load_3d(smem_u32(astage + (size_t)s * sh.halo_stage_bytes), &tmA, cb * 64, q0 - halo0,
-                        PH ? img * 4 + p : img, fb);
+            const uint32_t dst = smem_u32(astage + (size_t)s * sh.halo_stage_bytes);
+            mbar_expect_tx(fb, load_bytes);
+            if (PH)  // plane p's frame: rows y0 - 1 .., columns -1 ..
+              tma_load_4d(dst, &tmA.m[p], cb * 64, -1, tt * sh.ph_rows - 1, img, fb);
+            else
+              tma_load_3d(dst, &tmA.m[0], cb * 64, tt * 128 - halo0, img, fb);
             ++loads;
             if (++s == S) {
               s = 0;
@@ -655,8 +675,7 @@ __global__ void __launch_bounds__(224, 1)
                 }
               }
             } else {
-              // plane p's taps: filter row 0 starts one plane row earlier, filter
-              // column 0 one plane column earlier (rows pq + 1 of halo lead)
+              // plane p's taps, each at frame position m + (r != 0) * pq + (c != 0)
 #pragma unroll
               for (int t = 0; t < ph_ntaps(p); ++t) {
                 const int r = ph_tap_r(p, t), c = ph_tap_c(p, t);
@@ -688,33 +707,36 @@ __global__ void __launch_bounds__(224, 1)
   } else if (warp < 6) {
     const int q = warp & 3;
     int i = 0;
-    const int grid_pos = sh.ho * pitch;  // positions of one image's grid
+    const int grid_pos = sh.h * sh.ws;  // stride 1: positions of one image's stored grid
     for (int64_t t = first; t < mtiles; t += step, ++i) {
       const int a = i & 3;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
       const int img = (int)(t / sh.halo_tiles);
-      const int pos = (int)(t - (int64_t)img * sh.halo_tiles) * 128 + q * 32 + lane;  // grid position
-      const int y = pos / pitch, xg = pos - (pos / pitch) * pitch;
-      // the output column of this grid position, and whether it is one
-      const int xo = PH ? xg - 1 : xg - sh.pad;
-      const bool inner = pos < grid_pos && xo >= 0 && xo < sh.wo;
-      // Where the row goes (-1: nowhere) and whether it is a margin (zeros):
-      //   phase-plane output: the output pixel's plane row, plus (for xo < 2)
-      //     the plane row's zero column 0;
-      //   stride 1 with margins == padding: every grid position of the image
-      //     (its stored position), zeros at the margins;
+      const int tt = (int)(t - (int64_t)img * sh.halo_tiles);
+      const int m = q * 32 + lane;
+      // the output pixel of MMA row m, and whether it is one
+      int y, xo;
+      bool inner;
+      if (PH) {
+        const int row = m / pitch;
+        y = tt * sh.ph_rows + row;
+        xo = m - row * pitch;
+        inner = row < sh.ph_rows && y < sh.ho && xo < sh.wo;
+      } else {
+        const int pos = tt * 128 + m;  // stored position
+        y = pos / pitch;
+        xo = pos - y * pitch - sh.pad;
+        inner = pos < grid_pos && xo >= 0 && xo < sh.wo;
+      }
+      // Where the row goes (-1: nowhere) and the margin pixels it zeros:
+      //   stride 1 with margins == padding: every stored position of the
+      //     image, zeros at the margins;
       //   otherwise the output pixel with `owp` margins, the first and last
-      //     pixel of a row also zeroing that row's margins.
+      //     pixel of a row also zeroing that row's margin (owp <= 1 here).
       int64_t dpos = -1, zpos = -1, zpos2 = -1;
-      if (sh.out_phase) {
-        if (inner) {
-          const int hh = sh.ho / 2, wq = sh.wo / 2 + 1;
-          const int64_t prow_base = (((int64_t)img * 2 + (y & 1)) * 2 + (xo & 1)) * hh + (y >> 1);
-          dpos = prow_base * wq + (xo >> 1) + 1;
-          if (xo < 2) zpos = prow_base * wq;
-        }
-      } else if (!PH && sh.owp) {
+      if (!PH && sh.owp) {
+        const int pos = tt * 128 + m;
         if (pos < grid_pos) {
           if (inner)
             dpos = (int64_t)img * grid_pos + pos;
@@ -724,7 +746,7 @@ __global__ void __launch_bounds__(224, 1)
       } else if (inner) {
         const int64_t rowb = ((int64_t)img * sh.ho + y) * sh.wso;
         dpos = rowb + sh.owp + xo;
-        if (sh.owp && xo == 0) zpos = rowb;              // one margin pixel: owp is 1 here
+        if (sh.owp && xo == 0) zpos = rowb;
         if (sh.owp && xo == sh.wo - 1) zpos2 = rowb + sh.owp + sh.wo;
       }
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
@@ -780,10 +802,6 @@ __global__ void __launch_bounds__(224, 1)
 // c1, c2); rows past the map's second extent are clipped by the TMA. The
 // caller alternates two staging buffers per warp and calls
 // epi_stage_acquire() before reusing one.
-// Phase-plane output (c1 < 0): the 32 rows are 32 consecutive pixels of one
-// output row; the even ones go to staging rows 0..15, the odd ones to 16..31,
-// and two TMA stores of box {64, 16, 1, 1} put them into the row's two
-// column-parity planes at (c0 + 64*chunk, pc1, pc2, pc3) and (.., pc3 + 1).
 __device__ __forceinline__ void epi_stage_acquire(int lane) {
   if (lane == 0) bulk_wait_read<1>();
   __syncwarp();
@@ -791,9 +809,7 @@ __device__ __forceinline__ void epi_stage_acquire(int lane) {
 
 template <int BN>
 __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned char* stage, const CUtensorMap* tmO,
-                                              int c0, int c1, int c2, int lane, int pc1 = 0, int pc2 = 0,
-                                              int pc3 = 0) {
-  const int srow = c1 >= 0 ? lane : (lane & 1) * 16 + (lane >> 1);
+                                              int c0, int c1, int c2, int lane) {
 #pragma unroll
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -809,27 +825,19 @@ __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned
       __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
       pk[v] = *reinterpret_cast<uint32_t*>(&h);
     }
-    unsigned char* row = stage + (c / 2) * 4096 + srow * 128;
+    unsigned char* row = stage + (c / 2) * 4096 + lane * 128;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const int piece = (c % 2) * 4 + v;
-      *reinterpret_cast<uint4*>(row + ((piece ^ (srow & 7)) << 4)) =
+      *reinterpret_cast<uint4*>(row + ((piece ^ (lane & 7)) << 4)) =
           make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
     }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
   if (lane == 0) {
-    if (c1 >= 0) {
 #pragma unroll
-      for (int c = 0; c < BN / 64; ++c) tma_store_3d(tmO, smem_u32(stage + c * 4096), c0 + c * 64, c1, c2);
-    } else {
-#pragma unroll
-      for (int c = 0; c < BN / 64; ++c)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          tma_store_4d(tmO, smem_u32(stage + c * 4096 + h * 2048), c0 + c * 64, pc1, pc2, pc3 + h);
-    }
+    for (int c = 0; c < BN / 64; ++c) tma_store_3d(tmO, smem_u32(stage + c * 4096), c0 + c * 64, c1, c2);
     bulk_commit();
   }
 }
@@ -1124,18 +1132,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
         const int orow = img * sh.ho + oh0 + t;
         const int x = q * 32 + lane;
-        // phase-plane output: row y = oh0 + t's even and odd pixels go to
-        // planes (y & 1, 0) and (y & 1, 1), plane row y / 2, from column 1;
-        // x = 0 and x = 1 zero those plane rows' column 0
-        const int y = oh0 + t, pl = img * 4 + (y & 1) * 2;
-        epi_tma_store<BN>(tbase, relu, buf, &tmO, n0, sh.out_phase ? -1 : q * 32, orow, lane, 1 + q * 16, y >> 1,
-                          pl);
-        if (sh.out_phase && x < 2) {
-          uint4* z = reinterpret_cast<uint4*>(
-              out + (((int64_t)(pl + x) * (sh.ho / 2) + (y >> 1)) * (sh.wo / 2 + 1)) * sh.cout + n0);
-#pragma unroll
-          for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
-        }
+        epi_tma_store<BN>(tbase, relu, buf, &tmO, n0, q * 32, orow, lane);
         if (sh.owp && (x == 0 || x == sh.wo - 1)) {  // zero this output row's margin pixels
           __nv_bfloat16* p = out + ((int64_t)orow * sh.wso + sh.owp + x) * sh.cout + n0;
           for (int e = 1; e <= sh.owp; ++e) {
@@ -1388,9 +1385,6 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
 // columns the input buffer stores on each side of every row (its rows are
 // W + 2*in_wpad pixels long); the convolution's own padding is still `pad`.
 // out_wpad: the same for the output rows, which the kernel writes as zeros.
-// in_wpad = -1: the input is stored as phase planes (see ConvShape; a 3x3
-// stride-2 convolution with padding 1 over even H and W); out_wpad = -1: the
-// output is written so (even Ho and Wo).
 static ConvShape conv_shape(const LaunchArgs& la) {
   ConvShape sh{};
   sh.n = (int)la.nd[0];
@@ -1403,16 +1397,7 @@ static ConvShape conv_shape(const LaunchArgs& la) {
   sh.pad = la.a[9].i32;
   sh.wpad = la.a[11].i32;
   sh.owp = la.a[12].i32;
-  if (sh.wpad == -1) {
-    sh.in_phase = 1;
-    sh.wpad = 0;
-  }
-  if (sh.owp == -1) {
-    sh.out_phase = 1;
-    sh.owp = 0;
-  }
   sh.ws = sh.w + 2 * sh.wpad;
-  sh.pq = sh.w / 2 + 1;
   if (sh.stride > 0) {
     sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
     sh.wo = (sh.w + 2 * sh.pad - sh.k) / sh.stride + 1;
@@ -1435,21 +1420,13 @@ mtl_status conv_check(const LaunchArgs& la, const uint64_t* bytes) {
     return fail(MTL_ERR_ARGUMENT, "conv2d: sizes must be positive (paddings non-negative, out_wpad at most 64)");
   if (sh.ho <= 0 || sh.wo <= 0) return fail(MTL_ERR_ARGUMENT, "conv2d: the filter does not fit the padded input");
   const int am = conv_amode(sh);
-  if (sh.in_phase && am != A_HALO)
-    return fail(MTL_ERR_UNSUPPORTED,
-                "conv2d: a phase-plane input (in_wpad = -1) needs a 3x3 stride-2 convolution with padding 1, even H "
-                "and W, Cin a multiple of 64, W/2 + 1 <= 127, out_wpad in {-1, 0, 1}");
-  if (sh.out_phase && (am != A_HALO && am != A_ROWS || sh.ho % 2 || sh.wo % 2))
-    return fail(MTL_ERR_UNSUPPORTED,
-                "conv2d: a phase-plane output (out_wpad = -1) needs even Ho and Wo and the halo or raw-row path");
   if (sh.cin % 8 && !(sh.cin == 4 && (am == A_WINDOW4 || am == A_WINDOW4_RECT || am == A_ROWS)))
     return fail(MTL_ERR_UNSUPPORTED,
                 "conv2d: Cin must be a multiple of 8 (pad the channels), or 4 for an input stored with its padding "
                 "columns (at least 128 KiB), got %d",
                 sh.cin);
   if (sh.cout % 64) return fail(MTL_ERR_UNSUPPORTED, "conv2d: Cout must be a multiple of 64, got %d", sh.cout);
-  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * (sh.out_phase ? sh.wo + 2 : sh.wso) * sh.cout * 2,
-                            (uint64_t)sh.n * sh.h * (sh.in_phase ? sh.w + 2 : sh.ws) * sh.cin * 2,
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2,
                             (uint64_t)sh.taps * sh.cin * sh.cout * 2};
   const char* what[3] = {"the output", "the input", "the weights"};
   for (int i = 0; i < 3; ++i) {
@@ -1550,25 +1527,36 @@ static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, con
   return cudaGetLastError();
 }
 
+// The four parity planes of a plain NHWC input for the stride-2 halo path:
+// plane pr * 2 + pc is {Cin, columns of parity pc, rows of parity pr, N} with
+// pixel stride 2 * Cin, row stride 2 * W * Cin, starting at pixel (pr, pc);
+// box {64, pq, ph_rows + 1, 1} (one frame).
+static mtl_status make_plane_maps(HaloMaps* maps, const void* in, const ConvShape& sh) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t px = (cuuint64_t)sh.cin * 2;
+  for (int p = 0; p < 4; ++p) {
+    const int pr = p >> 1, pc = p & 1;
+    cuuint64_t dims[4] = {(cuuint64_t)sh.cin, (cuuint64_t)(sh.w - pc + 1) / 2, (cuuint64_t)(sh.h - pr + 1) / 2,
+                          (cuuint64_t)sh.n};
+    cuuint64_t strides[3] = {2 * px, 2 * (cuuint64_t)sh.w * px, (cuuint64_t)sh.h * sh.w * px};
+    cuuint32_t box[4] = {64, (cuuint32_t)sh.pq, (cuuint32_t)(sh.ph_rows + 1), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    const void* base = reinterpret_cast<const __nv_bfloat16*>(in) + ((int64_t)pr * sh.w + pc) * sh.cin;
+    CUresult r = enc(&maps->m[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(MTL_ERR_ARGUMENT, "conv2d: parity-plane tensor map rejected (CUresult %d)", (int)r);
+  }
+  return MTL_OK;
+}
+
 // The output as {Cout, Wo, N*Ho} (pixel stride Cout, row stride (Wo + 2*owp)
 // * Cout, starting after the left margin) for TMA stores of {64, 32, 1}.
-// Phase-plane output: {Cout, Wo/2 + 1, Ho/2, N*4} with box {64, 16, 1, 1}.
 static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
-  if (sh.out_phase) {
-    const cuuint64_t wq = (cuuint64_t)sh.wo / 2 + 1, hh = (cuuint64_t)sh.ho / 2, px = (cuuint64_t)sh.cout * 2;
-    cuuint64_t dims[4] = {(cuuint64_t)sh.cout, wq, hh, (cuuint64_t)sh.n * 4};
-    cuuint64_t strides[3] = {px, wq * px, hh * wq * px};
-    cuuint32_t box[4] = {64, 16, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, out, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-      return fail(MTL_ERR_ARGUMENT, "conv2d: phase-plane output tensor map rejected (CUresult %d)", (int)r);
-    return MTL_OK;
-  }
   cuuint64_t dims[3] = {(cuuint64_t)sh.cout, (cuuint64_t)sh.wo, (cuuint64_t)sh.n * sh.ho};
   cuuint64_t strides[2] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.wso * sh.cout * 2};
   cuuint32_t box[3] = {64, 32, 1};
@@ -1596,7 +1584,7 @@ static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, con
 }
 
 template <int BN, bool PH>
-static cudaError_t launch_halo(const CUtensorMap& tw, const CUtensorMap& ta, void* out, const ConvShape& sh, int relu,
+static cudaError_t launch_halo(const CUtensorMap& tw, const HaloMaps& ta, void* out, const ConvShape& sh, int relu,
                                int sm_count, cudaStream_t s) {
   const uint32_t smem = halo_smem_bytes(sh, HaloCfg<BN>::kBBlock);
   cudaError_t e = cudaFuncSetAttribute(conv_halo_kernel<BN, PH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1641,19 +1629,25 @@ static double pick_rect(ConvShape& sh, int sx, int sy) {
 
 // The flat-halo plan (A_HALO) for a 3x3 convolution with padding 1 and Cin a
 // multiple of 64: at stride 1 over an input that stores its padding column on
-// each side (the tiles' margin positions must waste under 15 % of the MMA
-// rows), or at stride 2 over phase planes (any waste: no other path reads
-// them). The widest BN dividing Cout whose resident weights leave room for at
-// least two halo stages in the 227 KiB of shared memory, where the halo fits
-// one TMA box (at most 256 rows). Returns BN, or 0.
+// each side, at stride 2 over plain rows (no stored margins) whose output rows
+// have at most 126 pixels; either way the tiles' unused positions must waste
+// under 15 % of the MMA rows (measured at stride 2: 77 % busy rows over the
+// 28 x 28 x 128 input took 67 us against 36 us for rectangles). The widest BN
+// dividing Cout whose resident weights leave room for at least two halo
+// stages in the 227 KiB of shared memory, where the halo fits one TMA box (at
+// most 256 rows). Returns BN, or 0.
 static int halo_plan(ConvShape& sh) {
   if (sh.cin % 64 || sh.k != 3 || sh.pad != 1) return 0;
-  if (sh.out_phase && (sh.ho % 2 || sh.wo % 2)) return 0;
   int rows, tiles, max_stages;
-  if (sh.in_phase) {
-    if (sh.stride != 2 || sh.h % 2 || sh.w % 2 || sh.owp > 1) return 0;
-    rows = 128 + sh.pq + 1;
-    tiles = (sh.ho * sh.pq + 127) / 128;
+  if (sh.stride == 2) {
+    if (sh.wpad != 0 || sh.owp > 1 || sh.h < 2 || sh.w < 2) return 0;
+    sh.pq = sh.wo + 1;
+    if (sh.pq > 127) return 0;
+    sh.ph_rows = std::min(128 / sh.pq, sh.ho);
+    tiles = (sh.ho + sh.ph_rows - 1) / sh.ph_rows;
+    if ((double)sh.ho * sh.wo < 0.85 * tiles * 128.0) return 0;
+    rows = 128 + sh.pq + 1;  // the frame ((ph_rows + 1) * pq) and every MMA row's reads
+    sh.ph_box_bytes = 64 * 2 * sh.pq * (sh.ph_rows + 1);
     max_stages = 8;  // four loads (planes) per tile and channel block
   } else {
     if (sh.stride != 1 || sh.wpad != 1) return 0;
@@ -1713,12 +1707,6 @@ static bool rows_plan(ConvShape& sh, int src_c = 0) {
 // descriptors of smaller tensors on drivers up to 13.1; those small inputs
 // take the gather path instead).
 static int conv_amode(ConvShape& sh) {
-  if (sh.in_phase) {  // phase planes: the stride-2 halo or nothing
-    ConvShape t = sh;
-    if (!halo_plan(t)) return -1;
-    sh = t;
-    return A_HALO;
-  }
   const uint64_t in_bytes = (uint64_t)sh.n * sh.h * sh.ws * sh.cin * 2;
   const bool corners_ok = sh.pad + sh.wpad <= 127 && sh.pad - (sh.k - 1) - sh.wpad >= -128;
   if (!corners_ok || in_bytes < (128u << 10) || sh.stride > 8) return A_GATHER;
@@ -1833,16 +1821,19 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   if (am == A_HALO) {
     ConvShape hs = sh;
     const int bn = halo_plan(hs);
-    // stored rows {Cin, H * stored W, N}, or the planes {Cin, H/2 * (W/2 + 1), N * 4}
-    const mtl_status st = sh.in_phase ? make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)(sh.h / 2) * sh.pq,
-                                                      (uint64_t)sh.n * 4, (uint32_t)hs.halo_rows)
-                                      : make_bf16_map(&ta, in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
-                                                      (uint32_t)hs.halo_rows);
-    if (st) return st;
-    cudaError_t e = sh.in_phase ? (bn == 128 ? launch_halo<128, true>(tw, ta, out, hs, relu, la.sm_count, s)
-                                             : launch_halo<64, true>(tw, ta, out, hs, relu, la.sm_count, s))
-                                : (bn == 128 ? launch_halo<128, false>(tw, ta, out, hs, relu, la.sm_count, s)
-                                             : launch_halo<64, false>(tw, ta, out, hs, relu, la.sm_count, s));
+    HaloMaps maps;
+    memset(&maps, 0, sizeof maps);
+    const bool ph = sh.stride == 2;
+    if (ph) {
+      if (mtl_status st = make_plane_maps(&maps, in, hs)) return st;
+    } else if (mtl_status st = make_bf16_map(&maps.m[0], in, (uint64_t)sh.cin, (uint64_t)sh.h * sh.ws, (uint64_t)sh.n,
+                                             (uint32_t)hs.halo_rows)) {
+      return st;
+    }
+    cudaError_t e = ph ? (bn == 128 ? launch_halo<128, true>(tw, maps, out, hs, relu, la.sm_count, s)
+                                    : launch_halo<64, true>(tw, maps, out, hs, relu, la.sm_count, s))
+                       : (bn == 128 ? launch_halo<128, false>(tw, maps, out, hs, relu, la.sm_count, s)
+                                    : launch_halo<64, false>(tw, maps, out, hs, relu, la.sm_count, s));
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }
@@ -1862,8 +1853,7 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
 // out_wpad (i); ndrange = images. The first convolution of a network straight
 // from its NCHW input: the raw-row kernel with the NCHW -> NHWC conversion in
 // shared memory (C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of
-// at most 128 pixels, Cout a multiple of 64). out_wpad = -1 writes the output
-// as phase planes.
+// at most 128 pixels, Cout a multiple of 64).
 static ConvShape nchw_conv_shape(const LaunchArgs& la) {
   ConvShape sh{};
   sh.n = (int)la.nd[0];
@@ -1876,10 +1866,6 @@ static ConvShape nchw_conv_shape(const LaunchArgs& la) {
   sh.pad = la.a[9].i32;
   sh.wpad = sh.pad;
   sh.owp = la.a[11].i32;
-  if (sh.owp == -1) {  // phase-plane output
-    sh.out_phase = 1;
-    sh.owp = 0;
-  }
   sh.ws = sh.w + 2 * sh.wpad;
   if (sh.stride > 0) {
     sh.ho = (sh.h + 2 * sh.pad - sh.k) / sh.stride + 1;
@@ -1899,12 +1885,11 @@ mtl_status nchwconv_check(const LaunchArgs& la, const uint64_t* bytes) {
   if (sh.n < 0 || sh.h <= 0 || sh.w <= 0 || sh.k <= 0 || sh.stride <= 0 || sh.pad < 0 || c <= 0 || sh.cout <= 0 ||
       sh.owp < 0 || sh.owp > 64 || sh.ho <= 0 || sh.wo <= 0)
     return fail(MTL_ERR_ARGUMENT, "conv2d_nchw: bad sizes");
-  if (c > 4 || sh.stride != 2 || sh.w % 8 || sh.ws % 2 || sh.cout % 64 || !rows_plan(sh, c) ||
-      (sh.out_phase && (sh.ho % 2 || sh.wo % 2)))
+  if (c > 4 || sh.stride != 2 || sh.w % 8 || sh.ws % 2 || sh.cout % 64 || !rows_plan(sh, c))
     return fail(MTL_ERR_UNSUPPORTED,
                 "conv2d_nchw: needs C <= 4, stride 2, k <= 8, W a multiple of 8, output rows of at most 128 pixels "
-                "and Cout a multiple of 64 (and even Ho and Wo for a phase-plane output)");
-  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * (sh.out_phase ? sh.wo + 2 : sh.wso) * sh.cout * 2, (uint64_t)sh.n * c * sh.h * sh.w * 2,
+                "and Cout a multiple of 64");
+  const uint64_t need[3] = {(uint64_t)sh.n * sh.ho * sh.wso * sh.cout * 2, (uint64_t)sh.n * c * sh.h * sh.w * 2,
                             (uint64_t)sh.taps * 4 * sh.cout * 2};
   const char* what[3] = {"the output", "the input", "the weights"};
   for (int i = 0; i < 3; ++i) {

@@ -318,27 +318,12 @@ def cnn_input(batch_total: int, seed: int = 3, device: str = "cuda"):
     return torch.rand((batch_total, 3, 224, 224), generator=g, device=device).to(torch.bfloat16)
 
 
-def phase_input_pays(h: int, w: int, cin: int, k: int, s: int) -> bool:
-    """Whether a conv over an h x w x cin input reads it as phase planes: a 3x3
-    stride-2 conv over even sizes whose weights (one 64-wide column block) stay
-    resident in shared memory and whose 128-position tiles over the
-    (h/2) x (w/2 + 1) plane grid keep at least 85 % of the MMA rows busy."""
-    if k != 3 or s != 2 or h % 2 or w % 2 or cin % 64 or w // 2 + 1 > 127:
-        return False
-    if 9 * cin * 64 * 2 > 160 * 1024:
-        return False
-    ho, pq = h // 2, w // 2 + 1
-    tiles = -(-ho * pq // 128)
-    return ho * (w // 2) >= 0.85 * tiles * 128
-
-
 def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 1, **plan_kw) -> CnnWorkload:
     """The forward pass as one graph: nine conv+ReLU passes over transients
     (aliased by the placer; the stem reads the NCHW input and converts it to
     padded NHWC rows in shared memory; the input of each stride-1 conv is
-    stored with its padding columns; the input of a stride-2 conv, where that
-    pays, as four phase planes), then GAP+FC into the logits. With world > 1
-    this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
+    stored with its padding columns), then GAP+FC into the logits. With
+    world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
     import torch
     device = f"cuda:{dev.ordinal}"
     per = batch // world
@@ -359,12 +344,9 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
         # ahead of a stride-1 conv, store its padding columns (zeros, written by
         # this conv's epilogue), which lets that conv read every filter tap as
         # one shifted run of stored pixels
-        # ahead of a stride-2 conv that reads phase planes, write them (owp = -1)
         nxt_layer = CNN_LAYERS[i + 1] if i + 1 < len(CNN_LAYERS) else None
         owp = nxt_layer[1] // 2 if nxt_layer is not None and nxt_layer[4] == 1 else 0
-        if nxt_layer is not None and phase_input_pays(ho, wo, cout, nxt_layer[1], nxt_layer[4]):
-            owp = -1
-        nxt = Transient.Buffer(g, np.uint16, per * ho * (wo + (2 if owp < 0 else 2 * owp)) * cout)
+        nxt = Transient.Buffer(g, np.uint16, per * ho * (wo + 2 * owp) * cout)
         if i == 0:  # the stem reads the NCHW input itself (converted in shared memory)
             compute(g, name, lambda p, src=cur, dst=nxt, wt=W[name], h=h, w=w, cout=cout, k=k, s=s, pad=pad,
                     owp=owp: dispatch(p, kernels.conv2d_nchw_bf16, (

@@ -150,7 +150,8 @@ def test_conv_with_stored_margin(dev, cin, n, h, w, cout, k, s, pad, wpad):
     (2, 40, 40, 64, 128, 3, 1, 1, 1, 1),    # halo, BN = 128, three stages
     (3, 37, 45, 64, 64, 3, 1, 1, 1, 1),     # halo, odd sizes, tiles end past the image
     (2, 30, 30, 64, 64, 5, 1, 2, 2, 2),     # 5x5: the halo exceeds one box -> rectangles, 2-pixel margins
-    (2, 112, 112, 64, 64, 3, 2, 1, 0, 1),   # rectangles writing margins (the first stage's stride-2 conv)
+    (2, 112, 112, 64, 64, 3, 2, 1, 0, 1),   # stride-2 halo writing margins (the first stage's stride-2 conv)
+    (2, 112, 112, 64, 64, 3, 2, 1, 1, 1),   # the same over an input with stored margins: rectangles
     (4, 28, 28, 128, 256, 3, 2, 1, 1, 1),   # flat im2col runs, margins in and out
     (1, 9, 9, 64, 64, 3, 1, 1, 0, 1),       # gather (small input) writing margins
 ])
@@ -174,163 +175,81 @@ def test_conv_margins_and_halo(dev, n, h, w, cin, cout, k, s, pad, wpad, owp):
     assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
 
 
-# Phase planes: a tensor (n, H, W, C) stored as (n, row parity, column parity,
-# H/2, W/2 + 1, C) with column 0 of every plane row zero. A 3x3 stride-2
-# convolution with padding 1 reads each filter tap from one plane as a flat
-# run of plane positions shifted by 0, 1, W/2 + 1 or W/2 + 2 from the tile's
-# halo start, like the stride-1 halo path reads stored rows.
-def to_phase(x):
-    n, h, w, c = x.shape
-    pl = np.zeros((n, 2, 2, h // 2, w // 2 + 1, c), x.dtype)
-    for pr in range(2):
-        for pc in range(2):
-            pl[:, pr, pc, :, 1:] = x[:, pr::2, pc::2]
-    return pl
-
-
-def from_phase(pl):
-    n, _, _, hh, wq, c = pl.shape
-    y = np.empty((n, 2 * hh, 2 * (wq - 1), c), pl.dtype)
-    for pr in range(2):
-        for pc in range(2):
-            y[:, pr::2, pc::2] = pl[:, pr, pc, :, 1:]
-    return y
-
-
-def phase_taps(p):
-    """Filter taps (r, c) of plane p = 2 * row parity + column parity and their
-    shift in plane positions from the halo start (pq + 1 positions before the
-    output position's own): row 0 lies one plane row up, column 0 one column left."""
+# Stride-2 halo: a 3x3 stride-2 conv (padding 1) over plain NHWC rows reads
+# the input as four parity planes (tensor maps with pixel and row stride 2).
+# A tile is T output rows; per plane one load brings the frame of plane rows
+# y0 - 1 .. y0 + T and columns -1 .. Wo - 1 (pq = Wo + 1 positions a row), and
+# tap (r, c) of MMA row m reads frame position m + (r != 0) * pq + (c != 0).
+def stride2_taps(p):
+    """Filter taps (r, c) read from parity plane p = 2 * row parity + column parity."""
     rows = [1] if p >> 1 == 0 else [0, 2]
     cols = [1] if p & 1 == 0 else [0, 2]
     return [(r, c) for r in rows for c in cols]
 
 
-def test_phase_plane_addressing_matches_oracle():
-    """The flat-shift addressing of the stride-2 halo kernel, restated in numpy
-    over phase planes, against the oracle's direct convolution."""
+@pytest.mark.parametrize("h,w", [(10, 14), (9, 13), (12, 7)])
+def test_stride2_frame_addressing_matches_oracle(h, w):
+    """The stride-2 halo kernel's frames and shifted reads, restated in numpy,
+    against the oracle's direct convolution (even and odd sizes)."""
     rng = np.random.default_rng(23)
-    n, h, w, cin, cout = 2, 10, 14, 8, 16
+    n, cin, cout = 2, 8, 16
     x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
     wt = _rand_bits(rng, (3, 3, cin, cout), scale=0.3)
     ref, _ = O.conv_bf16(x, wt, 2, 1, relu=False)
-    pl = O.bf16_to_f32(to_phase(x)).astype(np.float64)
+    ho, wo = ref.shape[1:3]
+    xf = O.bf16_to_f32(x).astype(np.float64)
     wf = O.bf16_to_f32(wt).astype(np.float64)
-    hh, pq = h // 2, w // 2 + 1
-    ho, wo = h // 2, w // 2
-    lead = pq + 1
-    got = np.zeros((n, ho * pq, cout))
+    pq = wo + 1
+    T = min(128 // pq, ho)
+    got = np.zeros((n, ho, wo, cout))
     for img in range(n):
-        for p in range(4):
-            flat = pl[img, p >> 1, p & 1].reshape(hh * pq, cin)
-            halo = np.concatenate([np.zeros((lead, cin)), flat, np.zeros((lead, cin))])
-            for (r, c) in phase_taps(p):
-                start = (0 if r == 0 else pq) + (0 if c == 0 else 1)
-                got[img] += halo[start:start + ho * pq] @ wf[r, c]
-    got = got.reshape(n, ho, pq, cout)[:, :, 1:]
+        for y0 in range(0, ho, T):
+            acc = np.zeros((128, cout))
+            for p in range(4):
+                pr, pc = p >> 1, p & 1
+                # past the frame: stale shared memory, never read for an output pixel
+                frame = np.full((128 + pq + 1, cin), np.nan)
+                frame[:(T + 1) * pq] = 0.0
+                for R in range(T + 1):
+                    for J in range(-1, wo):
+                        iy, ix = 2 * (y0 - 1 + R) + pr, 2 * J + pc
+                        if 0 <= iy < h and 0 <= ix < w:
+                            frame[R * pq + J + 1] = xf[img, iy, ix]
+                for (r, c) in stride2_taps(p):
+                    off = (pq if r else 0) + (1 if c else 0)
+                    acc += frame[off:off + 128] @ wf[r, c]
+            for m in range(128):
+                y, xo = y0 + m // pq, m % pq
+                if m // pq < T and y < ho and xo < wo:
+                    got[img, y, xo] = acc[m]
     assert np.allclose(got, ref, rtol=1e-12, atol=1e-12)
-    assert np.array_equal(from_phase(to_phase(x)), x)
 
 
-# A stride-2 3x3 conv over a phase-plane input (in_wpad = -1): the stride-2
-# halo kernel, four plane loads per tile and channel block. Outputs plain, with
-# one margin column, or as phase planes (out_wpad = -1).
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,h,w,cin,cout,owp", [
-    (4, 112, 112, 64, 64, 0),    # the first stage's stride-2 conv (BN = 64, six stages)
+    (4, 112, 112, 64, 64, 0),    # the first stage's stride-2 conv (BN = 64, two rows a tile, six stages)
     (4, 56, 56, 64, 128, 0),     # the second stage's (BN = 128, four stages: one tile in flight)
-    (3, 28, 28, 128, 256, 1),    # two channel blocks, four column blocks, output margins
-    (3, 38, 46, 64, 64, 1),      # tiles end past the image
-    (2, 56, 56, 64, 64, -1),     # phase planes in and out
+    (3, 24, 40, 128, 256, 1),    # two channel blocks, four column blocks, output margins
+    (3, 37, 45, 64, 64, 1),      # odd sizes: a short last tile, odd planes one row / column shorter
     (48, 56, 56, 64, 128, 0),    # several tiles per CTA: both issuers wait on the same four stages
-    (24, 112, 112, 64, 64, -1),  # several tiles per CTA over six stages, phase planes out
+    (24, 112, 112, 64, 64, 1),   # several tiles per CTA over six stages, output margins
 ])
-def test_conv_phase_input(dev, n, h, w, cin, cout, owp):
+def test_conv_stride2_halo(dev, n, h, w, cin, cout, owp):
     import torch
     rng = np.random.default_rng(29)
     x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
     wt = _rand_bits(rng, (3, 3, cin, cout), scale=float(np.sqrt(2.0 / (9 * cin))))
-    ho, wo = h // 2, w // 2
-    xt = torch.from_numpy(to_phase(x).view(np.int16)).cuda()
-    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
-    shape = (n, 2, 2, ho // 2, wo // 2 + 1, cout) if owp < 0 else (n, ho, wo + 2 * owp, cout)
-    out = torch.full(shape, -1, dtype=torch.int16, device="cuda")
-    st = torch.cuda.current_stream().cuda_stream
-    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, 3, 2, 1, 1, -1, owp), n, stream=st)
-    torch.cuda.synchronize()
-    got = out.cpu().numpy().view(np.uint16)
     ref, _ = O.conv_bf16(x, wt, 2, 1, relu=True)
-    if owp < 0:
-        assert not got[..., 0, :].any()
-        close_layer(from_phase(got), ref)
-    else:
-        close_layer(got[:, :, owp:owp + wo], ref)
-        assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
-
-
-# Phase-plane outputs (out_wpad = -1) of the layers that feed a stride-2 conv:
-# the stride-1 halo kernel and the raw-row stem (from NHWC rows or NCHW).
-@pytest.mark.gpu
-@pytest.mark.parametrize("kind,n,h,w,cin,cout", [
-    ("halo", 4, 56, 56, 64, 64),      # the first stage's second conv
-    ("halo", 2, 28, 28, 128, 128),    # BN = 128
-    ("nchw", 2, 224, 224, 3, 64),     # the stem
-    ("nchw", 3, 60, 96, 3, 128),      # two column blocks
-    ("rows", 4, 64, 80, 4, 64),       # the raw-row kernel over stored NHWC rows
-])
-def test_conv_phase_output(dev, kind, n, h, w, cin, cout):
-    import torch
-    rng = np.random.default_rng(31)
-    st = torch.cuda.current_stream().cuda_stream
-    if kind == "halo":
-        k, s, pad = 3, 1, 1
-        x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
-        wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
-        stored = np.zeros((n, h, w + 2, cin), np.uint16)
-        stored[:, :, 1:1 + w] = x
-        ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
-    elif kind == "nchw":
-        k, s, pad = 7, 2, 3
-        x = _rand_bits(rng, (n, cin, h, w), nonneg=True)
-        wt = _rand_bits(rng, (k, k, 4, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
-        wt[:, :, cin:] = 0
-        stored = x
-        ref, _ = O.conv_bf16(O.nchw_to_nhwc(x, 4), wt, s, pad, relu=True)
-    else:
-        k, s, pad = 7, 2, 3
-        x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
-        wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
-        stored = np.zeros((n, h, w + 2 * pad, cin), np.uint16)
-        stored[:, :, pad:pad + w] = x
-        ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
     ho, wo = ref.shape[1:3]
-    xt = torch.from_numpy(stored.view(np.int16)).cuda()
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
     wtt = torch.from_numpy(wt.view(np.int16)).cuda()
-    out = torch.full((n, 2, 2, ho // 2, wo // 2 + 1, cout), -1, dtype=torch.int16, device="cuda")
-    if kind == "nchw":
-        M.launch(M.kernels.conv2d_nchw_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, 1, -1), n, stream=st)
-    else:
-        M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, k, s, pad, 1, 1 if kind == "halo" else pad, -1),
-                 n, stream=st)
+    out = torch.full((n, ho, wo + 2 * owp, cout), -1, dtype=torch.int16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    M.launch(M.kernels.conv2d_bf16, (out, xt, wtt, h, w, cin, cout, 3, 2, 1, 1, 0, owp), n, stream=st)
     torch.cuda.synchronize()
     got = out.cpu().numpy().view(np.uint16)
-    assert not got[..., 0, :].any()
-    close_layer(from_phase(got), ref)
-
-
-@pytest.mark.gpu
-def test_conv_phase_refusals(dev):
-    import torch
-    t = torch.zeros(1 << 22, dtype=torch.int16, device="cuda")
-    st = torch.cuda.current_stream().cuda_stream
-    with pytest.raises(M.MantleError, match="phase-plane input"):  # stride 1
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 56, 56, 64, 64, 3, 1, 1, 1, -1, 0), 2, stream=st)
-    with pytest.raises(M.MantleError, match="phase-plane input"):  # odd width
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 56, 55, 64, 64, 3, 2, 1, 1, -1, 0), 2, stream=st)
-    with pytest.raises(M.MantleError, match="phase-plane output"):  # odd output height
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 27, 28, 64, 64, 3, 1, 1, 1, 1, -1), 2, stream=st)
-    with pytest.raises(M.MantleError, match="phase-plane output"):  # a path without it (rectangles)
-        M.launch(M.kernels.conv2d_bf16, (t, t, t, 56, 56, 64, 64, 3, 2, 1, 1, 0, -1), 2, stream=st)
+    close_layer(got[:, :, owp:owp + wo], ref)
+    assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
 
 
 # The stem straight from an NCHW input: each stage's channel-plane rows are
