@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   uint64_t* empty = bars + kConvStages;
   uint64_t* tfull = bars + 2 * kConvStages;
   uint64_t* tempty = bars + 2 * kConvStages + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kConvStages + 4);
+  uint64_t* idle = bars + 2 * kConvStages + 4;  // the issuer's MMAs all done (drain before exit)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kConvStages + 5);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -151,6 +152,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 4);
     }
+    mbar_init(smem_u32(idle), 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -190,6 +192,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
+      int64_t loads = 0;
       const int cblocks = sh.cin / 64;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         int m0, n0, img, oh, ow;
@@ -255,13 +258,22 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
             else
               tma_load_3d(b_dst + c * 8192, &tmW, n0 + c * 64, kb * 64, 0, fb);
           }
+          ++loads;
           if (++s == kConvStages) {
             s = 0;
             ph ^= 1;
           }
         }
       }
-    w_done:;
+    w_done:
+      // no load may still be landing when the CTA leaves (an aborted run):
+      // wait for the last phase armed on each stage used (the gather mode's
+      // stages also count the gather threads' arrivals: not waited for here)
+      if (AM != A_GATHER)
+        for (int u = 0; u < kConvStages && u < loads; ++u) {
+          const int64_t g = loads - 1 - u;
+          drain_phase(smem_u32(&full[g % kConvStages]), (uint32_t)((g / kConvStages) & 1));
+        }
     }
   } else if (warp == 1) {
     // ── MMA ──
@@ -311,6 +323,9 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
         if (!ok) break;
         tc_commit(smem_u32(&tfull[a]));
       }
+      // every MMA issued has finished before TMEM is freed
+      tc_commit(smem_u32(idle));
+      drain_phase(smem_u32(idle), 0);
     }
   } else if (warp < 6) {
     // ── epilogue: ReLU, bf16, NHWC rows ──
