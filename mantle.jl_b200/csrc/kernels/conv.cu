@@ -461,6 +461,240 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols) : "memory");
 }
 
+// ── two M tiles per CTA over flat im2col runs (A_IM2COL, Cout % 256 == 0) ──
+// These layers wait on their loads, not on the tensor core: with four 48 KiB
+// stages in flight a K block took about 950 cycles against 512 of MMAs (the
+// loads' latency under load, about 2 us, over the bytes in flight). A CTA
+// here computes 256 pixels x 256 channels: per K block it loads two 128-pixel
+// A runs and ONE 256-channel weight block (64 KiB, three stages) and issues
+// eight N = 256 MMAs, so the same bytes in flight carry half again as many
+// MACs. The two accumulators (pixels 0-127 and 128-255 of the tile) fill the
+// 512 TMEM columns, so a tile's epilogue does not overlap the next tile.
+constexpr int kM2Stages = 3;
+constexpr uint32_t kM2B = 64 * 256 * 2;               // one K block of 256 output channels
+constexpr uint32_t kM2Stage = 2 * kConvA + kM2B;      // 64 KiB
+constexpr int kM2Smem = kM2Stages * (int)kM2Stage + 2048;
+constexpr uint32_t kM2Idesc = idesc_bf16_f32(128, 256, false, true);
+
+__global__ void __launch_bounds__(192, 1)
+    conv_m2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+                   __nv_bfloat16* __restrict__ out, const ConvShape sh, int relu) {
+  constexpr int S = kM2Stages;
+  extern __shared__ unsigned char msm_raw[];
+  unsigned char* ring =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(msm_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S * kM2Stage);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 1;
+  uint64_t* idle = bars + 2 * S + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tiles_m = (int)((sh.mtot + 255) / 256);
+  const int tiles_n = sh.cout / 256;
+  const int64_t ntiles = (int64_t)tiles_m * tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), 1);
+    }
+    mbar_init(smem_u32(tfull), 1);
+    mbar_init(smem_u32(tempty), 4);
+    mbar_init(smem_u32(idle), 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  // tile t -> first pixel m0 (256 a tile) and column offset n0, grouped 16 M
+  // tiles at a time (the weight blocks of one column range stay in L2)
+  auto coord = [&](int64_t t, int64_t& m0, int& n0) {
+    const int r = (int)t;
+    const int group = r / (kConvGroupM * tiles_n);
+    const int first_m = group * kConvGroupM;
+    const int gsize = min(kConvGroupM, tiles_m - first_m);
+    const int in_group = r % (kConvGroupM * tiles_n);
+    m0 = (int64_t)(first_m + in_group % gsize) * 256;
+    n0 = (in_group / gsize) * 256;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int64_t loads = 0;
+      const int cblocks = sh.cin / 64;
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        int64_t m0;
+        int n0;
+        coord(t, m0, n0);
+        // the two 128-pixel runs: im2col base corners (a run past the last
+        // pixel is not loaded; its rows are never stored)
+        int bw[2], bh[2], img[2];
+        bool has[2];
+        for (int hf = 0; hf < 2; ++hf) {
+          const int64_t mr = m0 + hf * 128;
+          has[hf] = mr < sh.mtot;
+          img[hf] = 0;
+          int oh = 0, ow = 0;
+          if (has[hf]) {
+            img[hf] = (int)(mr / ((int64_t)sh.ho * sh.wo));
+            const int rem = (int)(mr - (int64_t)img[hf] * sh.ho * sh.wo);
+            oh = rem / sh.wo;
+            ow = rem - oh * sh.wo;
+          }
+          bw[hf] = ow * sh.stride - sh.pad + sh.wpad;
+          bh[hf] = oh * sh.stride - sh.pad;
+        }
+        int tap = 0, cb = 0;
+        for (int kb = 0; kb < sh.kblocks; ++kb) {
+          if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto w_done;
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, kM2B + (has[0] ? kConvA : 0u) + (has[1] ? kConvA : 0u));
+          const uint32_t a_dst = smem_u32(ring + s * kM2Stage);
+          const int r = tap / sh.k, c = tap - (tap / sh.k) * sh.k;
+          for (int hf = 0; hf < 2; ++hf)
+            if (has[hf])
+              tma_load_im2col_4d(a_dst + hf * kConvA, &tmA, cb * 64, bw[hf], bh[hf], img[hf], (uint16_t)c,
+                                 (uint16_t)r, fb);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            tma_load_3d(a_dst + 2 * kConvA + q * 8192, &tmW, n0 + q * 64, kb * 64, 0, fb);
+          if (++cb == cblocks) {
+            cb = 0;
+            ++tap;
+          }
+          ++loads;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    w_done:
+      for (int u = 0; u < S && u < loads; ++u) {
+        const int64_t g = loads - 1 - u;
+        drain_phase(smem_u32(&full[g % S]), (uint32_t)((g / S) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      const uint32_t ring0 = smem_u32(ring);
+      const uint64_t a0 = smem_desc(ring0, 16, 1024);
+      const uint64_t b0 = smem_desc(ring0 + 2 * kConvA, 64 * 128, 1024);
+      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        if (!wait_phase(smem_u32(tempty), (i & 1) ^ 1, abort, &g_conv_timeouts)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < sh.kblocks; ++kb) {
+          if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t so = (uint64_t)((s * kM2Stage) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t b = b0 + so + kk * 128;
+            if (kk == 0) {
+              tc_mma(tmem, a0 + so, b, kM2Idesc, kb != 0);
+              tc_mma(tmem + 256, a0 + so + (kConvA >> 4), b, kM2Idesc, kb != 0);
+            } else {
+              tc_mma_acc(tmem, a0 + so + kk * 2, b, kM2Idesc);
+              tc_mma_acc(tmem + 256, a0 + so + (kConvA >> 4) + kk * 2, b, kM2Idesc);
+            }
+          }
+          tc_commit(smem_u32(&empty[s]));
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(tfull));
+      }
+      tc_commit(smem_u32(idle));
+      drain_phase(smem_u32(idle), 0);
+    }
+  } else {
+    // ── epilogue: each thread two pixels (its TMEM lane in both accumulators) ──
+    const int q = warp & 3;
+    int i = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      if (!wait_phase(smem_u32(tfull), i & 1, abort, &g_conv_timeouts)) break;
+      tc_fence_after();
+      int64_t m0;
+      int n0;
+      coord(t, m0, n0);
+      for (int hf = 0; hf < 2; ++hf) {
+        int64_t m = m0 + hf * 128 + q * 32 + lane;
+        const bool mok = m < sh.mtot;
+        int x = 0;
+        if (sh.owp && mok) {
+          const int img = (int)(m / ((int64_t)sh.ho * sh.wo));
+          const int rem = (int)(m - (int64_t)img * sh.ho * sh.wo);
+          const int y = rem / sh.wo;
+          x = rem - y * sh.wo;
+          m = ((int64_t)img * sh.ho + y) * sh.wso + sh.owp + x;  // stored output pixel
+        }
+        const int margin = sh.owp && mok && (x == 0 || x == sh.wo - 1) ? (x == 0 ? -1 : 1) : 0;
+        __nv_bfloat16* orow = out + m * sh.cout + n0;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * 256);
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          if (mok) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int v = 0; v < 16; ++v) {
+              float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+              if (relu) {
+                x0 = fmaxf(x0, 0.f);
+                x1 = fmaxf(x1, 0.f);
+              }
+              __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+              pk[v] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            for (int e = 1; margin && e <= sh.owp; ++e) {
+              uint4* z = reinterpret_cast<uint4*>(orow + (int64_t)margin * e * sh.cout + c * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) z[v] = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(tempty));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+}
+
 // ── stride-1 convolution over a flat halo (A_HALO) ──
 // For stride 1 with the input stored with `pad` zero columns on each side,
 // output pixel (y, x) at stored position q = y*ws + x + pad reads, for filter
@@ -1612,6 +1846,26 @@ static cudaError_t launch_halo(const CUtensorMap& tw, const HaloMaps& ta, void* 
   return cudaGetLastError();
 }
 
+// Whether two 128-pixel runs per CTA beat one for a 256-wide im2col layer:
+// a two-run tile takes about 1.7 times a one-run tile (measured on the
+// 14x14x256 and 7x7x512 layers at batch 256), so it pays when halving the
+// tile count saves a whole round of tiles over the SMs.
+static bool m2_pays(const ConvShape& sh, int sm_count) {
+  const int64_t t1 = (sh.mtot + 127) / 128 * (sh.cout / 256), t2 = (sh.mtot + 255) / 256 * (sh.cout / 256);
+  const int64_t r1 = (t1 + sm_count - 1) / sm_count, r2 = (t2 + sm_count - 1) / sm_count;
+  return 1.7 * (double)r2 < (double)r1;
+}
+
+static cudaError_t launch_m2(const CUtensorMap& tw, const CUtensorMap& ta, void* out, const ConvShape& sh, int relu,
+                             int sm_count, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(conv_m2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kM2Smem);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((sh.mtot + 255) / 256) * (sh.cout / 256);
+  const int grid = (int)std::min<int64_t>(tiles, sm_count);
+  conv_m2_kernel<<<grid, 192, kM2Smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  return cudaGetLastError();
+}
+
 template <int AM>
 static cudaError_t launch_conv_bn(int bn, const CUtensorMap& tw, const CUtensorMap& ta, const void* in, void* out,
                                   const ConvShape& sh, int relu, int sm_count, cudaStream_t s) {
@@ -1849,6 +2103,11 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
                                     : launch_halo<64, true>(tw, maps, out, hs, relu, la.sm_count, s))
                        : (bn == 128 ? launch_halo<128, false>(tw, maps, out, hs, relu, la.sm_count, s)
                                     : launch_halo<64, false>(tw, maps, out, hs, relu, la.sm_count, s));
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
+  if (am == A_IM2COL && BN == 256 && m2_pays(sh, la.sm_count)) {
+    cudaError_t e = launch_m2(tw, ta, out, sh, relu, la.sm_count, s);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }

@@ -79,6 +79,8 @@ def _rand_bits(rng, shape, scale=1.0, nonneg=False):
     (6, 14, 14, 256, 512, 3, 2, 1),   # im2col; 7x7 outputs, BN = 256
     (3, 7, 7, 512, 512, 3, 1, 0),     # im2col; 7x7 in and out, no ReLU
     (100, 14, 14, 128, 512, 3, 1, 1),  # im2col; 154 M tiles, two column tiles each, several per CTA
+    (195, 7, 7, 512, 512, 3, 1, 1),   # im2col, two 128-pixel runs per CTA (150 one-run tiles > 148 SMs);
+                                      # the last tile's second run past the end
     (2, 112, 96, 8, 64, 7, 2, 1),     # 8-channel im2col (the stem's shape)
     (3, 61, 45, 8, 128, 7, 2, 1),     # 8-channel im2col; odd sizes
 ])
