@@ -296,11 +296,28 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
     tp = ROOT / "profiles" / "scatter_add_traffic.json"
     if tp.exists():
         traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    # What bounds it in practice: the shared-memory atomics. The same call with
+    # 2^12 bins (one CTA holds every bin: no cluster, no redundant streaming)
+    # over the same 2^24 values and uniform indices is the atomic floor.
+    gen = torch.Generator(device=f"cuda:{local}").manual_seed(1234)
+    idx_small = torch.randint(0, 1 << 12, (w.n,), generator=gen, device=f"cuda:{local}", dtype=torch.int32)
+    acc_small = torch.zeros(1 << 12, device=f"cuda:{local}")
+    hist_small = torch.zeros(1 << 12, dtype=torch.int32, device=f"cuda:{local}")
+    fargs = (acc_small, hist_small, B["va"], idx_small, 1 << 12, 0)
+    fws = torch.empty(max(M.workspace_bytes(M.kernels.scatter_add, fargs, w.n), 16), dtype=torch.uint8,
+                      device=f"cuda:{local}")
+    flaunch = lambda: M.launch(M.kernels.scatter_add, fargs, w.n, stream=stream, workspace=fws)  # noqa: E731
+    for _ in range(3):
+        flaunch()
+    floor_ms = device_time_ms(stream, flaunch, kreps) / kreps
     roofline = {"bound": "hbm", "kernel": "scatter_add (scatter a: 2^24 values -> 2^16 bins + histogram)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                 "algorithmic_bytes": algo_bytes, "peak_kind": f"{peak_kind} (burst copy)",
-                "kernel_ms": round(k_ms, 4)}
+                "kernel_ms": round(k_ms, 4),
+                "atomic_floor_ms": round(floor_ms, 4),
+                "frac_of_atomic_floor": round(floor_ms / k_ms, 4),
+                "atomic_floor": "the same call with 2^12 bins (all bins in one CTA's shared memory), measured here"}
 
     # End to end through the public API: each step the four input arrays go
     # from pinned host memory through Update, the graph replays, and the bins
@@ -397,7 +414,8 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
                    "l2": f"{copies} copies of the graph (4 x 64 MiB) replayed in turn: inputs larger than the L2"},
         "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None},
+                     "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
+                     "timed": "the whole replay (one graph launch per step, the gap between replays included)"},
         "e2e": e2e, "gpu_launches": nk * args.steps, "clocks": clk.summary(),
     }
     return line
