@@ -740,6 +740,84 @@ __host__ __device__ inline uint32_t halo_smem_bytes(const ConvShape& sh, uint32_
   return 1024 + (uint32_t)sh.kblocks * bblock + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 256;
 }
 
+// The epilogue of one halo tile (t-th of the grid), accumulator a, this
+// warp's 32 rows (lane quarter q): ReLU, bf16, NHWC stores and margin zeros.
+template <int BN, bool PH>
+__device__ __forceinline__ void halo_store_tile(const ConvShape& sh, uint32_t tmem, int a, int q, int lane, int64_t t,
+                                                __nv_bfloat16* __restrict__ out, int n0, int relu) {
+  const int pitch = PH ? sh.pq : sh.ws;
+  const int grid_pos = sh.h * sh.ws;  // stride 1: positions of one image's stored grid
+  const int img = (int)(t / sh.halo_tiles);
+  const int tt = (int)(t - (int64_t)img * sh.halo_tiles);
+  const int m = q * 32 + lane;
+  // the output pixel of MMA row m, and whether it is one
+  int y, xo;
+  bool inner;
+  if (PH) {
+    const int row = m / pitch;
+    y = tt * sh.ph_rows + row;
+    xo = m - row * pitch;
+    inner = row < sh.ph_rows && y < sh.ho && xo < sh.wo;
+  } else {
+    const int pos = tt * 128 + m;  // stored position
+    y = pos / pitch;
+    xo = pos - y * pitch - sh.pad;
+    inner = pos < grid_pos && xo >= 0 && xo < sh.wo;
+  }
+  // Where the row goes (-1: nowhere) and the margin pixels it zeros:
+  //   stride 1 with margins == padding: every stored position of the
+  //     image, zeros at the margins;
+  //   otherwise the output pixel with `owp` margins, the first and last
+  //     pixel of a row also zeroing that row's margin (owp <= 1 here).
+  int64_t dpos = -1, zpos = -1, zpos2 = -1;
+  if (!PH && sh.owp) {
+    const int pos = tt * 128 + m;
+    if (pos < grid_pos) {
+      if (inner)
+        dpos = (int64_t)img * grid_pos + pos;
+      else
+        zpos = (int64_t)img * grid_pos + pos;
+    }
+  } else if (inner) {
+    const int64_t rowb = ((int64_t)img * sh.ho + y) * sh.wso;
+    dpos = rowb + sh.owp + xo;
+    if (sh.owp && xo == 0) zpos = rowb;
+    if (sh.owp && xo == sh.wo - 1) zpos2 = rowb + sh.owp + sh.wo;
+  }
+  const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+  __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tbase + c * 32, r);
+    if (dpos >= 0) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int v = 0; v < 16; ++v) {
+        float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+        if (relu) {
+          x0 = fmaxf(x0, 0.f);
+          x1 = fmaxf(x1, 0.f);
+        }
+        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        pk[v] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(drow + c * 32);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+    }
+  }
+  // margin pixels: zeros over this column block
+#pragma unroll 1
+  for (int zz = 0; zz < 2; ++zz) {
+    const int64_t zp = zz ? zpos2 : zpos;
+    if (zp < 0) continue;
+    uint4* z = reinterpret_cast<uint4*>(out + zp * sh.cout + n0);
+#pragma unroll
+    for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
 // Taps of phase plane p = 2 * row parity + column parity for a 3x3 stride-2
 // filter with padding 1: row parity 0 holds filter row 1, parity 1 rows 0 and
 // 2 (row 0 one plane row up); columns likewise (column 0 one plane column
@@ -956,80 +1034,11 @@ __global__ void __launch_bounds__(224, 1)
   } else if (warp < 6) {
     const int q = warp & 3;
     int i = 0;
-    const int grid_pos = sh.h * sh.ws;  // stride 1: positions of one image's stored grid
     for (int64_t t = first; t < mtiles; t += step, ++i) {
       const int a = i & 3;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
-      const int img = (int)(t / sh.halo_tiles);
-      const int tt = (int)(t - (int64_t)img * sh.halo_tiles);
-      const int m = q * 32 + lane;
-      // the output pixel of MMA row m, and whether it is one
-      int y, xo;
-      bool inner;
-      if (PH) {
-        const int row = m / pitch;
-        y = tt * sh.ph_rows + row;
-        xo = m - row * pitch;
-        inner = row < sh.ph_rows && y < sh.ho && xo < sh.wo;
-      } else {
-        const int pos = tt * 128 + m;  // stored position
-        y = pos / pitch;
-        xo = pos - y * pitch - sh.pad;
-        inner = pos < grid_pos && xo >= 0 && xo < sh.wo;
-      }
-      // Where the row goes (-1: nowhere) and the margin pixels it zeros:
-      //   stride 1 with margins == padding: every stored position of the
-      //     image, zeros at the margins;
-      //   otherwise the output pixel with `owp` margins, the first and last
-      //     pixel of a row also zeroing that row's margin (owp <= 1 here).
-      int64_t dpos = -1, zpos = -1, zpos2 = -1;
-      if (!PH && sh.owp) {
-        const int pos = tt * 128 + m;
-        if (pos < grid_pos) {
-          if (inner)
-            dpos = (int64_t)img * grid_pos + pos;
-          else
-            zpos = (int64_t)img * grid_pos + pos;
-        }
-      } else if (inner) {
-        const int64_t rowb = ((int64_t)img * sh.ho + y) * sh.wso;
-        dpos = rowb + sh.owp + xo;
-        if (sh.owp && xo == 0) zpos = rowb;
-        if (sh.owp && xo == sh.wo - 1) zpos2 = rowb + sh.owp + sh.wo;
-      }
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
-      __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        if (dpos >= 0) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int v = 0; v < 16; ++v) {
-            float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
-            if (relu) {
-              x0 = fmaxf(x0, 0.f);
-              x1 = fmaxf(x1, 0.f);
-            }
-            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-            pk[v] = *reinterpret_cast<uint32_t*>(&h);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(drow + c * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-        }
-      }
-      // margin pixels: zeros over this column block
-#pragma unroll 1
-      for (int zz = 0; zz < 2; ++zz) {
-        const int64_t zp = zz ? zpos2 : zpos;
-        if (zp < 0) continue;
-        uint4* z = reinterpret_cast<uint4*>(out + zp * sh.cout + n0);
-#pragma unroll
-        for (int v = 0; v < BN / 8; ++v) z[v] = make_uint4(0, 0, 0, 0);
-      }
+      halo_store_tile<BN, PH>(sh, tmem, a, q, lane, t, out, n0, relu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
