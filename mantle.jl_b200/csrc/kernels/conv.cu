@@ -909,8 +909,9 @@ __global__ void __launch_bounds__(224, 1)
       uint32_t ph = 0;
       int64_t loads = 0;
       for (int64_t t = first; t < mtiles; t += step) {
-        const int img = (int)(t / sh.halo_tiles);
-        const int tt = (int)(t - (int64_t)img * sh.halo_tiles);
+        const int64_t tg = PH ? mtiles - 1 - t : t;  // the grid tile (stride 2: last image first)
+        const int img = (int)(tg / sh.halo_tiles);
+        const int tt = (int)(tg - (int64_t)img * sh.halo_tiles);
         for (int cb = 0; cb < cblocks; ++cb)
           for (int p = 0; p < kLoads; ++p) {
             if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto p_done;
@@ -1038,7 +1039,7 @@ __global__ void __launch_bounds__(224, 1)
       const int a = i & 3;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
-      halo_store_tile<BN, PH>(sh, tmem, a, q, lane, t, out, n0, relu);
+      halo_store_tile<BN, PH>(sh, tmem, a, q, lane, PH ? mtiles - 1 - t : t, out, n0, relu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
