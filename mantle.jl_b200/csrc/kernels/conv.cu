@@ -54,6 +54,7 @@ struct ConvShape {
   // A_HALO: halo rows per channel block, tiles per image, A stages and their
   // bytes, column blocks (Cout / BN)
   int halo_rows, halo_tiles, halo_stages, halo_stage_bytes, nblk;
+  int halo_stg;  // the halo epilogue stages its stores (2 KiB per epilogue warp after the barriers)
   int taps, cpt;  // kh*kw; 16-byte chunks per pixel (cin / 8)
   int kblocks;    // ceil(taps * cin / 64)
   int64_t mtot;   // n * ho * wo
@@ -737,14 +738,16 @@ struct HaloCfg {
 };
 
 __host__ __device__ inline uint32_t halo_smem_bytes(const ConvShape& sh, uint32_t bblock) {
-  return 1024 + (uint32_t)sh.kblocks * bblock + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 256;
+  return 1024 + (uint32_t)sh.kblocks * bblock + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 256 +
+         (sh.halo_stg ? 4 * 2048 : 0);
 }
 
 // The epilogue of one halo tile (t-th of the grid), accumulator a, this
 // warp's 32 rows (lane quarter q): ReLU, bf16, NHWC stores and margin zeros.
 template <int BN, bool PH>
 __device__ __forceinline__ void halo_store_tile(const ConvShape& sh, uint32_t tmem, int a, int q, int lane, int64_t t,
-                                                __nv_bfloat16* __restrict__ out, int n0, int relu) {
+                                                __nv_bfloat16* __restrict__ out, int n0, int relu,
+                                                unsigned char* stg) {
   const int pitch = PH ? sh.pq : sh.ws;
   const int grid_pos = sh.h * sh.ws;  // stride 1: positions of one image's stored grid
   const int img = (int)(t / sh.halo_tiles);
@@ -786,8 +789,43 @@ __device__ __forceinline__ void halo_store_tile(const ConvShape& sh, uint32_t tm
   }
   const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
   __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
+  if (stg) {
+    // Per 32-channel chunk: each lane puts its pixel's 64 bytes in the warp's
+    // staging rows (16-byte unit v of row l at v ^ ((l >> 1) & 3): no bank
+    // conflicts), then four lanes per pixel store whole 64-byte runs, eight
+    // pixels an instruction, instead of 32 pixel rows touched per instruction.
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tbase + c * 32, r);
+      uint32_t pk[16];
+#pragma unroll
+      for (int v = 0; v < 16; ++v) {
+        float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+        if (relu) {
+          x0 = fmaxf(x0, 0.f);
+          x1 = fmaxf(x1, 0.f);
+        }
+        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        pk[v] = *reinterpret_cast<uint32_t*>(&h);
+      }
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        *reinterpret_cast<uint4*>(stg + lane * 64 + ((v ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int p = it * 8 + (lane >> 2), u = lane & 3;
+        const long long dp = __shfl_sync(0xffffffffu, (long long)dpos, p);
+        const uint4 val = *reinterpret_cast<const uint4*>(stg + p * 64 + ((u ^ ((p >> 1) & 3)) << 4));
+        if (dp >= 0) reinterpret_cast<uint4*>(out + dp * sh.cout + n0 + c * 32)[u] = val;
+      }
+      __syncwarp();
+    }
+  }
+#pragma unroll 1
+  for (int c = 0; c < (stg ? 0 : BN / 32); ++c) {
     uint32_t r[32];
     tmem_ld32(tbase + c * 32, r);
     if (dpos >= 0) {
@@ -854,6 +892,7 @@ __global__ void __launch_bounds__(224, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 27);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* prog = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2] loads each issuer has waited for
+  unsigned char* stg_base = reinterpret_cast<unsigned char*>(bars) + 256;  // [4] x 2 KiB epilogue staging
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int cblocks = sh.cin / 64;
@@ -1039,7 +1078,8 @@ __global__ void __launch_bounds__(224, 1)
       const int a = i & 3;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 2) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
-      halo_store_tile<BN, PH>(sh, tmem, a, q, lane, PH ? mtiles - 1 - t : t, out, n0, relu);
+      halo_store_tile<BN, PH>(sh, tmem, a, q, lane, PH ? mtiles - 1 - t : t, out, n0, relu,
+                              sh.halo_stg ? stg_base + q * 2048 : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
@@ -1944,6 +1984,8 @@ static int halo_plan(ConvShape& sh) {
     const int64_t avail = 232448 - 1024 - 256 - (int64_t)kblocks * 64 * bn * 2;
     const int stages = (int)std::min<int64_t>(max_stages, avail / stage);
     if (stages < 2) continue;
+    // staged epilogue stores where the 8 KiB of staging cost no stage
+    sh.halo_stg = std::min<int64_t>(max_stages, (avail - 4 * 2048) / stage) == stages;
     sh.kblocks = kblocks;
     sh.halo_rows = rows;
     sh.halo_tiles = tiles;
