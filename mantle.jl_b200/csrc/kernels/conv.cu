@@ -103,6 +103,41 @@ enum AMode {
 };
 __host__ __device__ constexpr bool is_rect(int am) { return am == A_RECT || am == A_WINDOW4_RECT; }
 
+// One 32-channel chunk of a warp's 32 output rows: lane l's 64 bytes (pk)
+// go to dst (null: this row is not stored) through the warp's 2 KiB of
+// staging (16-byte unit v of row l at v ^ ((l >> 1) & 3): no bank conflicts),
+// then four lanes per row store whole 64-byte runs, eight rows an instruction,
+// instead of every lane writing its own row (32 lines per instruction).
+__device__ __forceinline__ void stage_store_chunk(unsigned char* stg, int lane, uint4* dst, const uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int v = 0; v < 4; ++v)
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((v ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int p = it * 8 + (lane >> 2), u = lane & 3;
+    uint4* d = reinterpret_cast<uint4*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), p));
+    const uint4 val = *reinterpret_cast<const uint4*>(stg + p * 64 + ((u ^ ((p >> 1) & 3)) << 4));
+    if (d) d[u] = val;
+  }
+  __syncwarp();
+}
+
+// ReLU and bf16 of 32 fp32 accumulator columns, as 16 packed pairs.
+__device__ __forceinline__ void pack_bf16x32(const uint32_t (&r)[32], int relu, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int v = 0; v < 16; ++v) {
+    float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
+    if (relu) {
+      x0 = fmaxf(x0, 0.f);
+      x1 = fmaxf(x1, 0.f);
+    }
+    __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    pk[v] = *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
 template <int BN, int AM>
 struct ConvCfg {
   static constexpr uint32_t kB = 64 * BN * 2;
@@ -368,16 +403,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
         tmem_ld32(tbase + c * 32, r);
         if (mok) {
           uint32_t pk[16];
-#pragma unroll
-          for (int v = 0; v < 16; ++v) {
-            float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
-            if (relu) {
-              x0 = fmaxf(x0, 0.f);
-              x1 = fmaxf(x1, 0.f);
-            }
-            __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-            pk[v] = *reinterpret_cast<uint32_t*>(&h);
-          }
+          pack_bf16x32(r, relu, pk);
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
@@ -664,16 +690,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(tbase + c * 32, r);
           if (mok) {
             uint32_t pk[16];
-#pragma unroll
-            for (int v = 0; v < 16; ++v) {
-              float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
-              if (relu) {
-                x0 = fmaxf(x0, 0.f);
-                x1 = fmaxf(x1, 0.f);
-              }
-              __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-              pk[v] = *reinterpret_cast<uint32_t*>(&h);
-            }
+            pack_bf16x32(r, relu, pk);
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
             for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
@@ -790,38 +807,12 @@ __device__ __forceinline__ void halo_store_tile(const ConvShape& sh, uint32_t tm
   const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
   __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
   if (stg) {
-    // Per 32-channel chunk: each lane puts its pixel's 64 bytes in the warp's
-    // staging rows (16-byte unit v of row l at v ^ ((l >> 1) & 3): no bank
-    // conflicts), then four lanes per pixel store whole 64-byte runs, eight
-    // pixels an instruction, instead of 32 pixel rows touched per instruction.
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
+      uint32_t r[32], pk[16];
       tmem_ld32(tbase + c * 32, r);
-      uint32_t pk[16];
-#pragma unroll
-      for (int v = 0; v < 16; ++v) {
-        float x0 = __uint_as_float(r[2 * v]), x1 = __uint_as_float(r[2 * v + 1]);
-        if (relu) {
-          x0 = fmaxf(x0, 0.f);
-          x1 = fmaxf(x1, 0.f);
-        }
-        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-        pk[v] = *reinterpret_cast<uint32_t*>(&h);
-      }
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        *reinterpret_cast<uint4*>(stg + lane * 64 + ((v ^ ((lane >> 1) & 3)) << 4)) =
-            make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-      __syncwarp();
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int p = it * 8 + (lane >> 2), u = lane & 3;
-        const long long dp = __shfl_sync(0xffffffffu, (long long)dpos, p);
-        const uint4 val = *reinterpret_cast<const uint4*>(stg + p * 64 + ((u ^ ((p >> 1) & 3)) << 4));
-        if (dp >= 0) reinterpret_cast<uint4*>(out + dp * sh.cout + n0 + c * 32)[u] = val;
-      }
-      __syncwarp();
+      pack_bf16x32(r, relu, pk);
+      stage_store_chunk(stg, lane, dpos >= 0 ? reinterpret_cast<uint4*>(drow + c * 32) : nullptr, pk);
     }
   }
 #pragma unroll 1
