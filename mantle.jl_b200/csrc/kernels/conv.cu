@@ -1166,9 +1166,11 @@ __host__ __device__ inline uint32_t rows_raw_bytes(const ConvShape& sh, int src_
 }
 
 // Two MMA-issuing warps (1 and kRowsIssuer2) take alternate output rows of
-// each stage, each with two of the four TMEM accumulators.
+// each stage, each with two of the four TMEM accumulators. From NCHW input two
+// converter warps (6 and 8) take alternate rows of each stage (one converter
+// was busy 94 % of the time, the issuers waiting 17 % for its rows).
 template <int SRC_C>
-constexpr int rows_threads() { return SRC_C ? 256 : 224; }
+constexpr int rows_threads() { return SRC_C ? 288 : 224; }
 
 template <int CIN, int KT, int SRC_C>  // KT: the filter size when known at compile time (its interior rows fully unrolled), else 0
 __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
@@ -1207,7 +1209,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&full[i]), SRC_C ? 2 : 1);  // the two converters, or the producer's load
       mbar_init(smem_u32(&empty[i]), 2);
     }
     for (int a = 0; a < 4; ++a) {
@@ -1217,7 +1219,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
     mbar_init(smem_u32(bfull), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&raw_full[b]), 1);
-      mbar_init(smem_u32(&raw_empty[b]), 1);
+      mbar_init(smem_u32(&raw_empty[b]), 2);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1343,8 +1345,10 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
         }
       }
     }
-  } else if (SRC_C && warp == 6) {
-    // ── converter: raw channel-plane rows -> the stage's padded NHWC rows ──
+  } else if (SRC_C && (warp == 6 || warp == 8)) {
+    // ── converters: raw channel-plane rows -> the stage's padded NHWC rows,
+    // warp 6 the even rows of a stage, warp 8 the odd ones ──
+    const int half = warp == 6 ? 0 : 1;
     int s = 0, rb = 0;
     uint32_t ph = 0, rph = 0;
     for (int64_t u = first; u < units; u += step) {
@@ -1362,7 +1366,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
       unsigned char* dst = astage + (size_t)s * sh.halo_stage_bytes + (size_t)(lo - r0) * rowbytes;
       const int quads = sh.w / 4;
       const size_t plane = (size_t)hrows * sh.w * 2;
-      for (int j = 0; j < hi - lo; ++j) {
+      for (int j = half; j < hi - lo; j += 2) {
         const unsigned char* srow = src + (size_t)j * sh.w * 2;
         unsigned char* drow = dst + (size_t)j * rowbytes;
         for (int m = lane; m < quads; m += 32) {
