@@ -1090,10 +1090,12 @@ __global__ void __launch_bounds__(224, 1)
 // shared stores) into `stage` (1024-byte aligned, BN/64 x 4 KiB), then lane 0
 // stores each chunk with one TMA store of box {64, 32, 1} at (c0 + 64*chunk,
 // c1, c2); rows past the map's second extent are clipped by the TMA. The
-// caller alternates two staging buffers per warp and calls
-// epi_stage_acquire() before reusing one.
+// caller takes kRowsStg staging buffers per warp in turn and calls
+// epi_stage_acquire() before reusing one (three: with two the stem's epilogue
+// warps waited 16 % of their time for a store to finish reading).
+constexpr int kRowsStg = 3;
 __device__ __forceinline__ void epi_stage_acquire(int lane) {
-  if (lane == 0) bulk_wait_read<1>();
+  if (lane == 0) bulk_wait_read<kRowsStg - 1>();
   __syncwarp();
 }
 
@@ -1150,8 +1152,9 @@ __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned
 constexpr int kRowsG = 8;  // output rows per stage
 
 __host__ __device__ inline uint32_t rows_smem_bytes(const ConvShape& sh) {
-  // 1 KiB alignment slack, resident weights, stages, staging (4 warps x 2 x 4 KiB), barriers
-  return 1024 + (uint32_t)sh.kblocks * 8192 + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + 32768 + 256;
+  // 1 KiB alignment slack, resident weights, stages, staging (4 warps x kRowsStg x 4 KiB), barriers
+  return 1024 + (uint32_t)sh.kblocks * 8192 + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) +
+         4 * kRowsStg * 4096 + 256;
 }
 
 // With SRC_C > 0 the input is the network's NCHW tensor with SRC_C <= CIN
@@ -1185,8 +1188,8 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(rsm_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* astage = bres + (size_t)sh.kblocks * 8192;
   const int S = sh.halo_stages;
-  unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [4 warps][2][4 KiB]
-  unsigned char* raw = staging + 32768;                                 // SRC_C: [2][raw bytes]
+  unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [4 warps][kRowsStg][4 KiB]
+  unsigned char* raw = staging + 4 * kRowsStg * 4096;                   // SRC_C: [2][raw bytes]
   const uint32_t raw_bytes = SRC_C ? rows_raw_bytes(sh, SRC_C) : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + 2 * raw_bytes);
   uint64_t* full = bars;         // [S]
@@ -1406,7 +1409,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
   } else if (warp >= 2 && warp < 6) {
     // ── epilogue: one output row per tile, through shared memory and TMA stores ──
     const int q = warp & 3;
-    unsigned char* my_stage = staging + (warp - 2) * 8192;
+    unsigned char* my_stage = staging + (warp - 2) * kRowsStg * 4096;
     int i = 0;
     int cnt[2] = {0, 0};  // tiles seen per issuer
     bool ok = true;
@@ -1421,7 +1424,7 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
           break;
         }
         tc_fence_after();
-        unsigned char* buf = my_stage + (i & 1) * 4096;
+        unsigned char* buf = my_stage + (i % kRowsStg) * 4096;
         epi_stage_acquire(lane);
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
         const int orow = img * sh.ho + oh0 + t;
@@ -2005,7 +2008,8 @@ static bool rows_plan(ConvShape& sh, int src_c = 0) {
   // the last stage row's windows of the 128 tile rows: 127 * 16 + 16 * Cin bytes
   const int64_t stage = (hrows * rowbytes + 127 * 16 + 16 * sh.cin + 1023) & ~int64_t(1023);
   const int kblocks = (sh.k * 8 * sh.cin + 63) / 64;
-  const int64_t avail = 232448 - 1024 - (int64_t)kblocks * 8192 - 32768 - 256 - 2 * (int64_t)rows_raw_bytes(sh, src_c);
+  const int64_t avail =
+      232448 - 1024 - (int64_t)kblocks * 8192 - 4 * kRowsStg * 4096 - 256 - 2 * (int64_t)rows_raw_bytes(sh, src_c);
   const int stages = (int)std::min<int64_t>(4, avail / stage);
   if (stages < 2) return false;
   sh.kblocks = kblocks;
