@@ -808,11 +808,17 @@ __device__ __forceinline__ void halo_store_tile(const ConvShape& sh, uint32_t tm
   __nv_bfloat16* drow = out + (dpos >= 0 ? dpos : 0) * sh.cout + n0;
   if (stg) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32], pk[16];
-      tmem_ld32(tbase + c * 32, r);
-      pack_bf16x32(r, relu, pk);
-      stage_store_chunk(stg, lane, dpos >= 0 ? reinterpret_cast<uint4*>(drow + c * 32) : nullptr, pk);
+    for (int c0 = 0; c0 < BN / 32; c0 += 2) {  // two chunks' TMEM loads in flight before one wait
+      uint32_t rr[2][32];
+      tmem_ld32_nowait(tbase + c0 * 32, rr[0]);
+      tmem_ld32_nowait(tbase + (c0 + 1) * 32, rr[1]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[16];
+        pack_bf16x32(rr[h], relu, pk);
+        stage_store_chunk(stg, lane, dpos >= 0 ? reinterpret_cast<uint4*>(drow + (c0 + h) * 32) : nullptr, pk);
+      }
     }
   }
 #pragma unroll 1
@@ -1102,10 +1108,14 @@ __device__ __forceinline__ void epi_stage_acquire(int lane) {
 template <int BN>
 __device__ __forceinline__ void epi_tma_store(uint32_t tbase, int relu, unsigned char* stage, const CUtensorMap* tmO,
                                               int c0, int c1, int c2, int lane) {
+  // every chunk's TMEM load in flight before one wait
+  uint32_t rr[BN / 32][32];
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) tmem_ld32_nowait(tbase + c * 32, rr[c]);
+  tmem_wait_ld();
 #pragma unroll
   for (int c = 0; c < BN / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(tbase + c * 32, r);
+    const uint32_t (&r)[32] = rr[c];
     uint32_t pk[16];
 #pragma unroll
     for (int v = 0; v < 16; ++v) {
