@@ -203,6 +203,8 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the input (and the output's previous readers) are the last kernel's
+  pdl_trigger();
 
   // Tile t -> M tile and column offset, grouped 16 M tiles at a time. Flat
   // tiles start at pixel m0 = mt * 128; rectangles at (img, oh0, ow0).
@@ -546,6 +548,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the input (and the output's previous readers) are the last kernel's
+  pdl_trigger();
 
   // tile t -> first pixel m0 (256 a tile) and column offset n0, grouped 16 M
   // tiles at a time (the weight blocks of one column range stay in L2)
@@ -931,6 +935,8 @@ __global__ void __launch_bounds__(224, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the input (and the output's previous readers) are the last kernel's
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1248,6 +1254,8 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the input (and the output's previous readers) are the last kernel's
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1546,6 +1554,8 @@ __global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restric
                                                   int hw, int c) {
   extern __shared__ float part[];  // [G][c]
   const int img = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   const int units = c / (2 * V);
   const int G = max(1, min(kGapMaxGroups, (int)blockDim.x / units));
   const __nv_bfloat16* a = act + (int64_t)img * hw * c;
@@ -1607,6 +1617,8 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
   const int kc = (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
   const int kbeg = min(c, z * kc), kend = min(c, kbeg + kc);
   float acc[4][8] = {};
+  pdl_wait();
+  pdl_trigger();
   for (int k0 = kbeg; k0 < kend; k0 += kFcKc) {
     const int kn = min(kFcKc, kend - k0);
     if (vec) {  // kn, C and classes multiples of 4: whole float4s are in or out of range
@@ -1829,9 +1841,8 @@ static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, con
   const int64_t mtiles = is_rect(AM) ? (int64_t)sh.n * sh.tiles_x * sh.tiles_y : (sh.mtot + 127) / 128;
   const int64_t tiles = mtiles * (sh.cout / BN);
   const int grid = (int)std::min<int64_t>(tiles, (int64_t)sm_count * Cfg::kCtasPerSm);
-  conv_bf16_kernel<BN, AM><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(
-      tw, ta, reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
-  return cudaGetLastError();
+  return launch_pdl(conv_bf16_kernel<BN, AM>, grid, Cfg::kThreads, Cfg::kSmem, s, tw, ta,
+                    reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
 }
 
 // The four parity planes of a plain NHWC input for the stride-2 halo path:
@@ -1885,9 +1896,8 @@ static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, con
   const int64_t units = (int64_t)sh.n * ((sh.ho + kRowsG - 1) / kRowsG) * sh.nblk;
   int grid = (int)std::min<int64_t>(units, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_rows_kernel<CIN, KT, SRC_C><<<grid, rows_threads<SRC_C>(), smem, s>>>(
-      tw, to, reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
-  return cudaGetLastError();
+  return launch_pdl(conv_rows_kernel<CIN, KT, SRC_C>, grid, rows_threads<SRC_C>(), smem, s, tw, to,
+                    reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
 }
 
 template <int BN, bool PH>
@@ -1900,8 +1910,8 @@ static cudaError_t launch_halo(const CUtensorMap& tw, const HaloMaps& ta, void* 
   // whole column-block groups: CTA b serves column block b % nblk
   int grid = (int)std::min<int64_t>(tiles, sm_count);
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
-  conv_halo_kernel<BN, PH><<<grid, 224, smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
-  return cudaGetLastError();
+  return launch_pdl(conv_halo_kernel<BN, PH>, grid, 224, smem, s, tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh,
+                    relu);
 }
 
 // Whether two 128-pixel runs per CTA beat one for a 256-wide im2col layer:
@@ -1920,8 +1930,7 @@ static cudaError_t launch_m2(const CUtensorMap& tw, const CUtensorMap& ta, void*
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((sh.mtot + 255) / 256) * (sh.cout / 256);
   const int grid = (int)std::min<int64_t>(tiles, sm_count);
-  conv_m2_kernel<<<grid, 192, kM2Smem, s>>>(tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
-  return cudaGetLastError();
+  return launch_pdl(conv_m2_kernel, grid, 192, kM2Smem, s, tw, ta, reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
 }
 
 template <int AM>
