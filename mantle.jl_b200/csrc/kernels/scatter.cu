@@ -279,6 +279,86 @@ __global__ void scatter_reduce_kernel(const float* __restrict__ ws_acc,
   }
 }
 
+// The same sums with 16-byte loads and many more of them in flight (the
+// one-bin-a-thread form waits on L2 latency): a block takes 128 bins as 32
+// groups of four and splits the clusters eight ways, thread row g summing
+// clusters g, g + 8, ... in order; the eight row sums are then added in row
+// order. The order is fixed, so the result does not depend on scheduling.
+constexpr int kRedSplit = 8, kRedQuads = 32;
+template <bool ACC, bool HIST>
+__global__ void __launch_bounds__(kRedSplit* kRedQuads)
+    scatter_reduce4_kernel(const float4* __restrict__ ws_acc, const uint4* __restrict__ ws_hist, int nclusters,
+                           uint32_t nquads, float4* __restrict__ acc, uint4* __restrict__ hist, int accumulate) {
+  __shared__ float4 ra[kRedSplit][kRedQuads];
+  __shared__ uint4 rh[kRedSplit][kRedQuads];
+  const int q = threadIdx.x % kRedQuads, g = threadIdx.x / kRedQuads;
+  const uint32_t b = blockIdx.x * kRedQuads + q;
+  const bool in = b < nquads;
+  float4 sa = make_float4(0.f, 0.f, 0.f, 0.f);
+  uint4 sh = make_uint4(0u, 0u, 0u, 0u);
+  if (in) {
+#pragma unroll 4
+    for (int c = g; c < nclusters; c += kRedSplit) {
+      const int64_t o = (int64_t)c * nquads + b;
+      if (ACC) {
+        const float4 x = ws_acc[o];
+        sa.x += x.x, sa.y += x.y, sa.z += x.z, sa.w += x.w;
+      }
+      if (HIST) {
+        const uint4 y = ws_hist[o];
+        sh.x += y.x, sh.y += y.y, sh.z += y.z, sh.w += y.w;
+      }
+    }
+  }
+  if (ACC) ra[g][q] = sa;
+  if (HIST) rh[g][q] = sh;
+  __syncthreads();
+  if (g != 0 || !in) return;
+  if (ACC) {
+    float4 t = accumulate ? acc[b] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kRedSplit; ++j) {
+      const float4 x = ra[j][q];
+      t.x += x.x, t.y += x.y, t.z += x.z, t.w += x.w;
+    }
+    acc[b] = t;
+  }
+  if (HIST) {
+    uint4 t = accumulate ? hist[b] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < kRedSplit; ++j) {
+      const uint4 y = rh[j][q];
+      t.x += y.x, t.y += y.y, t.z += y.z, t.w += y.w;
+    }
+    hist[b] = t;
+  }
+}
+
+// The fixed-order sum of the clusters' partial tables into acc / hist: four
+// bins a thread when every table allows 16-byte loads, else one.
+static cudaError_t launch_reduce(cudaStream_t s, const float* ws_acc, const uint32_t* ws_hist, int ncl,
+                                 uint32_t nbins, float* acc, uint32_t* hist, int accumulate) {
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (nbins % 4 == 0 && a16(ws_acc) && a16(ws_hist) && a16(acc) && a16(hist)) {
+    const uint32_t nq = nbins / 4;
+    const unsigned blocks = (nq + kRedQuads - 1) / kRedQuads;
+    const auto* wa = reinterpret_cast<const float4*>(ws_acc);
+    const auto* wh = reinterpret_cast<const uint4*>(ws_hist);
+    auto* oa = reinterpret_cast<float4*>(acc);
+    auto* oh = reinterpret_cast<uint4*>(hist);
+    if (acc && hist)
+      scatter_reduce4_kernel<true, true><<<blocks, kRedSplit * kRedQuads, 0, s>>>(wa, wh, ncl, nq, oa, oh, accumulate);
+    else if (acc)
+      scatter_reduce4_kernel<true, false><<<blocks, kRedSplit * kRedQuads, 0, s>>>(wa, wh, ncl, nq, oa, oh, accumulate);
+    else
+      scatter_reduce4_kernel<false, true><<<blocks, kRedSplit * kRedQuads, 0, s>>>(wa, wh, ncl, nq, oa, oh, accumulate);
+  } else {
+    const unsigned blocks = (nbins + 255) / 256;
+    scatter_reduce_kernel<<<blocks, 256, 0, s>>>(ws_acc, ws_hist, ncl, nbins, acc, hist, accumulate);
+  }
+  return cudaGetLastError();
+}
+
 // Fallback for bin ranges no cluster can hold: atomics on the L2-resident table.
 __global__ void scatter_global_kernel(const float* __restrict__ v, const int* __restrict__ idx,
                                       int64_t n, uint32_t nbins, float* __restrict__ acc,
@@ -398,9 +478,7 @@ mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* 
       ncl = 0;
     }
     if (e == cudaSuccess) {
-      unsigned blocks = (unsigned)((nbins + 255) / 256);
-      scatter_reduce_kernel<<<blocks, 256, 0, s>>>(ws_acc, ws_hist, ncl, nbins, acc, hist, accumulate);
-      e = cudaGetLastError();
+      e = launch_reduce(s, ws_acc, ws_hist, ncl, (uint32_t)nbins, acc, hist, accumulate);
     }
   } else if (sh.cluster) {
     uint64_t need = (uint64_t)sh.nclusters * tables * (uint64_t)nbins * 4;
@@ -421,9 +499,7 @@ mtl_status scatter_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* 
       ncl = 0;
     }
     if (e == cudaSuccess) {
-      unsigned blocks = (unsigned)((nbins + 255) / 256);
-      scatter_reduce_kernel<<<blocks, 256, 0, s>>>(ws_acc, ws_hist, ncl, nbins, acc, hist, accumulate);
-      e = cudaGetLastError();
+      e = launch_reduce(s, ws_acc, ws_hist, ncl, (uint32_t)nbins, acc, hist, accumulate);
     }
   } else {
     if (!accumulate) {

@@ -116,6 +116,27 @@ def test_scatter_alignment_and_histogram_only(dev, offset, with_acc):
         np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
 
 
+@pytest.mark.parametrize("out_offset", [0, 1])  # 0: four bins a thread in the final sum; 1: one
+def test_scatter_accumulates_into_aligned_and_unaligned_tables(dev, out_offset):
+    import torch
+    n, nbins = (1 << 18) + 1, 1 << 16
+    v = seeded_uniform(3, n, 0, 1, 0)
+    idx = seeded_integers(3, n, nbins, 1)
+    base_a = seeded_uniform(3, nbins, -1, 1, 2)
+    base_h = seeded_integers(3, nbins, 1000, 3)
+    acc = torch.zeros(nbins + out_offset, device="cuda")[out_offset:]
+    hist = torch.zeros(nbins + out_offset, dtype=torch.int32, device="cuda")[out_offset:]
+    acc.copy_(torch.from_numpy(base_a))
+    hist.copy_(torch.from_numpy(base_h))
+    args = (acc, hist, torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda(), nbins, 1)
+    ws = torch.empty(M.workspace_bytes(M.kernels.scatter_add, args, n), dtype=torch.uint8, device="cuda")
+    M.launch(M.kernels.scatter_add, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
+    torch.cuda.synchronize()
+    want_a, want_h = O.scatter_f64(v, idx, nbins)
+    assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h + base_h.astype(np.uint32))
+    np.testing.assert_allclose(acc.cpu().numpy(), want_a + base_a, rtol=RTOL, atol=1e-5)
+
+
 def test_scatter_edge_cases(dev):
     nbins = 1000
     # out-of-range indices (negative and >= nbins) are skipped, never written
