@@ -221,7 +221,10 @@ mtl_status ew_launch_compiled(void* kernel, const EwProgram& p, void* stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long groups = n / 4;
-  const long long blocks = std::max<long long>(1, std::min<long long>((groups + 255) / 256, (long long)sms * 4));
+  // one two-group iteration per thread where the grid allows (blocks finish
+  // together; at 4 blocks an SM and 3-4 iterations a thread, 2^22-element
+  // runs took 14.3 us instead of 13.8-14.0), capped at 16 blocks an SM
+  const long long blocks = std::max<long long>(1, std::min<long long>((groups + 511) / 512, (long long)sms * 16));
   cudaError_t e = cudaLaunchKernel((const void*)kernel, dim3((unsigned)blocks), dim3(256), args.data(), 0,
                                    (cudaStream_t)stream);
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "compiled fused run: %s", cudaGetErrorString(e));

@@ -108,6 +108,7 @@ struct ModeGraph {
   std::vector<cudaGraphNode_t> upd_host, upd_dev;
   std::vector<int8_t> upd_host_on, upd_dev_on;
   int nkernels = 0, nedges = 0;
+  std::function<mtl_status(cudaStream_t)> direct;  // set for one-kernel plans (direct_launcher)
 };
 
 struct UpdateRt {
@@ -237,18 +238,25 @@ static mtl_status capture_graph(mtl_plan* pl, const std::function<mtl_status(cud
   return MTL_OK;
 }
 
-static mtl_status capture_dispatch(mtl_plan* pl, const Dispatch& d, cudaGraph_t* out) {
+using Launcher = std::function<mtl_status(cudaStream_t)>;
+
+// What a dispatch launches, with its resources resolved to this plan's memory.
+static Launcher dispatch_launcher(mtl_plan* pl, const Dispatch& d) {
   LaunchArgs la;
   void* ws;
   uint64_t wsb;
   resolve(pl, d, la, &ws, &wsb);
-  int kernel = d.kernel;
-  return capture_graph(pl, [&](cudaStream_t s) { return launch_kernel(kernel, la, ws, wsb, s); }, out);
+  const int kernel = d.kernel;
+  return [kernel, la, ws, wsb](cudaStream_t s) { return launch_kernel(kernel, la, ws, wsb, s); };
+}
+
+static mtl_status capture_dispatch(mtl_plan* pl, const Dispatch& d, cudaGraph_t* out) {
+  return capture_graph(pl, dispatch_launcher(pl, d), out);
 }
 
 // A fused run of elementwise passes (scheduled position p): one program, one
 // kernel. Transients the run keeps in registers are never stored.
-static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
+static mtl_status fused_launcher(mtl_plan* pl, int p, Launcher* out) {
   const mtl_graph* g = pl->g;
   std::vector<EwMember> ms;
   for (int pid : pl->a.steps[p]) {
@@ -278,8 +286,30 @@ static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
     if (st != MTL_OK && st != MTL_ERR_UNSUPPORTED) return st;  // NVRTC present but failing: an error
   }
   if (compiled)
-    return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_compiled(compiled, prog, s); }, out);
-  return capture_graph(pl, [&](cudaStream_t s) { return ew_launch_program(prog, s); }, out);
+    *out = [compiled, prog](cudaStream_t s) { return ew_launch_compiled(compiled, prog, s); };
+  else
+    *out = [prog](cudaStream_t s) { return ew_launch_program(prog, s); };
+  return MTL_OK;
+}
+
+static mtl_status capture_fused(mtl_plan* pl, int p, cudaGraph_t* out) {
+  Launcher f;
+  if (mtl_status s = fused_launcher(pl, p, &f)) return s;
+  return capture_graph(pl, f, out);
+}
+
+// A plan that is one step launching one kernel, with no updates and no
+// profiling, runs that launch directly on the device stream: back-to-back
+// kernel launches leave shorter gaps on the GPU than launches of one-node
+// graphs (measured ~3.5 us between replays of the fused chain's graph).
+static mtl_status direct_launcher(mtl_plan* pl, const ModeGraph& m, Launcher* out) {
+  *out = nullptr;
+  const mtl_graph* g = pl->g;
+  if (pl->a.order.size() != 1 || !g->updates.empty() || pl->o.profile || m.nkernels != 1) return MTL_OK;
+  if (pl->a.steps[0].size() > 1) return fused_launcher(pl, 0, out);
+  const Pass& ps = g->passes[pl->a.order[0]];
+  if (ps.kind == MTL_PASS_COMPUTE && ps.dispatches.size() == 1) *out = dispatch_launcher(pl, ps.dispatches[0]);
+  return MTL_OK;
 }
 
 // Scheduled position of a pass (the step that runs it), or -1.
@@ -421,6 +451,7 @@ static mtl_status build_mode(mtl_plan* pl, int mode) {
     CUDA_TRY(cudaGraphNodeSetEnabled(m.exec, m.upd_dev[u], 0));
     m.upd_host_on[u] = m.upd_dev_on[u] = 0;
   }
+  if (mtl_status st = direct_launcher(pl, m, &m.direct)) return st;
   m.built = true;
   return MTL_OK;
 }
@@ -741,6 +772,7 @@ mtl_status mtl_plan_run(mtl_plan* pl, int32_t barriers) {
   if (mtl_status s = build_mode(pl, mode)) return s;
   ModeGraph& m = pl->modes[mode];
   collect(pl);
+  if (m.direct) return m.direct(d->stream);
 
   auto t0 = std::chrono::steady_clock::now();
   std::vector<int> used_slot(pl->upd.size(), -1);
@@ -846,6 +878,8 @@ mtl_status mtl_plan_set_arg(mtl_plan* pl, int32_t pass, int32_t dispatch, int32_
     cudaError_t e = cudaGraphExecChildGraphNodeSetParams(m.exec, m.dispatch_nodes[pos][fused ? 0 : dispatch], child);
     cudaGraphDestroy(child);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "set_arg: %s", cudaGetErrorString(e));
+    if (m.direct)
+      if (mtl_status s = direct_launcher(pl, m, &m.direct)) return s;
   }
   return MTL_OK;
 }
