@@ -415,7 +415,7 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
         "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
-                     "timed": "the whole replay (one graph launch per step, the gap between replays included)"},
+                     "timed": "the whole run! per step (a one-kernel plan: one kernel launch per step, the gaps between steps included)"},
         "e2e": e2e, "gpu_launches": nk * args.steps, "clocks": clk.summary(),
     }
     return line
