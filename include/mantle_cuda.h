@@ -250,7 +250,9 @@ mtl_status mtl_plan_compile(mtl_graph* g, const mtl_plan_opts* opts, mtl_plan** 
 mtl_status mtl_plan_release(mtl_plan* plan);
 
 enum { MTL_BARRIERS_DERIVED = 0, MTL_BARRIERS_BACKEND = 1, MTL_BARRIERS_BOTH = 2 };
-/* run!(plan; barriers): ext/MantleLavaExt.jl:2076-2128 — one cudaGraphLaunch. */
+/* run!(plan; barriers): ext/MantleLavaExt.jl:2076-2128 — one cudaGraphLaunch on
+ * the device's stream; a plan that is a single kernel, with no updates and no
+ * profiling, launches that kernel directly on the same stream instead. */
 mtl_status mtl_plan_run(mtl_plan* plan, int32_t barriers);
 
 /* UpdateRef(x): ext/MantleLavaExt.jl:776-782. Stores the data for the next

@@ -210,22 +210,32 @@ mtl_status ew_compile(const EwProgram& p, void** kernel) {
 // Launch a compiled program (pointers must be 16-byte aligned).
 mtl_status ew_launch_compiled(void* kernel, const EwProgram& p, void* stream) {
   const int nin = (int)p.inputs.size(), nout = (int)p.outputs.size();
-  std::vector<void*> args;
-  std::vector<uint64_t> ptrs(nin + nout);
+  constexpr int kMaxPtrs = 32;  // well above what ew_program_fits lets through
+  if (nin + nout > kMaxPtrs) return fail(MTL_ERR_UNSUPPORTED, "compiled fused run: too many arguments");
+  // no allocation and no attribute query per launch: a one-kernel plan issues
+  // this for every run!
+  void* args[kMaxPtrs + 1];
+  uint64_t ptrs[kMaxPtrs];
   for (int i = 0; i < nin; ++i) ptrs[i] = p.inputs[i];
   for (int j = 0; j < nout; ++j) ptrs[nin + j] = p.outputs[j];
   long long n = p.n;
-  for (auto& x : ptrs) args.push_back(&x);
-  args.push_back(&n);
-  int dev = 0, sms = 148;
+  for (int i = 0; i < nin + nout; ++i) args[i] = &ptrs[i];
+  args[nin + nout] = &n;
+  static int sm_count[64] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = dev >= 0 && dev < 64 ? sm_count[dev] : 0;
+  if (sms <= 0) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+  }
   const long long groups = n / 4;
   // one two-group iteration per thread where the grid allows (blocks finish
   // together; at 4 blocks an SM and 3-4 iterations a thread, 2^22-element
   // runs took 14.3 us instead of 13.8-14.0), capped at 16 blocks an SM
   const long long blocks = std::max<long long>(1, std::min<long long>((groups + 511) / 512, (long long)sms * 16));
-  cudaError_t e = cudaLaunchKernel((const void*)kernel, dim3((unsigned)blocks), dim3(256), args.data(), 0,
+  cudaError_t e = cudaLaunchKernel((const void*)kernel, dim3((unsigned)blocks), dim3(256), args, 0,
                                    (cudaStream_t)stream);
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "compiled fused run: %s", cudaGetErrorString(e));
   return MTL_OK;

@@ -1,6 +1,7 @@
 // The CUDA side of the backend: devices, persistent buffers, and plans — a
 // compiled Mantle graph lowered to one CUDA graph and replayed with a single
-// cudaGraphLaunch per run!.
+// cudaGraphLaunch per run! (a plan that is one kernel, with no updates and no
+// profiling, launches that kernel directly instead).
 //
 // Lowering (ext/MantleLavaExt.jl:2076-2338 is what it replaces):
 //   * every dispatch becomes a child-graph node captured from its launch(es),
@@ -87,6 +88,8 @@ int device_ordinal(mtl_device* d) { return d ? d->ordinal : -1; }
 
 static mtl_status use_device(mtl_device* d) {
   if (!d) return fail(MTL_ERR_STATE, "no device");
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur == d->ordinal) return MTL_OK;
   CUDA_TRY(cudaSetDevice(d->ordinal));
   return MTL_OK;
 }
