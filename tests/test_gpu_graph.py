@@ -370,6 +370,39 @@ def test_copy_pass(dev):
     assert np.array_equal(c.array(), np.arange(n, dtype=np.float32) * 3)
 
 
+def test_set_arg_reaches_the_next_run(dev):
+    """Plan.set_arg changes a scalar for the next run!, both for a plan that is
+    a single kernel (launched without its graph) and for a fused run."""
+    n = 4096 + 3
+    a_h = seeded_uniform(5, n, -1, 1, 0)
+    b_h = seeded_uniform(5, n, -1, 1, 1)
+    a, b = M.Buffer(dev, a_h), M.Buffer(dev, b_h)
+    c = M.Buffer(dev, np.float32, n)
+    g = M.Graph(dev)
+    p = M.compute(g, "scale", lambda p: M.dispatch(p, M.kernels.scaleby, (
+        M.use(p, c, write=True), M.use(p, a, read=True), 3.0), n))
+    plan = M.Plan(g)
+    M.run(plan)
+    assert np.array_equal(c.array(), a_h * np.float32(3))
+    plan.set_arg(p, 0, 2, -0.5)
+    M.run(plan)
+    assert np.array_equal(c.array(), a_h * np.float32(-0.5))
+
+    t, d = M.Buffer(dev, np.float32, n), M.Buffer(dev, np.float32, n)
+    g2 = M.Graph(dev)
+    q = M.compute(g2, "scale", lambda p: M.dispatch(p, M.kernels.scaleby, (
+        M.use(p, t, write=True), M.use(p, a, read=True), 2.0), n))
+    M.compute(g2, "add", lambda p: M.dispatch(p, M.kernels.add, (
+        M.use(p, d, write=True), M.use(p, t, read=True), M.use(p, b, read=True)), n))
+    plan2 = M.Plan(g2, fuse=True)
+    M.run(plan2)
+    assert plan2.nkernels() == 1
+    np.testing.assert_allclose(d.array(), a_h * 2 + b_h, rtol=1e-6, atol=1e-7)
+    plan2.set_arg(q, 0, 2, 4.0)
+    M.run(plan2)
+    np.testing.assert_allclose(d.array(), a_h * 4 + b_h, rtol=1e-6, atol=1e-7)
+
+
 def test_disjoint_slices_both_land(dev):
     """test/test_window.jl:391-420: two writes into disjoint halves of one buffer
     are not ordered against each other, and both land."""
