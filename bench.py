@@ -41,7 +41,7 @@ sys.path.insert(0, str(ROOT))
 
 import numpy as np  # noqa: E402
 
-BASELINE_METRIC = "replayed-graph GB/s & TFLOP/s vs roofline; DNN images/sec at 1/2/4/8 B200"
+METRIC = "replayed-graph GB/s & TFLOP/s vs roofline; DNN images/sec at 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -354,7 +354,7 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
 
     nk = plan.nkernels()
     line = {
-        "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
         "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
@@ -404,7 +404,7 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
            "h2d_bytes_per_step": t["h2d_bytes_per_step"], "d2h_bytes_per_step": t["d2h_bytes_per_step"],
            "ms_per_step": round(t["seconds"] * 1e3, 3)}
     line = {
-        "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded PCG64, x,y,z U[-1,1]",
@@ -476,7 +476,7 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
                "kind": "port", "sample": f"{reps} x (forward + inverse of 1024 transforms of 4096), "
                                          f"oracle radix-2 in float, OpenMP, {dt:.1f} s"}
     return {
-        "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "c64",
         "data": "synthetic: seeded PCG64, re/im U[-1,1]",
@@ -542,7 +542,7 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
         cpu = {"value": round(done * rows * 2 * w.N * w.K / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
                "kind": "port", "sample": f"{done * rows} rows of one 8192^3 GEMM (oracle, double, OpenMP) in {dt:.1f} s"}
     return {
-        "metric": BASELINE_METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: torch Philox seed 1, normal(0,1)/sqrt(K) rounded to bf16",
@@ -632,7 +632,7 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     if comm is not None:
         comm.release()
     return {
-        "metric": BASELINE_METRIC, "value": round(images_s, 1), "unit": "images/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(images_s, 1), "unit": "images/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: torch Philox, input U[0,1) seed 4, He-normal weights seed 3",
@@ -704,7 +704,7 @@ def bench_showcase(args, ws, rank, local, peaks, peak_kind):
                "sample": f"{frames} frames of the thirteen passes through the oracle (shading and occlusion on "
                          f"OpenMP, the rest one thread) in {dt:.1f} s"}
     return {
-        "metric": BASELINE_METRIC, "value": round(ws * 1e3 / ms_step, 1), "unit": "frames/s", "n_gpus": ws,
+        "metric": METRIC, "value": round(ws * 1e3 / ms_step, 1), "unit": "frames/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded analytic scene (floor + spheres) ray-cast into the g-buffer and shadow map",
@@ -790,7 +790,7 @@ def reference_arm(args, ws, rank):
     dt = time.perf_counter() - t0
     v = nbytes / dt / 1e9
     return {
-        "metric": BASELINE_METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32", "impl": "reference",
         "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
