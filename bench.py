@@ -147,7 +147,8 @@ def max_over_ranks(ws, x: float) -> float:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    # NCCL reduces device tensors; gloo (the CPU tests of this plumbing) host ones
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
