@@ -1,33 +1,43 @@
 #!/usr/bin/env python
 """Benchmark of the Mantle graph hot path on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload all|scatter|chain|fft|gemm|cnn|showcase]
+                    [--impl ours|reference]
 
-A step is one replay (`run`) of the recorded graph of the workload over its
-synthetic inputs. The default workload is the two-scatters-plus-three-updates
-graph: two scatter-adds of 2^24 Float32 values by uniform Int32 index into
-2^16 bins (an Int32 histogram fused into the first), then three in-place
-updates with read-after-write hazards on a Float32[2^20] buffer. `value` is
-whole-job algorithmic GB/s: (16 B per scattered element + 36 B per updated
-element) x ranks / max-over-ranks time per step. The inputs (256 MiB per
-replay) are larger than the 126 MB L2, so no flush is needed between steps;
-the bins and the update buffers are L2-resident by design.
+A step is one replay (`run`) of a workload's recorded graph over its synthetic
+inputs. With no flags (`--workload all`) every config of the benchmark runs in
+turn, K timed steps each, and ONE line is printed:
 
-`--workload chain` runs the eight-kernel elementwise chain (N=2^22) instead.
+* the headline is the two-scatters-plus-three-updates graph: two scatter-adds
+  of 2^24 Float32 values by uniform Int32 index into 2^16 bins (an Int32
+  histogram fused into the first), then three in-place updates with
+  read-after-write hazards on a Float32[2^20] buffer. `value` is whole-job
+  algorithmic GB/s: (16 B per scattered element + 36 B per updated element) x
+  ranks / max-over-ranks time per step. Inputs (256 MiB per replay) exceed
+  the 126 MB L2, so steps replay back to back;
+* `workloads` holds one record per other config, each with its own
+  `value`, `ms_per_step`, `roofline`, `cpu_baseline`, `e2e` and `clocks`:
+  the eight-kernel elementwise chain (N = 2^22), the batched FFT (16384 x
+  4096 ComplexF32, forward then inverse), the dense GEMM (8 x 8192^3 bf16 ->
+  fp32) and the CNN forward (batch 256, 3 x 224 x 224).
 
-Multi-GPU (torchrun, one process per GPU): every rank replays its own
-independent graph on its own seeded data ("scaling": "weak"); no collective
-touches the data path. The barrier and the max-over-ranks reduction of the
-device-timed step go through torch.distributed (NCCL).
+Multi-GPU (torchrun, one process per GPU): the scatter and chain graphs are
+independent per rank ("scaling": "weak"); the GEMM batch, the FFT transforms
+and the CNN images are split across the ranks (`shard_range`, "scaling":
+"strong"), and only the CNN all-gathers its logits over NCCL, every step. The
+barrier and the max-over-ranks reduction of the device-timed steps go through
+torch.distributed.
 
-`--impl reference` times the CPU restatement of the same workload (the oracle,
-C + OpenMP on all host cores) — the reference itself is Julia on Vulkan and
-cannot run here. Under torchrun only rank 0 runs it.
+`--impl reference` times the CPU restatement of the same workloads (the
+oracle, C + OpenMP on all host cores) — the reference itself is Julia on
+Vulkan and cannot run here. Under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
 import argparse
+import gc
 import json
+import math
 import os
 import statistics
 import sys
@@ -43,6 +53,7 @@ import numpy as np  # noqa: E402
 
 METRIC = "replayed-graph GB/s & TFLOP/s vs roofline; DNN images/sec at 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20  # written between steps whose inputs could stay in the 126 MB L2
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -53,6 +64,17 @@ def load_peaks() -> tuple[dict, str]:
         except Exception:
             pass
     return FALLBACK_PEAKS, "fallback"
+
+
+def traffic_of(name: str):
+    """DRAM bytes per launch of a kernel from its committed ncu summary."""
+    tp = ROOT / "profiles" / f"{name}_traffic.json"
+    if tp.exists():
+        try:
+            return json.loads(tp.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
 
 
 # ── clocks during the timed region (NVML, read only) ────────────────────────
@@ -159,6 +181,16 @@ def finish(ws):
         dist.destroy_process_group()
 
 
+def release_device_memory(local: int) -> None:
+    """Between workloads: drop the last one's buffers and plans (their
+    finalizers free the device memory) and torch's cached blocks."""
+    import torch
+    torch.cuda.synchronize(local)
+    gc.collect()
+    torch.cuda.synchronize(local)
+    torch.cuda.empty_cache()
+
+
 # ── timing helpers ──────────────────────────────────────────────────────────
 def device_time_ms(stream_ptr: int, fn, steps: int) -> float:
     """CUDA events on the stream the work is launched on; sync on both sides."""
@@ -173,6 +205,25 @@ def device_time_ms(stream_ptr: int, fn, steps: int) -> float:
     b.synchronize()
     torch.cuda.synchronize()
     return a.elapsed_time(b)
+
+
+def device_time_flushed_ms(stream_ptr: int, fn, steps: int, local: int) -> float:
+    """Sum of per-step CUDA-event durations, with the L2 flushed between
+    steps (a 256 MiB buffer written on the same stream, outside the event
+    pairs), so a step finds none of its inputs in the 126 MB L2."""
+    import torch
+    s = torch.cuda.ExternalStream(stream_ptr)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for i in range(steps):
+            flush.fill_(float(i))
+            ev[i][0].record(s)
+            fn()
+            ev[i][1].record(s)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev)
 
 
 _PINNED: list = []
@@ -215,48 +266,192 @@ def e2e_time(dev, ws, steps: int, uploads, run, downloads) -> dict:
             "d2h_bytes_per_step": int(sum(h.nbytes for _, h in downloads))}
 
 
-# ── CPU baseline (oracle) ───────────────────────────────────────────────────
-def cpu_scatter_step(inp: dict, nbins: int, threads: int, frac: float = 1.0):
+# ── CPU timing (the oracle: the reference arm and every cpu_baseline leg) ───
+def cpu_timed(one, steps: int, budget_s: float, warm_s: float = 2.0) -> dict:
+    """Time `steps` steps of CPU work, each step `reps` calls of `one()` (which
+    returns the algorithmic units it processed), with `reps` chosen so the
+    steps take about `budget_s` together. Before timing, `one()` runs for
+    about `warm_s` untimed (threads spun up, pages touched, clocks settled).
+    The reference arm and the cpu_baseline leg of the GPU arm both time
+    through here, so the two figures are taken the same way."""
+    t0 = time.perf_counter()
+    one()
+    calls = 1
+    while time.perf_counter() - t0 < warm_s:
+        one()
+        calls += 1
+    per_call = max((time.perf_counter() - t0) / calls, 1e-9)
+    # a call slower than budget / steps (an image of the CNN, a band of the
+    # GEMM) makes each step one call and takes fewer steps
+    steps = max(1, steps)
+    if steps * per_call > budget_s:
+        steps, reps = max(1, int(budget_s / per_call)), 1
+    else:
+        reps = max(1, math.ceil(budget_s / (steps * per_call)))
+    units = 0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for _ in range(reps):
+            units += one()
+    dt = time.perf_counter() - t0
+    return {"units_per_s": units / dt, "seconds": dt, "steps": steps, "reps_per_step": reps,
+            "calls": steps * reps}
+
+
+def scatter_inputs(rank: int = 0, n: int = 1 << 24, nbins: int = 1 << 16, nupd: int = 1 << 20) -> dict:
+    """The scatter workload's host inputs, as build_scatter draws them."""
+    from mantle_cuda.workloads import seeded_integers, seeded_uniform
+    s = 10 * rank
+    return {"va": seeded_uniform(0, n, 0, 1, s + 0), "ia": seeded_integers(0, n, nbins, s + 1),
+            "vb": seeded_uniform(0, n, 0, 1, s + 2), "ib": seeded_integers(0, n, nbins, s + 3),
+            "b": seeded_uniform(0, nupd, -1, 1, s + 4), "c": seeded_uniform(0, nupd, -1, 1, s + 5),
+            "d": seeded_uniform(0, nupd, -1, 1, s + 6)}
+
+
+def cpu_scatter_step(inp: dict, nbins: int, threads: int) -> int:
     """One step of the workload on the CPU: two scatters + histogram + three
-    updates, float32 with private per-thread bins (oracle/mantle_oracle.c)."""
+    updates, float32 with private per-thread bins (oracle/mantle_oracle.c).
+    Returns the algorithmic bytes."""
     import ctypes as C
 
     from oracle import oracle as O
     lib = O.lib()
-    n = int(inp["ia"].size * frac)
-    nu = int(inp["b"].size * frac)
+    n = int(inp["ia"].size)
+    nu = int(inp["b"].size)
     st = cpu_scatter_step.__dict__.setdefault("scratch", {})
     key = (threads, nbins)
     if key not in st:
-        st[key] = (np.empty(threads * nbins, np.float32), np.empty(threads * nbins, np.uint32),
-                   np.empty(nbins, np.float32), np.empty(nbins, np.float32), np.empty(nbins, np.uint32))
+        st[key] = (np.zeros(threads * nbins, np.float32), np.zeros(threads * nbins, np.uint32),
+                   np.zeros(nbins, np.float32), np.zeros(nbins, np.float32), np.zeros(nbins, np.uint32))
     sf, su, acc_a, acc_b, hist = st[key]
+    if "b_work" not in inp:
+        inp["b_work"] = inp["b"].copy()
     f32p, i32p, u32p = C.POINTER(C.c_float), C.POINTER(C.c_int32), C.POINTER(C.c_uint32)
     P = lambda a, t: a.ctypes.data_as(t)  # noqa: E731
     lib.oracle_scatter_f32(P(inp["va"], f32p), P(inp["ia"], i32p), n, nbins, P(acc_a, f32p), P(hist, u32p),
                            P(sf, f32p), P(su, u32p), threads)
     lib.oracle_scatter_f32(P(inp["vb"], f32p), P(inp["ib"], i32p), n, nbins, P(acc_b, f32p), None,
                            P(sf, f32p), P(su, u32p), threads)
-    b = inp["b_work"]
-    lib.oracle_touch3(P(b, f32p), P(inp["c"], f32p), P(inp["d"], f32p), nu, threads)
+    lib.oracle_touch3(P(inp["b_work"], f32p), P(inp["c"], f32p), P(inp["d"], f32p), nu, threads)
     return 16 * n + 36 * nu
 
 
-def cpu_baseline_scatter(inp: dict, nbins: int, budget_s: float = 10.0) -> dict:
+def cpu_scatter(inp: dict, nbins: int, steps: int, budget_s: float) -> dict:
     from oracle import oracle as O
     threads = O.max_threads()
-    inp = dict(inp)
-    inp["b_work"] = inp["b"].copy()
-    cpu_scatter_step(inp, nbins, threads)  # warm
-    t0 = time.perf_counter()
-    nbytes = steps = 0
-    while time.perf_counter() - t0 < budget_s:
-        nbytes += cpu_scatter_step(inp, nbins, threads)
-        steps += 1
-    dt = time.perf_counter() - t0
-    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} full steps (2x 2^{int(np.log2(inp['ia'].size))} scatter + histogram + "
-                      f"3 updates on 2^{int(np.log2(inp['b'].size))}) in {dt:.1f} s"}
+    r = cpu_timed(lambda: cpu_scatter_step(inp, nbins, threads), steps, budget_s)
+    return {"value": round(r["units_per_s"] / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{r['steps']} steps x {r['reps_per_step']} full replays (2x 2^{int(np.log2(inp['ia'].size))} "
+                      f"scatter + histogram + 3 updates on 2^{int(np.log2(inp['b'].size))}), oracle C + OpenMP, "
+                      f"{r['seconds']:.1f} s after a 2 s warm-up"}
+
+
+def cpu_chain(inp: dict, steps: int, budget_s: float) -> dict:
+    """The eight kernels as eight OpenMP passes (oracle chain8_passes)."""
+    from oracle import oracle as O
+    threads = O.max_threads()
+    n = inp["x"].size
+
+    def one():
+        O.chain8_passes(inp["x"], inp["y"], inp["z"], threads=threads)
+        return 16 * n
+
+    r = cpu_timed(one, steps, budget_s)
+    return {"value": round(r["units_per_s"] / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{r['calls']} replays of the 8 kernels over 2^{int(np.log2(n))} elements (one OpenMP pass "
+                      f"per kernel), {r['seconds']:.1f} s; GB/s of the 16 compulsory bytes per element"}
+
+
+def cpu_fft(x: np.ndarray, steps: int, budget_s: float) -> dict:
+    """Forward + inverse of a sample of 1024 transforms (oracle, float, OpenMP)."""
+    from oracle import oracle as O
+    threads = O.max_threads()
+    sample = np.ascontiguousarray(x[:1024])
+
+    def one():
+        O.fft(O.fft(sample, f32=True), inverse=True, f32=True)
+        return 2 * 2 * 8 * sample.size
+
+    r = cpu_timed(one, steps, budget_s)
+    return {"value": round(r["units_per_s"] / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{r['calls']} x (forward + inverse of 1024 transforms of {x.shape[1]}), oracle radix-2 in "
+                      f"float, OpenMP, {r['seconds']:.1f} s"}
+
+
+def cpu_gemm(A: np.ndarray, B: np.ndarray, M: int, N: int, K: int, steps: int, budget_s: float) -> dict:
+    """Bands of 16 rows of one 8192^3 GEMM (oracle, double, OpenMP)."""
+    from oracle import oracle as O
+    threads = O.max_threads()
+    rows = 16
+    done = [0]
+
+    def one():
+        O.gemm_bf16(A[:1], B[:1], M, N, K, 1, row0=(done[0] * rows) % M, rows=rows)
+        done[0] += 1
+        return 2 * rows * N * K
+
+    r = cpu_timed(one, steps, budget_s)
+    return {"value": round(r["units_per_s"] / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{r['calls'] * rows} rows of one {M}x{N}x{K} GEMM (oracle, double accumulation, OpenMP), "
+                      f"{r['seconds']:.1f} s"}
+
+
+def cpu_cnn(x, wts, fc, steps: int, budget_s: float) -> dict:
+    """Whole images through the oracle forward pass (double, OpenMP)."""
+    from mantle_cuda.workloads import CNN_LAYERS, STEM_CPAD
+    from oracle import oracle as O
+    threads = O.max_threads()
+    done = [0]
+    nimg = x.shape[0]
+
+    def one():
+        i = done[0] % nimg
+        O.cnn_forward(x[i:i + 1], wts, fc, CNN_LAYERS, STEM_CPAD)
+        done[0] += 1
+        return 1
+
+    r = cpu_timed(one, steps, budget_s, warm_s=0.0)
+    return {"value": round(r["units_per_s"], 3), "unit": "images/s", "cores": threads, "kind": "port",
+            "sample": f"{r['calls']} images through the oracle forward pass (double, OpenMP), {r['seconds']:.1f} s"}
+
+
+# ── configs shared by both arms ─────────────────────────────────────────────
+def scatter_config(ws: int, n: int = 1 << 24, nbins: int = 1 << 16, nupd: int = 1 << 20) -> dict:
+    return {"workload": "two scatters + int32 histogram + three RAW updates (bench/two_scatters.jl, "
+                        "bench/three_updates.jl shape)",
+            "scatter_elements": n, "bins": nbins, "update_elements": nupd,
+            "graph": "5 passes, replayed as one CUDA graph", "parallelism": f"{ws} independent graphs",
+            "l2": "inputs (256 MiB/step) exceed the 126 MB L2; no flush"}
+
+
+SCATTER_DATA = "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]"
+
+
+def chain_config(ws: int, n: int, unfused: bool, copies: int = 4) -> dict:
+    return {"workload": "elementwise chain, 8 dependent kernels (axpy a=0.5, mul, add, fma, abs, sqrt(abs), "
+                        "scale 2, sub)" + (" (unfused)" if unfused else " (fused, compiled)"),
+            "n": n, "bytes_per_step": 16 * n, "parallelism": f"{ws} independent graphs",
+            "l2": f"{copies} copies of the graph (4 x 64 MiB) replayed in turn: inputs larger than the L2"}
+
+
+def fft_config(ws: int, batch: int, n: int) -> dict:
+    return {"workload": "batched 1-D complex FFT, forward then inverse", "transforms": batch, "length": n,
+            "bytes_per_step": 2 * 2 * 8 * batch * n,
+            "parallelism": f"{batch // ws} transforms per GPU on {ws} GPU(s), no collective",
+            "l2": "L2 flushed between steps (256 MiB written outside the timed events)"}
+
+
+def gemm_config(ws: int, batch: int, M: int, N: int, K: int) -> dict:
+    return {"workload": "dense GEMM C = A.B, bf16 in, fp32 accumulate and out", "M": M, "N": N, "K": K,
+            "batch": batch, "parallelism": f"{batch // ws} GEMM(s) per GPU on {ws} GPU(s), no collective",
+            "l2": "A and B 128 MiB each per GEMM, C 256 MiB, above the 126 MB L2; no flush"}
+
+
+def cnn_config(ws: int, total: int) -> dict:
+    return {"workload": "CNN inference: 7x7/2 stem, 4 stages of two 3x3 convs (64-512), ReLU, GAP, FC 1000",
+            "global_batch": total, "image": [3, 224, 224], "parallelism": f"batch split over {ws} GPUs"
+            + (", NCCL all-gather of the logits every step" if ws > 1 else ""),
+            "l2": "L2 flushed between steps (256 MiB written outside the timed events)"}
 
 
 # ── workloads ───────────────────────────────────────────────────────────────
@@ -293,10 +488,6 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
     k_ms = device_time_ms(stream, launch, kreps) / kreps
     algo_bytes = 8 * w.n
     achieved = algo_bytes / (k_ms * 1e-3) / 1e9
-    traffic = None
-    tp = ROOT / "profiles" / "scatter_add_traffic.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
     # What bounds it in practice: the shared-memory atomics. The same call with
     # 2^12 bins (one CTA holds every bin: no cluster, no redundant streaming)
     # over the same 2^24 values and uniform indices is the atomic floor.
@@ -313,12 +504,13 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
     floor_ms = device_time_ms(stream, flaunch, kreps) / kreps
     roofline = {"bound": "hbm", "kernel": "scatter_add (scatter a: 2^24 values -> 2^16 bins + histogram)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_of("scatter_add"),
                 "algorithmic_bytes": algo_bytes, "peak_kind": f"{peak_kind} (burst copy)",
                 "kernel_ms": round(k_ms, 4),
                 "atomic_floor_ms": round(floor_ms, 4),
                 "frac_of_atomic_floor": round(floor_ms / k_ms, 4),
                 "atomic_floor": "the same call with 2^12 bins (all bins in one CTA's shared memory), measured here"}
+    del scratch, fws, idx_small, acc_small, hist_small
 
     # End to end through the public API: each step the four input arrays go
     # from pinned host memory through Update, the graph replays, and the bins
@@ -351,23 +543,17 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = cpu_baseline_scatter(w.inputs, w.nbins, budget_s=args.cpu_seconds)
+        cpu = cpu_scatter(dict(w.inputs), w.nbins, args.steps, args.cpu_seconds)
 
     nk = plan.nkernels()
-    line = {
+    return {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
-        "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
-        "config": {"workload": "two scatters + int32 histogram + three RAW updates (bench/two_scatters.jl, "
-                               "bench/three_updates.jl shape)",
-                   "scatter_elements": w.n, "bins": w.nbins, "update_elements": w.nupd,
-                   "graph": "5 passes, replayed as one CUDA graph", "parallelism": f"{ws} independent graphs",
-                   "l2": "inputs (256 MiB/step) exceed the 126 MB L2; no flush"},
+        "data": SCATTER_DATA, "config": scatter_config(ws, w.n, w.nbins, w.nupd),
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": nk * args.steps, "kernels_per_step": nk, "clocks": clk.summary(),
     }
-    return line
 
 
 def bench_chain(args, ws, rank, local, peaks, peak_kind):
@@ -404,56 +590,54 @@ def bench_chain(args, ws, rank, local, peaks, peak_kind):
     e2e = {"value": round(ws * w.bytes_compulsory / t["seconds"] / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": t["h2d_bytes_per_step"], "d2h_bytes_per_step": t["d2h_bytes_per_step"],
            "ms_per_step": round(t["seconds"] * 1e3, 3)}
-    line = {
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_chain(w.inputs, args.steps, args.cpu_seconds)
+    achieved = w.bytes_compulsory / (ms_step * 1e-3) / 1e9
+    return {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded PCG64, x,y,z U[-1,1]",
-        "config": {"workload": "elementwise chain, 8 dependent kernels" + (" (unfused)" if args.unfused else
-                                                                            " (fused, compiled)"),
-                   "n": w.n, "bytes_per_step": nbytes,
-                   "l2": f"{copies} copies of the graph (4 x 64 MiB) replayed in turn: inputs larger than the L2"},
-        "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(nbytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
-                     "timed": "the whole run! per step (a one-kernel plan: one kernel launch per step, the gaps between steps included)"},
-        "e2e": e2e, "gpu_launches": nk * args.steps, "clocks": clk.summary(),
+        "config": chain_config(ws, w.n, args.unfused, copies),
+        "roofline": {"bound": "hbm", "kernel": "the fused chain kernel (one launch a step)" if not args.unfused
+                     else "8 elementwise kernels", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic_of("chain_fused") if not args.unfused else None,
+                     "algorithmic_bytes": w.bytes_compulsory, "peak_kind": f"{peak_kind} (burst copy)",
+                     "timed": "the whole run per step (one kernel launch a step, the gaps between steps included)"},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": nk * args.steps, "clocks": clk.summary(),
     }
-    return line
 
 
 def bench_fft(args, ws, rank, local, peaks, peak_kind):
     """16384 ComplexF32 transforms of 4096 points, forward then inverse, as a
-    two-pass graph; each rank runs its own batch (weak scaling, no collective)."""
-    import torch
-
+    two-pass graph; the transforms are split across the ranks (strong scaling,
+    no collective)."""
     import mantle_cuda as M
     from mantle_cuda.workloads import build_fft
-    from oracle import oracle as O
 
+    total = 16384
     dev = M.Device(local)
-    w = build_fft(dev, rank=rank)
+    w = build_fft(dev, batch=total, rank=rank, world=ws)
     for _ in range(args.warmup):
         M.run(w.plan)
     dev.synchronize()
     barrier(ws)
     with ClockSampler(local) as clk:
-        ms = device_time_ms(dev.stream, lambda: M.run(w.plan), args.steps)
+        ms = device_time_flushed_ms(dev.stream, lambda: M.run(w.plan), args.steps, local)
     ms_step = max_over_ranks(ws, ms / args.steps)
     value = ws * w.bytes_step / (ms_step * 1e-3) / 1e9
 
-    # The forward kernel alone on the same stream: 16 B per point.
+    # The forward kernel alone on the same stream (16 B per point), L2 flushed
+    # between launches.
     launch = lambda: M.launch(M.kernels.fft_c2c, (w.spectrum, w.x, w.n, 0), w.batch, stream=dev.stream)  # noqa: E731
     for _ in range(3):
         launch()
     kreps = max(10, min(args.steps, 100))
-    k_ms = device_time_ms(dev.stream, launch, kreps) / kreps
+    k_ms = device_time_flushed_ms(dev.stream, launch, kreps, local) / kreps
     algo = 16 * w.batch * w.n
     achieved = algo / (k_ms * 1e-3) / 1e9
-    traffic = None
-    tp = ROOT / "profiles" / "fft_traffic.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
     # end to end: the input from pinned host memory, forward + inverse, the
     # round trip back to the host
     back_host = np.empty(w.inputs["x"].shape, w.inputs["x"].dtype)
@@ -464,29 +648,16 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        threads = O.max_threads()
-        sample = w.inputs["x"][:1024]
-        O.fft(sample[:16], f32=True)
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < args.cpu_seconds:
-            O.fft(O.fft(sample, f32=True), inverse=True, f32=True)
-            reps += 1
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(reps * 2 * 2 * 8 * sample.size / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
-               "kind": "port", "sample": f"{reps} x (forward + inverse of 1024 transforms of 4096), "
-                                         f"oracle radix-2 in float, OpenMP, {dt:.1f} s"}
+        cpu = cpu_fft(w.inputs["x"], args.steps, args.cpu_seconds)
     return {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "c64",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "c64",
         "data": "synthetic: seeded PCG64, re/im U[-1,1]",
-        "config": {"workload": "batched 1-D complex FFT, forward then inverse", "transforms": w.batch,
-                   "length": w.n, "bytes_per_step": w.bytes_step, "parallelism": f"{ws} independent graphs",
-                   "l2": "512 MiB per array, above the 126 MB L2; no flush"},
-        "roofline": {"bound": "hbm", "kernel": "fft_kernel<3> (forward, 16384 x 4096)",
+        "config": fft_config(ws, total, w.n),
+        "roofline": {"bound": "hbm", "kernel": f"fft_pipe_kernel (forward, {w.batch} x {w.n})",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_of("fft_forward"),
                      "algorithmic_bytes": algo, "peak_kind": f"{peak_kind} (burst copy)", "kernel_ms": round(k_ms, 4)},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
     }
@@ -494,13 +665,13 @@ def bench_fft(args, ws, rank, local, peaks, peak_kind):
 
 def bench_gemm(args, ws, rank, local, peaks, peak_kind):
     """8 GEMMs of 8192^3 (bf16 in, fp32 accumulate and out) as one graph pass;
-    each rank runs its own batch of 8 (weak scaling, no collective)."""
+    the batch is split across the ranks (strong scaling, no collective)."""
     import mantle_cuda as M
     from mantle_cuda.workloads import build_gemm
-    from oracle import oracle as O
 
+    total = 8
     dev = M.Device(local)
-    w = build_gemm(dev, rank=rank)
+    w = build_gemm(dev, batch=total, rank=rank, world=ws)
     for _ in range(args.warmup):
         M.run(w.plan)
     dev.synchronize()
@@ -510,17 +681,14 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
     ms_step = max_over_ranks(ws, ms / args.steps)
     tflops = ws * w.flops_step / (ms_step * 1e-3) / 1e12
     per_gpu = w.flops_step / (ms_step * 1e-3) / 1e12
-    # The timed region is seconds of back-to-back GEMMs: the sustained peak is
-    # the denominator; the burst figure is reported beside it.
+    # The timed region is back-to-back GEMMs under the power cap: the sustained
+    # peak is the denominator; the burst figure is reported beside it.
     peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-    roofline = {"bound": "tensor", "kernel": "gemm_bf16_kernel (8 x 8192^3 per launch)",
+    roofline = {"bound": "tensor", "kernel": f"gemm_bf16_kernel ({w.batch} x 8192^3 per launch)",
                 "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(per_gpu / peak, 4),
-                "traffic": None, "algorithmic_flops": w.flops_step,
+                "traffic": traffic_of("gemm"), "algorithmic_flops": w.flops_step,
                 "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)",
                 "frac_of_burst_peak": round(per_gpu / peaks["bf16_tflops"], 4), "kernel_ms": round(ms_step, 4)}
-    tp = ROOT / "profiles" / "gemm_traffic.json"
-    if tp.exists():
-        roofline["traffic"] = json.loads(tp.read_text()).get("dram_bytes_per_launch")
     # end to end: A and B (bf16 bits) from pinned host memory, the batch of
     # GEMMs, C back to the host
     A_host, B_host = w.host_operands()
@@ -532,24 +700,13 @@ def bench_gemm(args, ws, rank, local, peaks, peak_kind):
            "ms_per_step": round(t["seconds"] * 1e3, 3)}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        A, B = w.host_operands()
-        A, B = A[:1], B[:1]
-        threads = O.max_threads()
-        rows, t0, done = 16, time.perf_counter(), 0
-        while time.perf_counter() - t0 < args.cpu_seconds:
-            O.gemm_bf16(A, B, w.M, w.N, w.K, 1, row0=(done * rows) % w.M, rows=rows)
-            done += 1
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(done * rows * 2 * w.N * w.K / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
-               "kind": "port", "sample": f"{done * rows} rows of one 8192^3 GEMM (oracle, double, OpenMP) in {dt:.1f} s"}
+        cpu = cpu_gemm(A_host, B_host, w.M, w.N, w.K, args.steps, args.cpu_seconds)
     return {
         "metric": METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: torch Philox seed 1, normal(0,1)/sqrt(K) rounded to bf16",
-        "config": {"workload": "dense GEMM C = A.B, bf16 in, fp32 accumulate and out", "M": w.M, "N": w.N, "K": w.K,
-                   "batch": w.batch, "parallelism": f"{ws} independent batches",
-                   "l2": "A and B 1 GiB each per step, above the 126 MB L2; no flush"},
+        "config": gemm_config(ws, total, w.M, w.N, w.K),
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps,
         "clocks": clk.summary(),
     }
@@ -560,12 +717,9 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     "strong"), each rank replays its forward graph on its images, and the
     logits are all-gathered over NCCL every step (N > 1)."""
     import mantle_cuda as M
-    from mantle_cuda.workloads import CNN_CLASSES, CNN_LAYERS, STEM_CPAD, build_cnn
-    from oracle import oracle as O
+    from mantle_cuda.workloads import CNN_CLASSES, build_cnn
 
     total = 256
-    if total % ws:
-        raise SystemExit(f"batch {total} does not split over {ws} GPUs")
     dev = M.Device(local)
     w = build_cnn(dev, batch=total, rank=rank, world=ws)
     comm = gathered = None
@@ -586,7 +740,7 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     dev.synchronize()
     barrier(ws)
     with ClockSampler(local) as clk:
-        ms = device_time_ms(dev.stream, step, args.steps)
+        ms = device_time_flushed_ms(dev.stream, step, args.steps, local)
     ms_step = max_over_ranks(ws, ms / args.steps)
     images_s = total / (ms_step * 1e-3)
     flops = 2 * total * (w.flops_step // (2 * w.batch))
@@ -595,7 +749,7 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     # bf16) go from pinned host memory into the input buffer, the graph
     # replays (and the logits are all-gathered when N > 1), and this rank's
     # logits come back to the host.
-    x_bits, _, _ = w.host_params()
+    x_bits, wts, fc = w.host_params()
     x_host = pinned_like(x_bits.view(np.int16))
     logits_host = np.empty(w.batch * CNN_CLASSES, np.float32)
 
@@ -621,31 +775,22 @@ def bench_cnn(args, ws, rank, local, peaks, peak_kind):
     per_gpu = tflops / ws
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        x, wts, fc = w.host_params()
-        threads = O.max_threads()
-        t0, done = time.perf_counter(), 0
-        while time.perf_counter() - t0 < args.cpu_seconds or done == 0:
-            O.cnn_forward(x[done % w.batch:done % w.batch + 1], wts, fc, CNN_LAYERS, STEM_CPAD)
-            done += 1
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(done / dt, 3), "unit": "images/s", "cores": threads, "kind": "port",
-               "sample": f"{done} images through the oracle forward pass (double, OpenMP) in {dt:.1f} s"}
+        cpu = cpu_cnn(x_bits, wts, fc, args.steps, args.cpu_seconds)
     if comm is not None:
+        dev.synchronize()
         comm.release()
     return {
         "metric": METRIC, "value": round(images_s, 1), "unit": "images/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: torch Philox, input U[0,1) seed 4, He-normal weights seed 3",
-        "config": {"workload": "CNN inference: 7x7/2 stem, 4 stages of two 3x3 convs (64-512), ReLU, GAP, FC 1000",
-                   "global_batch": total, "image": [3, 224, 224], "parallelism": f"batch split over {ws} GPUs"
-                   + (", NCCL all-gather of the logits every step" if ws > 1 else ""),
-                   "tflops": round(tflops, 1)},
+        "config": dict(cnn_config(ws, total), tflops=round(tflops, 1)),
         "roofline": {"bound": "tensor", "kernel": "the whole forward graph (conv2d_nchw_bf16 + 8 conv2d_bf16 + "
                                                   "gap + fc)",
                      "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(per_gpu / peak, 4),
-                     "traffic": None, "algorithmic_flops": flops // ws,
-                     "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)"},
+                     "traffic": traffic_of("cnn_forward"), "algorithmic_flops": flops // ws,
+                     "peak_kind": f"{peak_kind} (sustained cuBLAS bf16)",
+                     "frac_of_burst_peak": round(per_gpu / peaks["bf16_tflops"], 4)},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
     }
 
@@ -688,8 +833,8 @@ def bench_showcase(args, ws, rank, local, peaks, peak_kind):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         threads = O.max_threads()
-        t0, frames = time.perf_counter(), 0
-        while time.perf_counter() - t0 < args.cpu_seconds or frames == 0:
+
+        def one():
             lpos, _, _ = O.sc_move_lights(sc.centers, sc.params, sc.home, sc.lcol, sc.P, sc.first)
             O.sc_cull(sc.centers, sc.P[0:16])
             O.sc_cull(sc.centers, sc.P[32:48])
@@ -699,11 +844,12 @@ def bench_showcase(args, ws, rank, local, peaks, peak_kind):
                              sc.pertile)
             bloom = O.sc_blur(O.sc_blur(O.sc_bright(hdr, sc.P, sc.shift), 1, 0), 0, 1)
             O.sc_composite(hdr, bloom, sc.P, sc.shift)
-            frames += 1
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(frames / dt, 3), "unit": "frames/s", "cores": threads, "kind": "port",
-               "sample": f"{frames} frames of the thirteen passes through the oracle (shading and occlusion on "
-                         f"OpenMP, the rest one thread) in {dt:.1f} s"}
+            return 1
+
+        r = cpu_timed(one, args.steps, args.cpu_seconds, warm_s=0.0)
+        cpu = {"value": round(r["units_per_s"], 3), "unit": "frames/s", "cores": threads, "kind": "port",
+               "sample": f"{r['calls']} frames of the thirteen passes through the oracle (shading and occlusion on "
+                         f"OpenMP, the rest one thread) in {r['seconds']:.1f} s"}
     return {
         "metric": METRIC, "value": round(ws * 1e3 / ms_step, 1), "unit": "frames/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -719,6 +865,13 @@ def bench_showcase(args, ws, rank, local, peaks, peak_kind):
                      "traffic": None, "algorithmic_bytes": int(algo), "peak_kind": f"{peak_kind} (burst copy)"},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.plan.nkernels() * args.steps, "clocks": clk.summary(),
     }
+
+
+SUB_KEYS = ("value", "unit", "ms_per_step", "scaling", "dtype", "data", "config", "roofline", "cpu_baseline",
+            "e2e", "gpu_launches", "clocks")
+WORKLOADS = {"scatter": bench_scatter, "chain": bench_chain, "fft": bench_fft, "gemm": bench_gemm,
+             "cnn": bench_cnn, "showcase": bench_showcase}
+ALL_ORDER = ("chain", "fft", "gemm", "cnn")
 
 
 def profile_case(args, local):
@@ -739,6 +892,11 @@ def profile_case(args, local):
             scratch = torch.empty(max(wsb, 16), dtype=torch.uint8, device=f"cuda:{local}")
             for _ in range(3):
                 M.launch(M.kernels.scatter_add, kargs, w.n, stream=s, workspace=scratch)
+    elif args.profile == "chain":
+        from mantle_cuda.workloads import build_chain
+        ws_ = [build_chain(dev, seed=k, fuse=True) for k in range(4)]
+        for k in range(6):
+            M.run(ws_[k % 4].plan)
     elif args.profile == "gemm":
         from mantle_cuda.workloads import build_gemm
         w = build_gemm(dev, batch=1)
@@ -756,7 +914,7 @@ def profile_case(args, local):
             M.run(w.plan)
     elif args.profile == "fft":
         from mantle_cuda.workloads import build_fft
-        w = build_fft(dev, batch=4096)
+        w = build_fft(dev, batch=8192)
         for _ in range(3):
             M.launch(M.kernels.fft_c2c, (w.spectrum, w.x, w.n, 0), w.batch, stream=s)
     dev.synchronize()
@@ -764,44 +922,29 @@ def profile_case(args, local):
 
 
 def reference_arm(args, ws, rank):
-    """The CPU restatement of the same workload on all host cores."""
+    """The CPU restatement of the same workloads on all host cores, timed the
+    way the GPU arm's cpu_baseline legs are (`cpu_timed`)."""
     if rank != 0:
         return None
-    from mantle_cuda.workloads import seeded_integers, seeded_uniform
     n, nbins, nupd = 1 << 24, 1 << 16, 1 << 20
-    inp = {"va": seeded_uniform(0, n, 0, 1, 0), "ia": seeded_integers(0, n, nbins, 1),
-           "vb": seeded_uniform(0, n, 0, 1, 2), "ib": seeded_integers(0, n, nbins, 3),
-           "b": seeded_uniform(0, nupd, -1, 1, 4), "c": seeded_uniform(0, nupd, -1, 1, 5),
-           "d": seeded_uniform(0, nupd, -1, 1, 6)}
-    from oracle import oracle as O
-    threads = O.max_threads()
-    inp["b_work"] = inp["b"].copy()
-    # Size each step so the whole run stays within about a minute.
-    t0 = time.perf_counter()
-    cpu_scatter_step(inp, nbins, threads)
-    t1 = time.perf_counter() - t0
-    total = args.steps + args.warmup
-    frac = min(1.0, 60.0 / max(total * t1, 1e-9))
-    for _ in range(args.warmup):
-        cpu_scatter_step(inp, nbins, threads, frac)
-    t0 = time.perf_counter()
-    nbytes = 0
-    for _ in range(args.steps):
-        nbytes += cpu_scatter_step(inp, nbins, threads, frac)
-    dt = time.perf_counter() - t0
-    v = nbytes / dt / 1e9
-    return {
-        "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32", "impl": "reference",
-        "data": "synthetic: seeded PCG64, values U[0,1], indices U{0..65535}, update buffers U[-1,1]",
-        "config": {"workload": "two scatters + int32 histogram + three RAW updates", "scatter_elements": n,
-                   "bins": nbins, "update_elements": nupd, "fraction_per_step": round(frac, 4)},
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps of {frac:.3f} x the workload (oracle/mantle_oracle.c, "
-                                   "float32 private bins, OpenMP)"},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    inp = scatter_inputs(0, n, nbins, nupd)
+    cpu = cpu_scatter(inp, nbins, args.steps, args.cpu_seconds)
+    v = cpu["value"]
+    line = {
+        "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round((16 * n + 36 * nupd) / (v * 1e9) * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32", "impl": "reference",
+        "data": SCATTER_DATA, "config": scatter_config(ws, n, nbins, nupd),
+        "cpu_baseline": cpu,
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    return line
+
+
+def run_workload(name, args, ws, rank, local, peaks, peak_kind):
+    rec = WORKLOADS[name](args, ws, rank, local, peaks, peak_kind)
+    release_device_memory(local)
+    return rec
 
 
 def main():
@@ -810,12 +953,13 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["scatter", "chain", "fft", "gemm", "cnn", "showcase"], default="scatter")
+    ap.add_argument("--workload", choices=["all", *WORKLOADS], default="all",
+                    help="all (default): the scatter headline plus chain, fft, gemm and cnn records")
     ap.add_argument("--unfused", action="store_true", help="chain: time the unfused eight-kernel graph")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--profile-batch", type=int, default=64, help="--profile cnn: the batch (default 64)")
-    ap.add_argument("--profile", choices=["scatter", "fft", "gemm", "cnn", "showcase"], default=None,
+    ap.add_argument("--profile", choices=["scatter", "chain", "fft", "gemm", "cnn", "showcase"], default=None,
                     help="launch only the workload's dominant kernel three times (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -835,18 +979,15 @@ def main():
     ws, rank, local = dist_init()
     peaks, peak_kind = load_peaks()
     try:
-        if args.workload == "chain":
-            line = bench_chain(args, ws, rank, local, peaks, peak_kind)
-        elif args.workload == "fft":
-            line = bench_fft(args, ws, rank, local, peaks, peak_kind)
-        elif args.workload == "gemm":
-            line = bench_gemm(args, ws, rank, local, peaks, peak_kind)
-        elif args.workload == "cnn":
-            line = bench_cnn(args, ws, rank, local, peaks, peak_kind)
-        elif args.workload == "showcase":
-            line = bench_showcase(args, ws, rank, local, peaks, peak_kind)
+        if args.workload == "all":
+            line = run_workload("scatter", args, ws, rank, local, peaks, peak_kind)
+            subs = {}
+            for name in ALL_ORDER:
+                rec = run_workload(name, args, ws, rank, local, peaks, peak_kind)
+                subs[name] = {k: rec[k] for k in SUB_KEYS if k in rec}
+            line["workloads"] = subs
         else:
-            line = bench_scatter(args, ws, rank, local, peaks, peak_kind)
+            line = run_workload(args.workload, args, ws, rank, local, peaks, peak_kind)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -316,6 +316,17 @@ mtl_status mtl_launch(int32_t kernel, const mtl_arg* args, int32_t nargs, const 
  * down instead of hanging. *count receives how many waits ran out on the
  * current device since the last reset; reset != 0 clears the counters. */
 mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count);
+/* The wall-clock limit of those waits on the current device, in ns (no
+ * counterpart in the reference): 0 restores the default of 2 s; below 1 ms is
+ * refused. Tests shorten it to make a wait run out in milliseconds. */
+mtl_status mtl_set_wait_limit(uint64_t ns);
+/* Test hook for the same failure path (no counterpart in the reference): in
+ * the next `launches` launches of the named kernel family ("gemm_bf16" is the
+ * one that has the hook) CTA 0's producer issues no load, so that CTA's MMA
+ * issuer waits on a stage that never fills until the limit runs out, counts a
+ * timeout and winds down with nothing in flight; every other CTA computes its
+ * tiles. 0 clears. */
+mtl_status mtl_inject_stall(const char* kernel, int32_t launches);
 
 /* Scatter-add / histogram that allocates nothing (no counterpart in the
  * reference). For callers that cannot call cudaMalloc on this path: scratch
@@ -324,9 +335,11 @@ mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count);
  * results as the `scatter_add` kernel (acc or hist may be NULL), launched on
  * `stream` for the current device. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) — make it before any stream
- * capture. All calls share the array: calls that overlap on the GPU race, so
- * order them. A call whose bins need more scratch than the array holds fails
- * with MTL_ERR_ARGUMENT. */
+ * capture; the lookup is repeated when the call finds another CUDA context
+ * current (after cudaDeviceReset, for one), so make the first call after a
+ * reset outside a capture too. All calls share the array: calls that overlap
+ * on the GPU race, so order them. A call whose bins need more scratch than the
+ * array holds fails with MTL_ERR_ARGUMENT. */
 #define MTL_NOALLOC_SCRATCH_BYTES (20u << 20)
 mtl_status mtl_scatter_add_noalloc(float* acc, uint32_t* hist, const float* values, const int32_t* idx,
                                    int64_t n, int32_t nbins, int32_t accumulate, void* stream);
@@ -341,6 +354,10 @@ mtl_status mtl_comm_release(mtl_comm* comm);
 mtl_status mtl_comm_abort(mtl_comm* comm);
 /* ncclAllGather of `bytes` per rank, on the device stream. */
 mtl_status mtl_allgather(mtl_comm* comm, const void* send, void* recv, uint64_t bytes);
+/* How long mtl_comm_init and mtl_allgather wait, on the host, for the
+ * communicator before they give up with MTL_ERR_TIMEOUT (the communicator is
+ * then aborted): 60 s unless set, process-wide. */
+mtl_status mtl_comm_set_timeout(double seconds);
 
 #ifdef __cplusplus
 }

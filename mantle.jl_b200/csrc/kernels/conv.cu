@@ -2355,6 +2355,9 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
 
 // Host: read (and with reset, clear) this file's count of bounded waits that
 // ran out on the current device.
+// Host: the bounded waits' limit of this file's kernels on the current device.
+cudaError_t conv_set_wait_limit(unsigned long long ns) { return set_wait_limit_this_file(ns); }
+
 int conv_timeouts(bool reset) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_conv_timeouts, sizeof v) != cudaSuccess) {

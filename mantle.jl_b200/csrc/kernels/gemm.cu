@@ -30,12 +30,16 @@
 // Every wait on an mbarrier is bounded by a wall-clock limit (%globaltimer);
 // a wait that runs out sets an abort flag that the other roles see, so the CTA
 // winds down, releases its tensor memory and returns, and the host reads the
-// count of such CTAs from g_gemm_timeouts.
+// count of such CTAs from g_gemm_timeouts. `stall_cta` (-1 normally) is the
+// test hook for that path: the producer of that CTA issues no load at all, so
+// its MMA issuer waits on a stage that never fills until the limit runs out
+// (mtl_inject_stall; nothing is in flight when the CTA winds down).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "../mtl_internal.hpp"
@@ -78,7 +82,7 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tile
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     float* __restrict__ C, int M, int N, int K, int batch) {
+                     float* __restrict__ C, int M, int N, int K, int batch, int stall_cta) {
   extern __shared__ unsigned char gsm_raw[];
   // 1024-byte alignment: the 128-byte swizzle repeats every 8 rows of 128 B.
   unsigned char* gsm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ── TMA producer ──
-    if (lane == 0) {
+    if (lane == 0 && (int)blockIdx.x != stall_cta) {
       int s = 0;
       uint32_t ph = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -263,6 +267,13 @@ mtl_status make_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uin
   return MTL_OK;
 }
 
+// Launches left whose CTA 0 stalls (mtl_inject_stall("gemm_bf16", n)).
+static std::atomic<int> g_gemm_stalls{0};
+void gemm_inject_stall(int launches) { g_gemm_stalls.store(launches > 0 ? launches : 0); }
+
+// Host: the bounded waits' limit of this file's kernels on the current device.
+cudaError_t gemm_set_wait_limit(unsigned long long ns) { return set_wait_limit_this_file(ns); }
+
 // Arguments: C (B, f32), A (B, bf16), B (B, bf16), M, N, K (i); ndrange = batch.
 mtl_status gemm_check(const LaunchArgs& la, const uint64_t* bytes) {
   if (la.ndim != 1) return fail(MTL_ERR_ARGUMENT, "gemm: ndrange must be one-dimensional (the batch count)");
@@ -302,7 +313,13 @@ mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
   const int64_t tiles = (int64_t)((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * batch;
   const int grid = (int)std::min<int64_t>(tiles, la.sm_count);
-  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch);
+  int stall = -1;
+  for (int left = g_gemm_stalls.load(); left > 0;)
+    if (g_gemm_stalls.compare_exchange_weak(left, left - 1)) {
+      stall = 0;
+      break;
+    }
+  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
   return MTL_OK;

@@ -57,6 +57,9 @@ mtl_status blur_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* str
 int gemm_timeouts(bool reset);
 int conv_timeouts(bool reset);
 int fft_timeouts(bool reset);
+cudaError_t gemm_set_wait_limit(unsigned long long ns);
+cudaError_t conv_set_wait_limit(unsigned long long ns);
+void gemm_inject_stall(int launches);
 
 // ── checks ──────────────────────────────────────────────────────────────────
 static int64_t nd_total(const LaunchArgs& la) {
@@ -283,6 +286,22 @@ mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count) {
     total += v;
   }
   *count = total;
+  return MTL_OK;
+}
+
+mtl_status mtl_set_wait_limit(uint64_t ns) {
+  const uint64_t v = ns ? ns : 2000000000ull;
+  if (v < 1000000ull) return mtl::fail(MTL_ERR_ARGUMENT, "mtl_set_wait_limit: %llu ns is below 1 ms", (unsigned long long)v);
+  for (cudaError_t e : {mtl::gemm_set_wait_limit(v), mtl::conv_set_wait_limit(v)})
+    if (e != cudaSuccess) return mtl::fail(MTL_ERR_CUDA, "mtl_set_wait_limit: %s", cudaGetErrorString(e));
+  return MTL_OK;
+}
+
+mtl_status mtl_inject_stall(const char* kernel, int32_t launches) {
+  if (!kernel) return mtl::fail(MTL_ERR_ARGUMENT, "mtl_inject_stall: NULL kernel name");
+  if (std::strcmp(kernel, "gemm_bf16") != 0)
+    return mtl::fail(MTL_ERR_UNSUPPORTED, "mtl_inject_stall: only gemm_bf16 has a stall hook, not %s", kernel);
+  mtl::gemm_inject_stall(launches);
   return MTL_OK;
 }
 

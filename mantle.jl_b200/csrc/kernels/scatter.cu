@@ -245,7 +245,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) scatter_cluster_kernel(
       for (int64_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x)
         scatter_one<ACC, HIST>(idx[i], ACC ? v[i] : 0.f, rank, shift, acc_base, hist_base);
   } else {
-    const int64_t e0 = g0 * 4, e1 = cl == ncl - 1 ? n : g1 * 4;
+    // Unaligned inputs: plain loads over an element range of the cluster's
+    // own, chunked by elements (not groups), so every element of [0, n) lies
+    // in exactly one cluster's range whatever n and ncl are.
+    const int64_t per_e = (n + ncl - 1) / ncl;
+    const int64_t e0 = min(n, cl * per_e), e1 = min(n, e0 + per_e);
     for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x)
       scatter_one<ACC, HIST>(idx[i], ACC ? v[i] : 0.f, rank, shift, acc_base, hist_base);
   }

@@ -15,7 +15,14 @@
 
 namespace mtl {
 
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+// The wall-clock limit of every bounded wait in this translation unit, in ns:
+// 2 s unless the host shortened it (mtl_set_wait_limit, for the tests that
+// make a wait run out). One copy per .cu file that includes this header.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+static inline cudaError_t set_wait_limit_this_file(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns);
+}
 
 // ── PTX wrappers ─────────────────────────────────────────────────────────────
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -63,11 +70,11 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 // the CTA is aborting (this wait ran out, or another role's did).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort, int* timeouts) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), limit = g_wait_limit_ns;
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       *abort = 1;
       atomicAdd(timeouts, 1);
       return false;
@@ -78,20 +85,20 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
 // MMAs finishing) before leaving; used on exit paths, so it ignores `abort`.
 __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), limit = g_wait_limit_ns;
   while (!mbar_try_wait_sleep(bar, parity))
-    if (globaltimer() - t0 > kWaitLimitNs) return;
+    if (globaltimer() - t0 > limit) return;
 }
 // Bounded wait until another role's progress counter (in shared memory)
 // reaches `target`.
 __device__ __forceinline__ bool wait_progress(volatile int* counter, int target, volatile int* abort, int* timeouts) {
   if (*counter >= target) return true;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), limit = g_wait_limit_ns;
   for (;;) {
     __nanosleep(64);
     if (*counter >= target) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       *abort = 1;
       atomicAdd(timeouts, 1);
       return false;

@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -33,6 +34,8 @@ struct Nccl {
 };
 Nccl g_nccl;
 std::mutex g_nccl_mu;
+// How long a communicator's set-up and each collective may take, in seconds.
+std::atomic<double> g_timeout_s{60.0};
 
 mtl_status load_nccl() {
   std::lock_guard<std::mutex> lk(g_nccl_mu);
@@ -122,7 +125,7 @@ mtl_status mtl_comm_init(mtl_device* dev, int32_t nranks, int32_t rank, const vo
     delete c;
     return fail(MTL_ERR_NCCL, "ncclCommInitRankConfig: %s", g_nccl.GetErrorString(r));
   }
-  if (mtl_status s = wait_ready(c, 60.0)) {
+  if (mtl_status s = wait_ready(c, g_timeout_s.load())) {
     std::string msg = mtl_last_error();
     g_nccl.CommAbort(c->comm);
     release_device(c->dev);
@@ -154,7 +157,13 @@ mtl_status mtl_allgather(mtl_comm* c, const void* send, void* recv, uint64_t byt
   if (mtl_status s = injected("mtl_allgather")) return s;
   ncclResult_t r = g_nccl.AllGather(send, recv, bytes, ncclUint8, c->comm, c->stream);
   if (r != ncclSuccess && r != ncclInProgress) return fail(MTL_ERR_NCCL, "ncclAllGather: %s", g_nccl.GetErrorString(r));
-  return wait_ready(c, 60.0);
+  return wait_ready(c, g_timeout_s.load());
+}
+
+mtl_status mtl_comm_set_timeout(double seconds) {
+  if (!(seconds > 0.0)) return fail(MTL_ERR_ARGUMENT, "mtl_comm_set_timeout: %g s is not positive", seconds);
+  g_timeout_s.store(seconds);
+  return MTL_OK;
 }
 
 }  // extern "C"

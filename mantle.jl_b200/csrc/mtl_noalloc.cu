@@ -18,8 +18,13 @@
 // Host code must not pass the array's name to a kernel: on the host that name
 // is only a stand-in for the device symbol, not a device address. The first
 // call on each device looks the real address up with cudaGetSymbolAddress,
-// with that device current, and keeps it; later calls reuse it. Make that
-// first call outside any stream capture (the lookup may load the module).
+// with that device current, and keeps it together with the CUDA context it
+// belongs to; later calls in the same context reuse it. A call that finds a
+// different current context (after cudaDeviceReset, or under a context the
+// caller made current itself) looks the address up again, because the module
+// may then sit at another address. Make the first call on a device, and the
+// first after a reset, outside any stream capture (the lookup may load the
+// module).
 
 #include <cuda_runtime.h>
 
@@ -41,13 +46,33 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch[kMaxDevices] = {};
+void* g_ctx[kMaxDevices] = {};
 int g_sms[kMaxDevices] = {};
 
-// Once per device, with that device current: the device address of the array.
+// The driver's current context (CUcontext), through the runtime's entry-point
+// lookup so that nothing links libcuda directly; null where unavailable.
+void* current_context() {
+  using Fn = int (*)(void**);
+  static Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<Fn>(p);
+    return static_cast<Fn>(nullptr);
+  }();
+  void* ctx = nullptr;
+  if (fn && fn(&ctx) != 0) ctx = nullptr;
+  return ctx;
+}
+
+// With the device current: the device address of the array, looked up once
+// per device and context.
 mtl_status scratch_for(int dev, void** ptr, int* sms) {
   if (dev < 0 || dev >= kMaxDevices) return fail(MTL_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch[dev]) {
+  void* ctx = current_context();
+  if (!g_scratch[dev] || ctx != g_ctx[dev]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
@@ -57,6 +82,9 @@ mtl_status scratch_for(int dev, void** ptr, int* sms) {
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "device %d: %s", dev, cudaGetErrorString(e));
     g_scratch[dev] = p;
     g_sms[dev] = n;
+    // looked up under the context current now (cudaGetSymbolAddress makes the
+    // primary context current when none was)
+    g_ctx[dev] = current_context();
   }
   *ptr = g_scratch[dev];
   *sms = g_sms[dev];

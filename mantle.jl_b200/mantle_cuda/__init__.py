@@ -910,6 +910,19 @@ def inject_failure(entry_point: str, count: int = 1) -> None:
     check(lib().mtl_inject_failure(entry_point.encode(), count))
 
 
+def set_wait_limit(ns: int = 0) -> None:
+    """The wall-clock limit of the kernels' bounded waits on the current
+    device (0 restores the default 2 s; at least 1 ms)."""
+    check(lib().mtl_set_wait_limit(int(ns)))
+
+
+def inject_stall(kernel: str, launches: int = 1) -> None:
+    """In the next `launches` launches of `kernel` ("gemm_bf16"), CTA 0's
+    producer loads nothing, so that CTA's waits run out (a test of the
+    bounded-wait path); 0 clears."""
+    check(lib().mtl_inject_stall(kernel.encode(), launches))
+
+
 class Comm:
     """An NCCL communicator over the GPUs of one node (one per process/GPU),
     for the final all-gather of a sharded run. `unique_id` is NCCL's 128-byte
@@ -920,6 +933,13 @@ class Comm:
         buf = C.create_string_buffer(128)
         check(lib().mtl_comm_unique_id(buf))
         return buf.raw
+
+    @staticmethod
+    def set_timeout(seconds: float) -> None:
+        """How long set-up and each all-gather may wait for the other ranks
+        before failing with a timeout (the communicator is then aborted);
+        60 s unless set, for the whole process."""
+        check(lib().mtl_comm_set_timeout(float(seconds)))
 
     def __init__(self, dev: Device, nranks: int, rank: int, unique_id: bytes):
         if len(unique_id) != 128:

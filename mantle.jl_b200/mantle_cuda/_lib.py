@@ -133,11 +133,14 @@ PROTOTYPES = {
     "mtl_launch": (I32, [I32, C.POINTER(Arg), I32, PI64, I32, P, U64, P]),
     "mtl_scatter_add_noalloc": (I32, [P, P, P, P, I64, I32, I32, P]),
     "mtl_kernel_timeouts": (I32, [I32, C.POINTER(C.c_int64)]),
+    "mtl_set_wait_limit": (I32, [C.c_uint64]),
+    "mtl_inject_stall": (I32, [C.c_char_p, I32]),
     "mtl_comm_unique_id": (I32, [P]),
     "mtl_comm_init": (I32, [P, I32, I32, P, PP]),
     "mtl_comm_release": (I32, [P]),
     "mtl_comm_abort": (I32, [P]),
     "mtl_allgather": (I32, [P, P, P, U64]),
+    "mtl_comm_set_timeout": (I32, [C.c_double]),
 }
 
 

@@ -21,6 +21,20 @@ import numpy as np
 from . import Buffer, Graph, Plan, Transient, Update, compute, dispatch, kernels, use
 
 
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """The contiguous slice [lo, hi) of `total` independent units (images,
+    GEMMs of a batch, transforms) that rank `rank` of `world` runs. The units
+    split evenly: a total that `world` does not divide is refused, so every
+    rank does the same work and the slices, gathered in rank order, are the
+    whole batch."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    if total % world:
+        raise ValueError(f"{total} units do not split evenly over {world} ranks")
+    per = total // world
+    return rank * per, (rank + 1) * per
+
+
 def seeded_uniform(seed: int, n: int, lo: float, hi: float, stream: int = 0) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64([seed, stream]))
     return rng.uniform(lo, hi, n).astype(np.float32)
@@ -174,10 +188,17 @@ def seeded_complex(seed: int, shape: tuple, stream: int = 0) -> np.ndarray:
     return (re + 1j * im).astype(np.complex64).reshape(shape)
 
 
-def build_fft(dev, batch: int = 16384, n: int = 4096, seed: int = 2, rank: int = 0, **plan_kw) -> FftWorkload:
+def build_fft(dev, batch: int = 16384, n: int = 4096, seed: int = 2, rank: int = 0, world: int = 1,
+              **plan_kw) -> FftWorkload:
     """Two passes: the forward transform of x into the spectrum, then the
-    inverse of the spectrum back into x's shape."""
-    x_h = seeded_complex(seed, (batch, n), stream=rank)
+    inverse of the spectrum back into x's shape. With world > 1 this rank
+    transforms its shard_range of the `batch` transforms (the same input rows
+    whatever the world size); `FftWorkload.batch` is the shard's size."""
+    lo, hi = shard_range(batch, rank, world)
+    x_h = seeded_complex(seed, (batch, n), stream=0)
+    if (lo, hi) != (0, batch):
+        x_h = np.ascontiguousarray(x_h[lo:hi])
+    batch = hi - lo
     x = Buffer(dev, x_h.reshape(-1))
     spectrum = Buffer(dev, np.complex64, batch * n)
     back = Buffer(dev, np.complex64, batch * n)
@@ -229,9 +250,15 @@ def gemm_operands(batch: int, M: int, N: int, K: int, seed: int = 1, device: str
 
 
 def build_gemm(dev, batch: int = 8, M: int = 8192, N: int = 8192, K: int = 8192, seed: int = 1, rank: int = 0,
-               **plan_kw) -> GemmWorkload:
-    """One pass: C[b] = A[b]·B[b] over the whole batch (bf16 in, fp32 out)."""
-    A_t, B_t = gemm_operands(batch, M, N, K, seed=seed + 1000 * rank, device=f"cuda:{dev.ordinal}")
+               world: int = 1, **plan_kw) -> GemmWorkload:
+    """One pass: C[b] = A[b]·B[b] over the batch (bf16 in, fp32 out). With
+    world > 1 this rank runs its shard_range of the batch (the same operands
+    whatever the world size); `GemmWorkload.batch` is the shard's size."""
+    lo, hi = shard_range(batch, rank, world)
+    A_t, B_t = gemm_operands(batch, M, N, K, seed=seed, device=f"cuda:{dev.ordinal}")
+    if (lo, hi) != (0, batch):
+        A_t, B_t = A_t[lo:hi].contiguous(), B_t[lo:hi].contiguous()
+    batch = hi - lo
     A = Buffer.wrap(dev, A_t, dtype=np.uint16)
     B = Buffer.wrap(dev, B_t, dtype=np.uint16)
     C = Buffer(dev, np.float32, batch * M * N)
@@ -326,9 +353,10 @@ def build_cnn(dev, batch: int = 256, seed: int = 3, rank: int = 0, world: int = 
     world > 1 this rank runs images [rank*batch/world, (rank+1)*batch/world)."""
     import torch
     device = f"cuda:{dev.ordinal}"
-    per = batch // world
+    lo, hi = shard_range(batch, rank, world)
+    per = hi - lo
     x_all = cnn_input(batch, seed, device)
-    x_t = x_all[rank * per:(rank + 1) * per].contiguous()
+    x_t = x_all[lo:hi].contiguous()
     del x_all
     params = cnn_parameters(seed, device)
     x = Buffer.wrap(dev, x_t, dtype=np.uint16)

@@ -90,3 +90,52 @@ def test_gemm_full_size_sampled_rows(dev):
     for r0 in (0, 95, 4133, 8191):
         want = O.gemm_bf16(A, B, w.M, w.N, w.K, w.batch, row0=r0, rows=1)
         check(C[:, r0:r0 + 1], want)
+
+
+@pytest.mark.gpu
+def test_stalled_producer_wait_runs_out_and_the_context_stays_usable(dev):
+    # The failure path of the bounded waits, made to run in milliseconds: the
+    # limit is shortened to 20 ms and CTA 0's producer of the next launch
+    # loads nothing, so its MMA issuer's wait on the first stage runs out. The
+    # launch must return, the timeout must be counted, the other CTAs' tiles
+    # must be right, and the next normal launch on the same context must be
+    # right everywhere.
+    import time
+
+    import torch
+    from mantle_cuda.workloads import gemm_operands
+    A, B = gemm_operands(1, 512, 512, 512, seed=13)
+    want = torch.matmul(A.double(), B.double()).cpu().numpy()
+    C = torch.full((1, 512, 512), float("nan"), device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    M.kernel_timeouts(reset=True)
+    try:
+        M.set_wait_limit(20_000_000)
+        M.inject_stall("gemm_bf16", 1)
+        t0 = time.perf_counter()
+        M.launch(M.kernels.gemm_bf16, (C, A, B, 512, 512, 512), 1, stream=s)
+        torch.cuda.synchronize()
+        took = time.perf_counter() - t0
+    finally:
+        M.inject_stall("gemm_bf16", 0)
+        M.set_wait_limit(0)
+    ran_out = M.kernel_timeouts()
+    assert 1 <= ran_out <= 3, ran_out  # the issuer; the producer or epilogue may also reach the limit first
+    assert took < 1.0
+    got = C.cpu().numpy()
+    # tile 0 (rows 0..127, columns 0..255) belonged to the stalled CTA; the
+    # rest was computed
+    assert np.isnan(got[0, :128, :256]).all()
+    check(got[0, 128:, :], want[0, 128:, :])
+    check(got[0, :128, 256:], want[0, :128, 256:])
+    # the same context, the default limit, no stall: every tile, no new timeout
+    C.fill_(float("nan"))
+    M.launch(M.kernels.gemm_bf16, (C, A, B, 512, 512, 512), 1, stream=s)
+    torch.cuda.synchronize()
+    check(C.cpu().numpy(), want)
+    assert M.kernel_timeouts(reset=True) == ran_out
+    with pytest.raises(M.ArgumentError):
+        M.set_wait_limit(1000)
+    with pytest.raises(M.MantleError):
+        M.inject_stall("fft_c2c", 1)

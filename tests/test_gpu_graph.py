@@ -116,6 +116,27 @@ def test_scatter_alignment_and_histogram_only(dev, offset, with_acc):
         np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
 
 
+@pytest.mark.parametrize("n", [1, 5, 7, 4 * 74 + 3, 4 * 148 + 3, 1001, 20011])
+@pytest.mark.parametrize("nbins", [1 << 16, 1000])
+def test_scatter_unaligned_small_inputs_lose_no_element(dev, n, nbins):
+    # Unaligned values and indices take the plain-load path, whose per-cluster
+    # element ranges must cover every element for sizes far below the grid's
+    # cluster count too (n = 5 over 74 clusters, ragged tails).
+    import torch
+    v = seeded_uniform(17, n + 1, 0, 1, 0)
+    idx = seeded_integers(17, n + 1, nbins, 1)
+    vt, it = torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda()
+    acc = torch.zeros(nbins, device="cuda")
+    hist = torch.zeros(nbins, dtype=torch.int32, device="cuda")
+    args = (acc, hist, vt[1:], it[1:], nbins, 0)
+    ws = torch.empty(max(M.workspace_bytes(M.kernels.scatter_add, args, n), 16), dtype=torch.uint8, device="cuda")
+    M.launch(M.kernels.scatter_add, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
+    torch.cuda.synchronize()
+    want_a, want_h = O.scatter_f64(v[1:], idx[1:], nbins)
+    assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h)
+    np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
+
+
 @pytest.mark.parametrize("out_offset", [0, 1])  # 0: four bins a thread in the final sum; 1: one
 def test_scatter_accumulates_into_aligned_and_unaligned_tables(dev, out_offset):
     import torch

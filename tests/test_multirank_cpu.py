@@ -2,7 +2,8 @@
 
 What runs on N GPUs has two host-side parts that need no GPU: the timing
 reduction (every rank's step time, the maximum reported) with the barriers
-around it, and the sharding of the CNN batch — rank r runs images
+around it, and the sharding of a batch by `shard_range` (the helper the CNN,
+GEMM and FFT workloads slice their batches with) — rank r runs units
 [r*B/N, (r+1)*B/N) and the all-gather lays the ranks' logits out in rank
 order, so the gathered array is the whole batch's. Here each rank computes its
 shard's logits with the oracle's GAP + FC and the shards are gathered over
@@ -35,6 +36,7 @@ def _rank_main(rank: int, world: int, port: int, errors):
         import torch.distributed as dist
 
         import bench
+        from mantle_cuda.workloads import shard_range
         from oracle import oracle as O
 
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -49,8 +51,8 @@ def _rank_main(rank: int, world: int, port: int, errors):
             rng = np.random.default_rng(21)  # the same inputs on every rank
             act = O.bf16_bits(np.abs(rng.standard_normal((n, hw, 1, c)).astype(np.float32)))
             w = (rng.standard_normal((c, classes)) * np.sqrt(2.0 / c)).astype(np.float32)
-            per = n // world
-            mine = torch.from_numpy(O.gap_fc(act[rank * per:(rank + 1) * per], w))
+            lo, hi = shard_range(n, rank, world)
+            mine = torch.from_numpy(O.gap_fc(act[lo:hi], w))
             parts = [torch.empty_like(mine) for _ in range(world)]
             dist.all_gather(parts, mine)
             gathered = torch.cat(parts).numpy()

@@ -6,8 +6,9 @@ allocation could stall or fail mid-frame. It takes its scratch from a fixed
 array compiled into the library, shared by every call on the device.
 
 Checked here through the C ABI against the regular entry point (mtl_launch of
-`scatter_add` with caller-provided scratch), on two calls in a row so that the
-second call runs over the leftovers of the first. Tolerance as for every
+`scatter_add` with caller-provided scratch) and against the oracle, on two
+calls in a row so that the second call runs over the leftovers of the first,
+and with unaligned caller pointers at small sizes. Tolerance as for every
 scatter test: bit-exact counts, 1e-5 relative (and 1e-5 absolute) sums.
 
 This file is named to be collected last.
@@ -54,6 +55,47 @@ def test_noalloc_matches_regular_entry_point_twice(dev, nbins):
         _noalloc(None, h2, None, idx, n, nbins, 1, dev.stream)
         dev.synchronize()
         assert np.array_equal(h2.array(), 2 * h1.array())
+
+
+def test_noalloc_matches_oracle_twice(dev):
+    # Against the oracle directly (float64 sums, exact counts), two calls in a
+    # row over the same shared scratch.
+    from mantle_cuda.workloads import seeded_integers, seeded_uniform
+    from oracle import oracle as O
+    nbins = 1 << 16
+    for call in range(2):
+        n = (1 << 20) + 7 * call
+        vh = seeded_uniform(40 + call, n, 0, 1, 0)
+        ih = seeded_integers(40 + call, n, nbins, 1)
+        acc, hist = M.Buffer(dev, np.float32, nbins), M.Buffer(dev, np.int32, nbins)
+        _noalloc(acc, hist, M.Buffer(dev, vh), M.Buffer(dev, ih), n, nbins, 0, dev.stream)
+        dev.synchronize()
+        want_a, want_h = O.scatter_f64(vh, ih, nbins)
+        assert np.array_equal(hist.array().view(np.uint32), want_h)
+        np.testing.assert_allclose(acc.array(), want_a, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n", [5, 7, 4 * 74 + 3, 1001])
+def test_noalloc_unaligned_small_inputs(dev, n):
+    # Caller pointers one element past an allocation's start take the
+    # plain-load path; every element must land, whatever n is.
+    import torch
+    from oracle import oracle as O
+    nbins = 1 << 16
+    rng = np.random.default_rng(n)
+    vh = rng.random(n + 1, dtype=np.float32)
+    ih = rng.integers(0, nbins, n + 1, dtype=np.int32)
+    vt, it = torch.from_numpy(vh).cuda(), torch.from_numpy(ih).cuda()
+    acc = torch.zeros(nbins, device="cuda")
+    hist = torch.zeros(nbins, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    L.check(L.lib().mtl_scatter_add_noalloc(C.c_void_p(acc.data_ptr()), C.c_void_p(hist.data_ptr()),
+                                            C.c_void_p(vt[1:].data_ptr()), C.c_void_p(it[1:].data_ptr()), n,
+                                            nbins, 0, C.c_void_p(dev.stream)))
+    dev.synchronize()
+    want_a, want_h = O.scatter_f64(vh[1:], ih[1:], nbins)
+    assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h)
+    np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=1e-5, atol=1e-5)
 
 
 def test_noalloc_large_bins_and_bad_arguments(dev):
