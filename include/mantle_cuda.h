@@ -313,7 +313,8 @@ mtl_status mtl_launch(int32_t kernel, const mtl_arg* args, int32_t nargs, const 
  * reference, whose Vulkan queue waits are host-side): every spin on an
  * mbarrier in the tensor-core and FFT kernels gives up after a
  * wall-clock limit, records it in a device counter and lets its CTA wind
- * down instead of hanging. *count receives how many waits ran out on the
+ * down instead of hanging. *count receives how many CTAs gave up on a wait
+ * that ran out (one per CTA, however many of its threads were waiting) on the
  * current device since the last reset; reset != 0 clears the counters. */
 mtl_status mtl_kernel_timeouts(int32_t reset, int64_t* count);
 /* The wall-clock limit of those waits on the current device, in ns (no

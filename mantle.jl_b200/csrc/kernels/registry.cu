@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstring>
 
 #include "../mtl_internal.hpp"
@@ -146,6 +147,88 @@ static mtl_status run_clear_and_tally(const LaunchArgs& la, void*, uint64_t, voi
   return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "clear_and_tally: %s", cudaGetErrorString(e));
 }
 
+// ── transpose_scale!(dst, src, w, h, a)   test/test_window.jl:30-33 ──────────
+// Over the ndrange (nx, ny), 0-based: dst[ix*h + iy] = src[iy*w + ix] * a. The
+// read runs along rows of src and the write down columns of it, so a block
+// stages a 32 x 32 tile in shared memory (one column of padding: the column
+// reads hit 32 different banks) and both global accesses are 128-byte rows.
+constexpr int kTpTile = 32, kTpRows = 8;
+__global__ void __launch_bounds__(kTpTile* kTpRows)
+    transpose_scale_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t w, int64_t h, float a,
+                           int64_t nx, int64_t ny) {
+  __shared__ float tile[kTpTile][kTpTile + 1];
+  const int64_t x0 = (int64_t)blockIdx.x * kTpTile, y0 = (int64_t)blockIdx.y * kTpTile;
+#pragma unroll
+  for (int r = threadIdx.y; r < kTpTile; r += kTpRows) {
+    const int64_t ix = x0 + threadIdx.x, iy = y0 + r;
+    if (ix < nx && iy < ny) tile[r][threadIdx.x] = __fmul_rn(src[iy * w + ix], a);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = threadIdx.y; r < kTpTile; r += kTpRows) {
+    const int64_t ix = x0 + r, iy = y0 + threadIdx.x;
+    if (ix < nx && iy < ny) dst[ix * h + iy] = tile[threadIdx.x][r];
+  }
+}
+static mtl_status check_transpose_scale(const LaunchArgs& la, const uint64_t* bytes) {
+  if (la.ndim != 2) return fail(MTL_ERR_ARGUMENT, "transpose_scale: ndrange must be (w, h)");
+  const int64_t w = la.a[2].i32, h = la.a[3].i32, nx = la.nd[0], ny = la.nd[1];
+  if (w < 0 || h < 0 || nx > w || ny > h)
+    return fail(MTL_ERR_ARGUMENT, "transpose_scale: ndrange (%lld, %lld) exceeds w = %lld, h = %lld", (long long)nx,
+                (long long)ny, (long long)w, (long long)h);
+  if (nx > 0 && ny > 0) {
+    const uint64_t src_need = (uint64_t)((ny - 1) * w + nx) * 4, dst_need = (uint64_t)((nx - 1) * h + ny) * 4;
+    if (bytes[1] && bytes[1] < src_need)
+      return fail(MTL_ERR_ARGUMENT, "transpose_scale: src has %llu bytes, the launch reads %llu",
+                  (unsigned long long)bytes[1], (unsigned long long)src_need);
+    if (bytes[0] && bytes[0] < dst_need)
+      return fail(MTL_ERR_ARGUMENT, "transpose_scale: dst has %llu bytes, the launch writes %llu",
+                  (unsigned long long)bytes[0], (unsigned long long)dst_need);
+  }
+  return MTL_OK;
+}
+static mtl_status run_transpose_scale(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  const int64_t nx = la.nd[0], ny = la.nd[1];
+  if (nx <= 0 || ny <= 0) return MTL_OK;
+  if ((nx + kTpTile - 1) / kTpTile > INT32_MAX || (ny + kTpTile - 1) / kTpTile > 65535)
+    return fail(MTL_ERR_UNSUPPORTED, "transpose_scale: ndrange too large");
+  dim3 grid((unsigned)((nx + kTpTile - 1) / kTpTile), (unsigned)((ny + kTpTile - 1) / kTpTile));
+  transpose_scale_kernel<<<grid, dim3(kTpTile, kTpRows), 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<float*>(la.a[0].ptr), reinterpret_cast<const float*>(la.a[1].ptr), la.a[2].i32, la.a[3].i32,
+      la.a[4].f32, nx, ny);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "transpose_scale: %s", cudaGetErrorString(e));
+}
+
+// ── frombytes!(dst, src): dst = Float32(src & 0xff)   test/test_window.jl:84-87
+// 16-byte loads and stores when both pointers allow them.
+__global__ void frombytes_kernel(float* __restrict__ dst, const uint32_t* __restrict__ src, int64_t n, bool vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t n4 = n / 4;
+    for (int64_t q = i; q < n4; q += stride) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + q);
+      reinterpret_cast<float4*>(dst)[q] =
+          make_float4((float)(v.x & 0xffu), (float)(v.y & 0xffu), (float)(v.z & 0xffu), (float)(v.w & 0xffu));
+    }
+    for (int64_t k = 4 * n4 + i; k < n; k += stride) dst[k] = (float)(src[k] & 0xffu);
+  } else {
+    for (int64_t k = i; k < n; k += stride) dst[k] = (float)(src[k] & 0xffu);
+  }
+}
+static mtl_status run_frombytes(const LaunchArgs& la, void*, uint64_t, void* stream) {
+  const int64_t n = nd_total(la);
+  if (n <= 0) return MTL_OK;
+  const bool vec = ((la.a[0].ptr | la.a[1].ptr) & 15) == 0;
+  const int64_t work = vec ? (n + 3) / 4 : n;
+  const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)la.sm_count * 8);
+  frombytes_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<float*>(la.a[0].ptr), reinterpret_cast<const uint32_t*>(la.a[1].ptr), n, vec);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "frombytes: %s", cudaGetErrorString(e));
+}
+
 // ── the table ───────────────────────────────────────────────────────────────
 #define EW(name, sig, rd, wr) \
   { name, sig, true, rd, wr, check_elementwise, nullptr, nullptr, nullptr }
@@ -174,6 +257,11 @@ static KernelDesc g_kernels[] = {
     EW("scale", "BBf", 0b010, 0b001),
     EW("chain8", "BBBB", 0b1110, 0b0001),
     {"fill_span", "Bif", false, 0b000, 0b001, check_fill_span, nullptr, run_fill_span, nullptr},
+    // transpose_scale(dst, src, w, h, a) over the ndrange (w, h), 2-D
+    {"transpose_scale", "BBiif", false, 0b00010, 0b00001, check_transpose_scale, nullptr, run_transpose_scale,
+     nullptr},
+    // frombytes(dst f32, src u32): the low byte as a float
+    {"frombytes", "BB", false, 0b10, 0b01, check_elementwise, nullptr, run_frombytes, nullptr},
     {"bump_counter", "B", false, 0b1, 0b1, check_counter, nullptr, run_bump_counter, nullptr},
     {"clear_and_tally", "BB", false, 0b10, 0b11, check_counter, nullptr, run_clear_and_tally, nullptr},
     {"scatter_add", "bbbBii", false, 0b001100, 0b000011, scatter_check, scatter_workspace, scatter_run,

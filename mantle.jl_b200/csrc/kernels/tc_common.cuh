@@ -66,6 +66,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+// A wait ran out: the CTA aborts, and the thread that raises its abort flag
+// (the first of its threads whose wait ran out) counts one timeout, so the
+// counter counts CTAs that gave up, however many of their threads were waiting.
+__device__ __forceinline__ void abort_cta(volatile int* abort, int* timeouts) {
+  if (atomicExch(const_cast<int*>(abort), 1) == 0) atomicAdd(timeouts, 1);
+}
+
 // Bounded wait for the phase of `bar` with the given parity. Returns false when
 // the CTA is aborting (this wait ran out, or another role's did).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort, int* timeouts) {
@@ -75,8 +82,7 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
     if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > limit) {
-      *abort = 1;
-      atomicAdd(timeouts, 1);
+      abort_cta(abort, timeouts);
       return false;
     }
   }
@@ -99,8 +105,7 @@ __device__ __forceinline__ bool wait_progress(volatile int* counter, int target,
     if (*counter >= target) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > limit) {
-      *abort = 1;
-      atomicAdd(timeouts, 1);
+      abort_cta(abort, timeouts);
       return false;
     }
   }

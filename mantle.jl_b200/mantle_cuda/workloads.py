@@ -95,6 +95,46 @@ def build_chain(dev, n: int = 1 << 22, seed: int = 0, fuse: bool = False, single
     return ChainWorkload(n, x, y, z, out, g, plan, {"x": x_h, "y": y_h, "z": z_h})
 
 
+# ── independent chains (bench/independent.jl) ───────────────────────────────
+@dataclass
+class IndependentWorkload:
+    n: int
+    chains: int
+    stages: int
+    k: float
+    sources: list
+    outputs: list
+    graph: Graph
+    plan: Plan
+    inputs: dict
+
+    @property
+    def bytes_step(self) -> int:
+        """Each stir stage reads and writes n Float32."""
+        return 8 * self.n * self.chains * self.stages
+
+
+def build_independent(dev, n: int = 1 << 20, chains: int = 8, stages: int = 6, k: float = 1.001, seed: int = 6,
+                      **plan_kw) -> IndependentWorkload:
+    """bench/independent.jl:43-56: `chains` independent chains of `stages`
+    stir! passes each, declared interleaved stage by stage (c1 s1, c2 s1, ...),
+    every intermediate a transient. The reference's first buffer of a chain is
+    a transient nothing writes; here it is a persistent buffer of seeded data,
+    and the last is a persistent output, so the result can be checked."""
+    src_h = [seeded_uniform(seed, n, -2, 2, c) for c in range(chains)]
+    sources = [Buffer(dev, x) for x in src_h]
+    outputs = [Buffer(dev, np.float32, n) for _ in range(chains)]
+    g = Graph(dev)
+    bufs = [[sources[c]] + [Transient.Buffer(g, np.float32, n) for _ in range(stages - 1)] + [outputs[c]]
+            for c in range(chains)]
+    for s_ in range(stages):
+        for c in range(chains):
+            compute(g, f"c{c + 1} s{s_ + 1}", lambda p, c=c, s_=s_: dispatch(p, kernels.stir, (
+                use(p, bufs[c][s_ + 1], write=True), use(p, bufs[c][s_], read=True), k), n))
+    plan = Plan(g, **plan_kw)
+    return IndependentWorkload(n, chains, stages, k, sources, outputs, g, plan, {"sources": src_h})
+
+
 # ── two scatters + histogram + three updates ────────────────────────────────
 @dataclass
 class ScatterWorkload:

@@ -12,6 +12,8 @@
  *   touch1!..touch3!   bench/stress.jl:30-45   a = a*1.0001 + b (+ c)
  *   mix!               bench/fuzz.jl:19-22     dst = a*0.5 + b*0.25 + k
  *   stir!              bench/independent.jl:37-40
+ *   touch4!            bench/stress.jl:42-45
+ *   transpose_scale!, frombytes!   test/test_window.jl:30-33, 84-87
  *   advect!            bench/two_scatters.jl:46-62
  *   unpack!, blur!     bench/chain.jl:27-40
  *   point splat        bench/two_scatters.jl:11-26 (SCATTER: MVP projection,
@@ -173,6 +175,39 @@ void oracle_scatter_f32(const float* v, const int32_t* idx, int64_t n, int32_t n
       }
     }
   }
+}
+
+/* stir!(dst, src, k) over n elements (bench/independent.jl:37-40):
+ * dst = src*k + sin(src), in float. */
+void oracle_stir(float* dst, const float* src, float k, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float t = src[i] * k;
+    dst[i] = t + sinf(src[i]);
+  }
+}
+
+/* touch4!(a, b, c, d) (bench/stress.jl:42-45): a = a*1.0001 + b + c + d, left
+ * to right. */
+void oracle_touch4(float* a, const float* b, const float* c, const float* d, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float t = a[i] * 1.0001f;
+    t = t + b[i];
+    t = t + c[i];
+    a[i] = t + d[i];
+  }
+}
+
+/* transpose_scale!(dst, src, w, h, a) over the ndrange (nx, ny)
+ * (test/test_window.jl:30-33), 0-based: dst[ix*h + iy] = src[iy*w + ix]*a. */
+void oracle_transpose_scale(float* dst, const float* src, int32_t w, int32_t h, float a, int64_t nx,
+                            int64_t ny) {
+  for (int64_t iy = 0; iy < ny; ++iy)
+    for (int64_t ix = 0; ix < nx; ++ix) dst[ix * h + iy] = src[iy * w + ix] * a;
+}
+
+/* frombytes!(dst, src) (test/test_window.jl:84-87): dst = Float32(src & 0xff). */
+void oracle_frombytes(float* dst, const uint32_t* src, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = (float)(src[i] & 0xffu);
 }
 
 /* mix!(dst, a, b, k) over n elements (bench/fuzz.jl:19-22). */

@@ -663,6 +663,10 @@ def lib():
         h.oracle_scatter_f64.argtypes = [f32p, i32p, C.c_int64, C.c_int32, f64p, u32p, C.c_int]
         h.oracle_scatter_f32.argtypes = [f32p, i32p, C.c_int64, C.c_int32, f32p, u32p, f32p, u32p, C.c_int]
         h.oracle_mix.argtypes = [f32p, f32p, f32p, C.c_float, C.c_int64]
+        h.oracle_stir.argtypes = [f32p, f32p, C.c_float, C.c_int64]
+        h.oracle_touch4.argtypes = [f32p, f32p, f32p, f32p, C.c_int64]
+        h.oracle_transpose_scale.argtypes = [f32p, f32p, C.c_int32, C.c_int32, C.c_float, C.c_int64, C.c_int64]
+        h.oracle_frombytes.argtypes = [f32p, u32p, C.c_int64]
         h.oracle_fft_f64.argtypes = [f32p, f64p, C.c_int64, C.c_int, C.c_int, C.c_int]
         h.oracle_fft_f32.argtypes = [f32p, f32p, C.c_int64, C.c_int, C.c_int, C.c_int]
         u16p = C.POINTER(C.c_uint16)
@@ -707,6 +711,41 @@ def chain8_passes(x, y, z, threads=0):
     tmp = np.empty(7 * x.size, np.float32)
     lib().oracle_chain8_passes(_p(x, C.c_float), _p(y, C.c_float), _p(z, C.c_float), _p(out, C.c_float),
                                _p(tmp, C.c_float), x.size, threads)
+    return out
+
+
+def stir(src, k):
+    """stir!(dst, src, k): dst = src*k + sin(src) (bench/independent.jl:37-40)."""
+    src = np.ascontiguousarray(src, np.float32)
+    out = np.empty_like(src)
+    lib().oracle_stir(_p(out, C.c_float), _p(src, C.c_float), float(k), src.size)
+    return out
+
+
+def touch4(a, b, c, d):
+    """touch4!(a, b, c, d): a*1.0001 + b + c + d (bench/stress.jl:42-45)."""
+    a = np.array(a, np.float32)
+    lib().oracle_touch4(_p(a, C.c_float), _p(b, C.c_float), _p(c, C.c_float), _p(d, C.c_float), a.size)
+    return a
+
+
+def transpose_scale(src, w, h, a, nx=None, ny=None):
+    """transpose_scale!(dst, src, w, h, a) over the ndrange (nx, ny), default
+    (w, h) (test/test_window.jl:30-33); dst has w*h elements, zero where the
+    ndrange does not reach."""
+    src = np.ascontiguousarray(src, np.float32)
+    nx = w if nx is None else nx
+    ny = h if ny is None else ny
+    out = np.zeros(w * h, np.float32)
+    lib().oracle_transpose_scale(_p(out, C.c_float), _p(src, C.c_float), w, h, float(a), nx, ny)
+    return out
+
+
+def frombytes(src):
+    """frombytes!(dst, src): Float32(src & 0xff) (test/test_window.jl:84-87)."""
+    src = np.ascontiguousarray(src, np.uint32)
+    out = np.empty(src.size, np.float32)
+    lib().oracle_frombytes(_p(out, C.c_float), _p(src, C.c_uint32), src.size)
     return out
 
 

@@ -121,7 +121,7 @@ def test_stalled_producer_wait_runs_out_and_the_context_stays_usable(dev):
         M.inject_stall("gemm_bf16", 0)
         M.set_wait_limit(0)
     ran_out = M.kernel_timeouts()
-    assert 1 <= ran_out <= 3, ran_out  # the issuer; the producer or epilogue may also reach the limit first
+    assert ran_out == 1, ran_out  # one CTA gave up, whichever of its threads' waits ran out first
     assert took < 1.0
     got = C.cpu().numpy()
     # tile 0 (rows 0..127, columns 0..255) belonged to the stalled CTA; the
