@@ -55,6 +55,9 @@ mtl_status unpack_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status unpack_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status blur_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status blur_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status raster_check(const LaunchArgs& la, const uint64_t* bytes);
+uint64_t raster_workspace(const LaunchArgs& la);
+mtl_status raster_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 int gemm_timeouts(bool reset);
 int conv_timeouts(bool reset);
 int fft_timeouts(bool reset);
@@ -289,6 +292,12 @@ static KernelDesc g_kernels[] = {
     {"pack_bgra8", "BB", false, 0b10, 0b01, pack_check, nullptr, pack_run, nullptr},
     {"unpack_bgra8", "BBii", false, 0b10, 0b01, unpack_check, nullptr, unpack_run, nullptr},
     {"blur3x3", "BBii", false, 0b10, 0b01, blur_check, nullptr, blur_run, nullptr},
+    // headless triangle rasterisation of instanced meshes (the g-buffer and shadow
+    // passes of bench/showcase.jl and bench/deferred.jl): depth, out0..2, proto
+    // positions, proto normals, visible, counter, centers, sizes, colors, params,
+    // P, matrix offset, mode, W, H, vertices per instance; ndrange = instances
+    {"raster_instances", "BbbbBbBBBBbbBiiiii", false, 0x1FF0, 0xF, raster_check, raster_workspace, raster_run,
+     nullptr},
     // the showcase's compute passes (bench/showcase.jl), headless; P = scene constants
     {"sc_move_lights", "BBBBBBi", false, 0b0111110, 0b0000111, sc_move_lights_check, nullptr, sc_move_lights_run,
      nullptr},

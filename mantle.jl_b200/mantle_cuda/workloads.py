@@ -635,10 +635,92 @@ class ShowcaseScene:
     lcol: np.ndarray     # (nlight, 4) colour and intensity
     centers: np.ndarray  # (ninst, 4) instance bounding spheres; the last nlight stand for the lights
     params: np.ndarray   # (ninst, 4) instance surface parameters
+    # for a scene whose g-buffer and shadow map are rasterised in the frame
+    # (crystal_scene): the prototype triangle list and the instances' scale and
+    # yaw and colour; alb/mat/nrm/dep/smap are then None
+    ppos: np.ndarray | None = None   # (V, 4) prototype positions
+    pnrm: np.ndarray | None = None   # (V, 4) prototype normals
+    sizes: np.ndarray | None = None  # (ninst, 4) scale xyz, yaw
+    colors: np.ndarray | None = None  # (ninst, 4) albedo rgb, roughness
+    smap_res: int = 0
 
     @property
     def first(self) -> int:
         return self.centers.shape[0] - self.home.shape[0]
+
+    @property
+    def rasterised(self) -> bool:
+        return self.ppos is not None
+
+
+def shard_geometry():
+    """The crystal prototype of bench/showcase.jl:47-67: a six-sided base ring
+    (radius 1 at y = -1), a narrower ring (0.72 at y = 0.45), an apex and a
+    base point; 24 triangles wound counter-clockwise seen from outside, each
+    vertex carrying its face normal. Returns (positions, normals), (72, 4)
+    float32 each (w = 1 for positions, 0 for normals)."""
+    n = 6
+    ring = lambda y, r: [np.array([r * np.cos(2 * np.pi * i / n), y, r * np.sin(2 * np.pi * i / n)])  # noqa: E731
+                         for i in range(n)]
+    bot, top = ring(-1.0, 1.0), ring(0.45, 0.72)
+    apex, base = np.array([0.0, 1.0, 0.0]), np.array([0.0, -1.0, 0.0])
+    pos, nrm = [], []
+
+    def tri(a, b, c):
+        fn = np.cross(b - a, c - a)
+        fn /= np.linalg.norm(fn)
+        for q in (a, b, c):
+            pos.append([*q, 1.0])
+            nrm.append([*fn, 0.0])
+
+    for i in range(n):
+        j = (i + 1) % n
+        tri(bot[i], top[j], bot[j])
+        tri(bot[i], top[i], top[j])
+        tri(top[i], apex, top[j])
+        tri(base, bot[j], bot[i])
+    return np.asarray(pos, np.float32), np.asarray(nrm, np.float32)
+
+
+def crystal_field(rng, n: int, clearing: float = 46.0, nhero: int = 26, nseed: int = 34, spread: float = 24.0,
+                  extent: float = 230.0, hmax: float = 13.0, fat: float = 0.30):
+    """The instances of bench/showcase.jl:72-110 (crystals): a wide dark floor
+    shard, a ring of `nhero` tall crystals around an open plaza, and clustered
+    smaller ones beyond it, drawn from `rng` (numpy's PCG64 here, so the
+    stream is not the reference's, the distributions are). Returns centers
+    (x, y, z, bounding radius), sizes (scale xyz, yaw), colors (rgb,
+    roughness), params (metalness, emission, 0, 0), each (n, 4) float32."""
+    centers = [[0.0, -0.02, 0.0, 900.0]]
+    sizes = [[900.0, 0.02, 900.0, 0.0]]
+    colors = [[0.045, 0.047, 0.056, 0.13]]
+    params = [[0.30, 0.0, 0.0, 0.0]]
+
+    def one(x, z, hgt, rad):
+        centers.append([x, hgt, z, np.sqrt(rad * rad + hgt * hgt) * 1.05])
+        sizes.append([rad, hgt, rad, 2 * np.pi * rng.uniform()])
+        t = rng.uniform()
+        c = ([0.26 + 0.16 * t, 0.32 + 0.14 * t, 0.46 + 0.12 * t] if t < 0.80
+             else list(np.array([0.62, 0.44, 0.30]) * (0.7 + 0.5 * rng.uniform())))
+        colors.append([*c, 0.08 + 0.42 * rng.uniform() ** 2])
+        params.append([0.9 if rng.uniform() < 0.4 else 0.05, 0.0, 0.0, 0.0])
+
+    for _ in range(nhero):
+        a = 2 * np.pi * rng.uniform()
+        r = clearing + 18 * rng.uniform()
+        hgt = 20 + 22 * rng.uniform()
+        one(r * np.cos(a), r * np.sin(a), hgt, 0.20 * hgt * (0.7 + 0.5 * rng.uniform()))
+    cand = [(extent * (rng.uniform() - 0.5), extent * (rng.uniform() - 0.5)) for _ in range(3 * nseed)]
+    seeds = [q for q in cand if np.hypot(*q) > clearing + 12][:nseed]
+    while len(centers) < n:
+        sx, sz = seeds[rng.integers(0, len(seeds))]
+        x = sx + spread * rng.standard_normal()
+        z = sz + spread * rng.standard_normal()
+        if np.hypot(x, z) < clearing:
+            continue
+        hgt = 1.5 + hmax * rng.uniform() ** 2.2
+        one(x, z, hgt, fat * hgt * (0.55 + 0.9 * rng.uniform()))
+    f = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    return f(centers), f(sizes), f(colors), f(params)
 
 
 def showcase_scene(w: int = 1600, h: int = 900, seed: int = 9, smap_res: int = 2048, nlight: int = 44,
@@ -743,25 +825,74 @@ class ShowcaseWorkload:
         return self.scene.home.shape[0]
 
 
+def crystal_scene(w: int = 1600, h: int = 900, seed: int = 9, smap_res: int = 2048, nshard: int = 5000,
+                  nlight: int = 44, t: float = 3.0) -> ShowcaseScene:
+    """The showcase's own scene (bench/showcase.jl:620-676): `nshard` crystal
+    instances of the 24-triangle prototype plus one small crystal riding on
+    each of the `nlight` lights, seen by the orbit camera at time t and the
+    sun's orthographic box; settings as showcase_scene. The g-buffer and the
+    shadow map are rasterised by the frame itself (build_showcase adds the
+    two raster passes), so they are None here."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    ppos, pnrm = shard_geometry()
+    centers, sizes, colors, params = crystal_field(rng, nshard)
+    base = showcase_scene(w=16, h=16, seed=seed, smap_res=16, nlight=nlight, ninst=nshard + nlight, t=t)
+    home, lcol = base.home, base.lcol
+    lc, ls, lk, lp = [], [], [], []
+    for i in range(nlight):  # the sources ride along as instances (bench/showcase.jl:623-629)
+        r = 0.4 + 0.7 * rng.uniform()
+        lc.append([0.0, 0.0, 0.0, 2 * r])
+        ls.append([r, r * 1.6, r, 2 * np.pi * rng.uniform()])
+        lk.append([*lcol[i, :3], 0.5])
+        lp.append([0.0, 1.0, 0.0, 0.0])
+    f = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    centers = np.concatenate([centers, f(lc)])
+    sizes = np.concatenate([sizes, f(ls)])
+    colors = np.concatenate([colors, f(lk)])
+    params = np.concatenate([params, f(lp)])
+    vp, _ = showcase_camera(t, 62.0, 14.0, w, h)
+    P = base.P.copy()
+    P[0:16], P[16:32] = _colmajor(vp), _colmajor(np.linalg.inv(vp))
+    _, eye = showcase_camera(t, 62.0, 14.0, w, h)
+    P[48:51] = eye
+    P[SC_OFF["stexel"]] = 2 * 150.0 / smap_res
+    return ShowcaseScene(w, h, 16, 32, 12, 4, P, None, None, None, None, None, home, lcol, centers, params,
+                         ppos=ppos, pnrm=pnrm, sizes=sizes, colors=colors, smap_res=smap_res)
+
+
 def build_showcase(dev, scene: ShowcaseScene, **plan_kw) -> ShowcaseWorkload:
     """The showcase's compute passes as one graph, in the reference's order
     (bench/showcase.jl:700-790): clear the two counters, move the lights, cull
     against the camera and the sun, write both draw commands, then tiles, SSAO,
     the AO blur, lighting, bright pass, the separable bloom blur and the
-    composite. The g-buffer and the shadow map are persistent inputs (their
-    raster passes are not built); the tile lists, occlusion, HDR and bloom
-    images are transients, placed and aliased by the planner. Scene constants
-    live in the persistent buffer `P` (update it per frame)."""
+    composite. For a rasterised scene (crystal_scene) the shadow map and the
+    g-buffer are drawn by two raster passes after the draw counts, from the
+    culled lists, as bench/showcase.jl:727-745 draws them; otherwise they are
+    persistent inputs. Either way they are persistent buffers (readable after
+    the frame); the tile lists, occlusion, HDR and bloom images are transients,
+    placed and aliased by the planner. Scene constants live in the persistent
+    buffer `P` (update it per frame)."""
     s = scene
     w, h, tile, pertile, shift = s.w, s.h, s.tile, s.pertile, s.shift
     ntx, nty = -(-w // tile), -(-h // tile)
     aow, aoh = -(-w // 2), -(-h // 2)
     bw, bh = -(-w // shift), -(-h // shift)
     ninst, nlight = s.centers.shape[0], s.home.shape[0]
-    B = {k: Buffer(dev, np.ascontiguousarray(v)) for k, v in dict(
-        P=s.P, alb=s.alb.reshape(-1), mat=s.mat.reshape(-1), nrm=s.nrm.reshape(-1), dep=s.dep.reshape(-1),
-        smap=s.smap.reshape(-1), home=s.home.reshape(-1), lcol=s.lcol.reshape(-1),
-        centers=s.centers.reshape(-1), params=s.params.reshape(-1)).items()}
+    res = s.smap_res if s.rasterised else s.smap.shape[0]
+    inputs = dict(P=s.P, home=s.home.reshape(-1), lcol=s.lcol.reshape(-1), centers=s.centers.reshape(-1),
+                  params=s.params.reshape(-1))
+    if s.rasterised:
+        inputs.update(ppos=s.ppos.reshape(-1), pnrm=s.pnrm.reshape(-1), sizes=s.sizes.reshape(-1),
+                      colors=s.colors.reshape(-1))
+    else:
+        inputs.update(alb=s.alb.reshape(-1), mat=s.mat.reshape(-1), nrm=s.nrm.reshape(-1), dep=s.dep.reshape(-1),
+                      smap=s.smap.reshape(-1))
+    B = {k: Buffer(dev, np.ascontiguousarray(v)) for k, v in inputs.items()}
+    if s.rasterised:
+        for k in ("alb", "mat", "nrm"):
+            B[k] = Buffer(dev, np.uint32, w * h)
+        B["dep"] = Buffer(dev, np.float32, w * h)
+        B["smap"] = Buffer(dev, np.float32, res * res)
     B["lpos"] = Buffer(dev, np.float32, 4 * nlight)
     for k in ("visible", "sunvisible"):
         B[k] = Buffer(dev, np.ones(ninst, np.uint32))
@@ -799,6 +930,16 @@ def build_showcase(dev, scene: ShowcaseScene, **plan_kw) -> ShowcaseWorkload:
     compute(g, "sun cull", lambda p: dispatch(p, kernels.sc_cull, (
         W(p, B["sunvisible"]), RW(p, B["suncounter"]), R(p, B["centers"]), R(p, B["P"]), 32), ninst))
     compute(g, "draw count", draw_count)
+    if s.rasterised:
+        nv = s.ppos.shape[0]
+        compute(g, "shadow", lambda p: dispatch(p, kernels.raster_instances, (
+            W(p, B["smap"]), None, None, None, R(p, B["ppos"]), None, R(p, B["sunvisible"]), R(p, B["suncounter"]),
+            R(p, B["centers"]), R(p, B["sizes"]), None, None, R(p, B["P"]), SC_OFF["sunvp"], 1, res, res, nv),
+            ninst))
+        compute(g, "gbuffer", lambda p: dispatch(p, kernels.raster_instances, (
+            W(p, B["dep"]), W(p, B["alb"]), W(p, B["mat"]), W(p, B["nrm"]), R(p, B["ppos"]), R(p, B["pnrm"]),
+            R(p, B["visible"]), R(p, B["counter"]), R(p, B["centers"]), R(p, B["sizes"]), R(p, B["colors"]),
+            R(p, B["params"]), R(p, B["P"]), SC_OFF["vp"], 0, w, h, nv), ninst))
     compute(g, "tiles", lambda p: dispatch(p, kernels.sc_tile_lights, (
         W(p, tl), W(p, tc), R(p, B["dep"]), R(p, B["lpos"]), R(p, B["P"]), w, h, tile, nlight, pertile),
         (ntx, nty)))
@@ -809,7 +950,7 @@ def build_showcase(dev, scene: ShowcaseScene, **plan_kw) -> ShowcaseWorkload:
     compute(g, "light", lambda p: dispatch(p, kernels.sc_shade, (
         W(p, hdr), R(p, B["alb"]), R(p, B["mat"]), R(p, B["nrm"]), R(p, B["dep"]), R(p, B["lpos"]),
         R(p, B["lcol"]), R(p, tl), R(p, tc), R(p, B["smap"]), R(p, aomap), R(p, B["P"]), tile, pertile,
-        s.smap.shape[0]), (w, h)))
+        res), (w, h)))
     compute(g, "bright", lambda p: dispatch(p, kernels.sc_bright, (W(p, bloom_a), R(p, hdr), R(p, B["P"]), w, h,
                                                                    shift), (bw, bh)))
     compute(g, "blur x", lambda p: dispatch(p, kernels.sc_blur, (W(p, bloom_b), R(p, bloom_a), 1, 0), (bw, bh)))

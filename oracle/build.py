@@ -13,7 +13,7 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-SRCS = [HERE / "mantle_oracle.c", HERE / "showcase_oracle.c"]
+SRCS = [HERE / "mantle_oracle.c", HERE / "showcase_oracle.c", HERE / "raster_oracle.c"]
 OUT = HERE / "liboracle.so"
 
 

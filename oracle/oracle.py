@@ -683,6 +683,9 @@ def lib():
         I = C.c_int  # noqa: E741
         h.oracle_sc_move_lights.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, I, I]
         h.oracle_sc_cull.argtypes = [u8p, f32p, f32p, I]
+        h.oracle_raster_instances.restype = C.c_int64
+        h.oracle_raster_instances.argtypes = [f32p, u32p, u32p, u32p, f32p, f32p, u32p, C.c_uint32, f32p, f32p, f32p,
+                                              f32p, f32p, I, I, I, I, I]
         h.oracle_sc_tile_lights.argtypes = [u32p, u32p, f32p, f32p, f32p, I, I, I, I, I]
         h.oracle_sc_shade.argtypes = [f32p, u32p, u32p, u32p, f32p, f32p, f32p, u32p, u32p, f32p, f32p, f32p,
                                       I, I, I, I, I]
@@ -923,6 +926,22 @@ def sc_move_lights(centers, params, home, lcol, P, first):
     lib().oracle_sc_move_lights(_p(pos, C.c_float), _p(c, C.c_float), _p(q, C.c_float), _f(home), _f(lcol), _f(P),
                                 first, n)
     return pos, c, q
+
+
+def raster_instances(ppos, pnrm, visible, count, centers, sizes, colors, params, M, mode, w, h):
+    """The triangle rasteriser of oracle/raster_oracle.c: draw instances
+    visible[:count] (1-based) of the prototype. Returns (depth (h, w) float32,
+    [out0, out1, out2] (h, w) uint32 or None per mode, pieces drawn)."""
+    f = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)  # noqa: E731
+    dep = np.zeros((h, w), np.float32)
+    outs = [np.zeros((h, w), np.uint32) if (mode == 0 or (mode == 2 and k < 2)) else None for k in range(3)]
+    vis = np.ascontiguousarray(visible, np.uint32)
+    n = lib().oracle_raster_instances(
+        _p(dep, C.c_float), *[_p(o, C.c_uint32) for o in outs], _p(f(ppos), C.c_float), _p(f(pnrm), C.c_float),
+        _p(vis, C.c_uint32), int(count), _p(f(centers), C.c_float), _p(f(sizes), C.c_float), _p(f(colors), C.c_float),
+        _p(f(params), C.c_float), _p(f(M), C.c_float), mode, w, h, int(np.asarray(ppos).shape[0]),
+        int(np.asarray(centers).shape[0]))
+    return dep, outs, n
 
 
 def sc_cull(centers, M):
