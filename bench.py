@@ -504,6 +504,19 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
     for _ in range(3):
         flaunch()
     floor_ms = device_time_ms(stream, flaunch, kreps) / kreps
+    # The same call on repeated bins, the splat-like case: 90 % of the indices
+    # in 64 bins. Warps that see their bins repeat sum in the warp first.
+    rng = np.random.Generator(np.random.PCG64([4321, 9]))
+    hot = torch.from_numpy(rng.choice(w.nbins, 64, replace=False).astype(np.int32)).to(f"cuda:{local}")
+    gs = torch.Generator(device=f"cuda:{local}").manual_seed(4321)
+    idx_skew = torch.randint(0, w.nbins, (w.n,), generator=gs, device=f"cuda:{local}", dtype=torch.int32)
+    pick = torch.rand(w.n, generator=gs, device=f"cuda:{local}") < 0.9
+    idx_skew[pick] = hot[torch.randint(0, 64, (int(pick.sum()),), generator=gs, device=f"cuda:{local}")]
+    sargs = (B["acc_a"], B["hist"], B["va"], idx_skew, w.nbins, 0)
+    slaunch = lambda: M.launch(M.kernels.scatter_add, sargs, w.n, stream=stream, workspace=scratch)  # noqa: E731
+    for _ in range(3):
+        slaunch()
+    skew_ms = device_time_ms(stream, slaunch, kreps) / kreps
     roofline = {"bound": "hbm", "kernel": "scatter_add (scatter a: 2^24 values -> 2^16 bins + histogram)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_of("scatter_add"),
@@ -511,8 +524,11 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
                 "kernel_ms": round(k_ms, 4),
                 "atomic_floor_ms": round(floor_ms, 4),
                 "frac_of_atomic_floor": round(floor_ms / k_ms, 4),
-                "atomic_floor": "the same call with 2^12 bins (all bins in one CTA's shared memory), measured here"}
-    del scratch, fws, idx_small, acc_small, hist_small
+                "atomic_floor": "the same call with 2^12 bins (all bins in one CTA's shared memory), measured here",
+                "skewed_ms": round(skew_ms, 4),
+                "skewed_gbs": round(algo_bytes / (skew_ms * 1e-3) / 1e9, 1),
+                "skewed": "the same call with 90 % of the indices in 64 of the 2^16 bins (warp-aggregated atomics)"}
+    del scratch, fws, idx_small, acc_small, hist_small, idx_skew
 
     # End to end through the public API: each step the four input arrays go
     # from pinned host memory through Update, the graph replays, and the bins

@@ -33,8 +33,9 @@
 // Work split: a setup kernel transforms, clips, snaps and culls one prototype
 // triangle per thread and sorts the pieces by screen size: those whose box is
 // at most 64 x 64 pixels go to a list rasterised one warp per piece (lanes over
-// the box), the others to a list rasterised per 16 x 16 screen tile by a CTA,
-// each thread one pixel, keeping its minimum in a register and merging once.
+// the box), the others to a list rasterised per 16 x 16 screen tile by a CTA
+// that first selects the big pieces meeting its tile, then tests them one
+// pixel per thread, keeping its minimum in a register and merging once.
 //
 // Modes: 0 the showcase's g-buffer (albedo + roughness, metalness + emission,
 // normal, each RGBA8 packed R in the low byte, and depth), 1 depth only (the
@@ -46,6 +47,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdint>
 
 #include "../mtl_internal.hpp"
@@ -91,6 +93,7 @@ struct Scratch {
   uint32_t* counts;         // [0] warp list, [1] big list
   Piece* warp_list;
   Piece* big_list;
+  uint2* big_box;           // the big pieces' boxes, packed (x0 | y0 << 16, x1 | y1 << 16)
   uint64_t cap;             // pieces per list
 };
 
@@ -241,20 +244,29 @@ __device__ bool make_piece(const CV (&poly)[kMaxPoly], int n, int sub, int W, in
   return *bx0 <= *bx1 && *by0 <= *by1;
 }
 
+// Depth from the three edge values at a sample of a positively oriented
+// piece: the barycentric weights e_i / S (S = e0 + e1 + e2, twice the
+// piece's area in subpixels, the same at every sample) applied to the
+// vertices' depths, as ((e0 z0 + e1 z1) + e2 z2) * (1 / S). -1 when the depth
+// is outside [0, 1) (the clip range, and the test LESS against 1).
+__device__ __forceinline__ float depth_of(float f0, float f1, float f2, const float (&z)[3], float inv_s) {
+  const float d = (f0 * z[0] + f1 * z[1] + f2 * z[2]) * inv_s + 0.f;  // + 0: a depth of -0 becomes +0
+  return (d >= 0.f && d < 1.f) ? d : -1.f;
+}
+__device__ __forceinline__ float inv_area(const int32_t (&X)[3], const int32_t (&Y)[3]) {
+  return 1.f / (float)edge(X[0], Y[0], X[1], Y[1], X[2], Y[2]);
+}
 // Depth at sample (sx, sy) of a positively oriented piece, or -1 when the
-// sample is not covered (or fails the clip range / the test against 1).
+// sample is not covered (or the depth is out of range).
 __device__ __forceinline__ float piece_depth(const int32_t (&X)[3], const int32_t (&Y)[3], const float (&z)[3],
-                                             int64_t sx, int64_t sy) {
+                                             float inv_s, int64_t sx, int64_t sy) {
   const int64_t e0 = edge(X[1], Y[1], X[2], Y[2], sx, sy);
   const int64_t e1 = edge(X[2], Y[2], X[0], Y[0], sx, sy);
   const int64_t e2 = edge(X[0], Y[0], X[1], Y[1], sx, sy);
   if (!inside(e0, owns_edge(X[1], Y[1], X[2], Y[2])) || !inside(e1, owns_edge(X[2], Y[2], X[0], Y[0])) ||
       !inside(e2, owns_edge(X[0], Y[0], X[1], Y[1])))
     return -1.f;
-  const float S = (float)(e0 + e1 + e2);
-  const float l0 = (float)e0 / S, l1 = (float)e1 / S, l2 = (float)e2 / S;
-  const float d = (l0 * z[0] + l1 * z[1] + l2 * z[2]) + 0.f;  // + 0: a depth of -0 becomes +0
-  return (d >= 0.f && d < 1.f) ? d : -1.f;
+  return depth_of((float)e0, (float)e1, (float)e2, z, inv_s);
 }
 __device__ __forceinline__ unsigned long long key_of(float d, uint32_t prim) {
   return ((unsigned long long)__float_as_uint(d) << 32) | prim;
@@ -290,11 +302,19 @@ __global__ void __launch_bounds__(kSetupThreads) raster_setup_kernel(RasterArgs 
     const int64_t area = (int64_t)(bx1 - bx0 + 1) * (by1 - by0 + 1);
     const bool big = area > kWarpBox;
     const uint32_t at = atomicAdd(&s.counts[big ? 1 : 0], 1u);
-    if (at < s.cap) (big ? s.big_list : s.warp_list)[at] = p;
+    if (at < s.cap) {
+      (big ? s.big_list : s.warp_list)[at] = p;
+      if (big) s.big_box[at] = make_uint2((uint32_t)bx0 | ((uint32_t)by0 << 16), (uint32_t)bx1 | ((uint32_t)by1 << 16));
+    }
   }
 }
 
 // ── the warp list: one warp per piece, lanes over its box ───────────────────
+// The edge values step by constants from pixel to pixel: e(x0 + dx, y0 + dy) =
+// e(x0, y0) + A dx + B dy. When every value over the box fits 32 bits (a box
+// of at most 64 x 64 pixels whose vertices lie near it) the lanes step in
+// 32-bit integers; otherwise they evaluate each edge in 64 bits. The values
+// are the same integers either way.
 __global__ void __launch_bounds__(256) raster_warp_kernel(Scratch s, int W) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -304,41 +324,77 @@ __global__ void __launch_bounds__(256) raster_warp_kernel(Scratch s, int W) {
     const Piece p = s.warp_list[e];
     const int bw = p.bx1 - p.bx0 + 1;
     const int area = bw * (p.by1 - p.by0 + 1);
+    const float inv_s = inv_area(p.X, p.Y);
+    const int64_t sx0 = (int64_t)p.bx0 * kSub + kSub / 2, sy0 = (int64_t)p.by0 * kSub + kSub / 2;
+    int64_t E0[3], A[3], B[3];
+    int32_t bias[3];
+    int64_t bound = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int a = k == 0 ? 1 : (k == 1 ? 2 : 0), b = k == 0 ? 2 : (k == 1 ? 0 : 1);
+      E0[k] = edge(p.X[a], p.Y[a], p.X[b], p.Y[b], sx0, sy0);
+      A[k] = -(int64_t)(p.Y[b] - p.Y[a]) * kSub;
+      B[k] = (int64_t)(p.X[b] - p.X[a]) * kSub;
+      bias[k] = owns_edge(p.X[a], p.Y[a], p.X[b], p.Y[b]) ? 0 : 1;  // inside: e >= bias
+      const int64_t bk = (E0[k] < 0 ? -E0[k] : E0[k]) + (A[k] < 0 ? -A[k] : A[k]) * (bw - 1) +
+                         (B[k] < 0 ? -B[k] : B[k]) * (p.by1 - p.by0);
+      bound = bk > bound ? bk : bound;
+    }
+    const bool narrow = bound < (int64_t)INT32_MAX;
     for (int i = lane; i < area; i += 32) {
-      const int px = p.bx0 + i % bw, py = p.by0 + i / bw;
-      const float d = piece_depth(p.X, p.Y, p.z, (int64_t)px * kSub + kSub / 2, (int64_t)py * kSub + kSub / 2);
+      const int dx = i % bw, dy = i / bw;
+      int64_t ev[3];
+      if (narrow) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) ev[k] = (int32_t)E0[k] + (int32_t)A[k] * dx + (int32_t)B[k] * dy;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) ev[k] = E0[k] + A[k] * dx + B[k] * dy;
+      }
+      if (ev[0] < bias[0] || ev[1] < bias[1] || ev[2] < bias[2]) continue;
+      const float d = depth_of((float)ev[0], (float)ev[1], (float)ev[2], p.z, inv_s);
       if (d < 0.f) continue;
       const unsigned long long k = key_of(d, p.prim);
-      unsigned long long* v = s.vis + (int64_t)py * W + px;
+      unsigned long long* v = s.vis + (int64_t)(p.by0 + dy) * W + (p.bx0 + dx);
       if (k < *v) atomicMin(v, k);
     }
   }
 }
 
 // ── the big list: one CTA per 16 x 16 tile, one pixel per thread ─────────────
-constexpr int kBigChunk = 128;
+// The CTA first picks out, all threads together, the big pieces whose boxes
+// meet its tile (from the packed boxes, 8 bytes a piece), then tests only
+// those against its pixels, in rounds of kFilter pieces.
+constexpr int kFilter = 1024;
 __global__ void __launch_bounds__(kTile* kTile) raster_big_kernel(Scratch s, int W, int H) {
-  __shared__ Piece chunk[kBigChunk];
+  __shared__ uint32_t hits[kFilter];
+  __shared__ int nhits;
   const int px = blockIdx.x * kTile + threadIdx.x % kTile, py = blockIdx.y * kTile + threadIdx.x / kTile;
-  const int tx0 = blockIdx.x * kTile, ty0 = blockIdx.y * kTile;
-  const int tx1 = tx0 + kTile - 1, ty1 = ty0 + kTile - 1;
+  const uint32_t tx0 = blockIdx.x * kTile, ty0 = blockIdx.y * kTile;
+  const uint32_t tx1 = tx0 + kTile - 1, ty1 = ty0 + kTile - 1;
   const uint32_t n = min(s.counts[1], (uint32_t)s.cap);
   unsigned long long best = ~0ull;
   const int64_t sx = (int64_t)px * kSub + kSub / 2, sy = (int64_t)py * kSub + kSub / 2;
-  for (uint32_t base = 0; base < n; base += kBigChunk) {
-    const uint32_t m = min((uint32_t)kBigChunk, n - base);
+  for (uint32_t base = 0; base < n; base += kFilter) {
+    const uint32_t m = min((uint32_t)kFilter, n - base);
+    if (threadIdx.x == 0) nhits = 0;
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) chunk[i] = s.big_list[base + i];
+    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+      const uint2 b = s.big_box[base + i];
+      const uint32_t bx0 = b.x & 0xffffu, by0 = b.x >> 16, bx1 = b.y & 0xffffu, by1 = b.y >> 16;
+      if (bx1 >= tx0 && bx0 <= tx1 && by1 >= ty0 && by0 <= ty1) hits[atomicAdd(&nhits, 1)] = base + i;
+    }
     __syncthreads();
-    for (uint32_t i = 0; i < m; ++i) {
-      const Piece& p = chunk[i];
-      if (p.bx1 < tx0 || p.bx0 > tx1 || p.by1 < ty0 || p.by0 > ty1) continue;  // uniform across the CTA
+    const int nh = nhits;
+    for (int j = 0; j < nh; ++j) {
+      const Piece& p = s.big_list[hits[j]];
       if (px > p.bx1 || px < p.bx0 || py > p.by1 || py < p.by0) continue;
-      const float d = piece_depth(p.X, p.Y, p.z, sx, sy);
+      const float d = piece_depth(p.X, p.Y, p.z, inv_area(p.X, p.Y), sx, sy);
       if (d < 0.f) continue;
       const unsigned long long k = key_of(d, p.prim);
       best = k < best ? k : best;
     }
+    __syncthreads();
   }
   if (px < W && py < H && best != ~0ull) atomicMin(s.vis + (int64_t)py * W + px, best);
 }
@@ -379,11 +435,10 @@ __global__ void __launch_bounds__(256) raster_resolve_kernel(RasterArgs a, Scrat
   const int64_t e0 = edge(sv[1].X, sv[1].Y, sv[2].X, sv[2].Y, sx, sy);
   const int64_t e1 = edge(sv[2].X, sv[2].Y, sv[0].X, sv[0].Y, sx, sy);
   const int64_t e2 = edge(sv[0].X, sv[0].Y, sv[1].X, sv[1].Y, sx, sy);
-  const float S = (float)(e0 + e1 + e2);
-  const float l0 = (float)e0 / S, l1 = (float)e1 / S, l2 = (float)e2 / S;
-  // perspective-correct weights of the piece's vertices, then of the
-  // prototype triangle's
-  const float q0 = l0 * sv[0].iw, q1 = l1 * sv[1].iw, q2 = l2 * sv[2].iw;
+  // perspective-correct weights of the piece's vertices (the screen-space
+  // weights e_i / S over w_i, normalised: S cancels), then of the prototype
+  // triangle's
+  const float q0 = (float)e0 * sv[0].iw, q1 = (float)e1 * sv[1].iw, q2 = (float)e2 * sv[2].iw;
   const float qs = q0 + q1 + q2;
   const float b0 = q0 / qs, b1 = q1 / qs, b2 = q2 / qs;
   const CV& v0 = poly[vi[0]];
@@ -463,7 +518,7 @@ static uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
 uint64_t raster_workspace(const LaunchArgs& la) {
   const uint64_t W = (uint64_t)std::max(la.a[15].i32, 0), H = (uint64_t)std::max(la.a[16].i32, 0);
-  return align256(W * H * 8) + 256 + 2 * align256(pieces_cap(la) * sizeof(Piece));
+  return align256(W * H * 8) + 256 + 2 * align256(pieces_cap(la) * sizeof(Piece)) + align256(pieces_cap(la) * 8);
 }
 
 mtl_status raster_check(const LaunchArgs& la, const uint64_t* bytes) {
@@ -529,6 +584,8 @@ mtl_status raster_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* s
   s.warp_list = reinterpret_cast<Piece*>(p);
   p += align256(s.cap * sizeof(Piece));
   s.big_list = reinterpret_cast<Piece*>(p);
+  p += align256(s.cap * sizeof(Piece));
+  s.big_box = reinterpret_cast<uint2*>(p);
   cudaError_t e = cudaMemsetAsync(s.vis, 0xff, (size_t)a.W * a.H * 8, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(s.counts, 0, 256, st);
   const int64_t threads = (int64_t)a.ninst * a.T;

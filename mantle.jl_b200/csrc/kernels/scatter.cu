@@ -166,6 +166,57 @@ __device__ __forceinline__ void scatter_one(int b, float v, uint32_t rank, int s
                  : "memory");
 }
 
+// The warp-aggregated form of scatter_one, for inputs whose bins repeat (a
+// splat that lands many points on the same pixels, a skewed histogram): the
+// lanes whose elements fall in the same bin of this CTA's range find each
+// other with __match_any_sync, sum their values inside the warp (a pairwise
+// tree over the group's lanes in rank order), and the group's first lane
+// issues one shared-memory atomic per table, adding the group's size to the
+// histogram. Lanes whose element this CTA does not own, or that carry no
+// element (bin -1), get a key of their own and do nothing. The whole warp
+// must be converged here.
+template <bool ACC, bool HIST>
+__device__ __forceinline__ void scatter_agg(int b, float v, uint32_t rank, int shift, uint32_t acc_base,
+                                            uint32_t hist_base) {
+  const unsigned lane = threadIdx.x & 31;
+  const bool mine = ((uint32_t)b >> shift) == rank;
+  const unsigned peers = __match_any_sync(0xffffffffu, mine ? (uint32_t)b : (0x80000000u | lane));
+  const int r = __popc(peers & ((1u << lane) - 1u));  // this lane's rank in its group
+  const int gsz = __popc(peers);
+  float sum = v;
+  if (ACC) {
+    for (int d = 1; __any_sync(0xffffffffu, d < gsz); d <<= 1) {
+      const bool has = r + d < gsz;
+      const int src = has ? (int)__fns(peers, 0, r + d + 1) : (int)lane;
+      const float t = __shfl_sync(0xffffffffu, sum, src);
+      if (has && (r & (2 * d - 1)) == 0) sum += t;
+    }
+  }
+  if (mine && r == 0) {
+    const uint32_t off = ((uint32_t)b & ((1u << shift) - 1)) * 4;
+    if (ACC) asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(acc_base + off), "f"(sum) : "memory");
+    if (HIST) asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(hist_base + off), "r"(gsz) : "memory");
+  }
+}
+
+// Whether a warp's elements repeat bins often enough for the aggregated form:
+// at least one in eight of the elements this CTA owns shares its bin with a
+// lower lane. Warp-uniform (every lane gets the warp's totals).
+__device__ __forceinline__ bool repeats_often(const int (&b)[8], uint32_t rank, int shift) {
+  const unsigned lane = threadIdx.x & 31;
+  int own = 0, dup = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool mine = ((uint32_t)b[k] >> shift) == rank;
+    const unsigned peers = __match_any_sync(0xffffffffu, mine ? (uint32_t)b[k] : (0x80000000u | lane));
+    own += mine;
+    dup += mine && (peers & ((1u << lane) - 1u)) != 0;
+  }
+  own = (int)__reduce_add_sync(0xffffffffu, (unsigned)own);
+  dup = (int)__reduce_add_sync(0xffffffffu, (unsigned)dup);
+  return own > 0 && 8 * dup >= own;
+}
+
 // CTA `rank` of cluster `cl` applies the elements of chunk `cl` that fall in its
 // bin range; partials go to ws[cl][nbins] per table.
 template <bool ACC, bool HIST>
@@ -194,51 +245,54 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) scatter_cluster_kernel(
   const int64_t g1 = min(n4, g0 + per_cl);
   const bool vec = ((reinterpret_cast<uintptr_t>(idx) | (ACC ? reinterpret_cast<uintptr_t>(v) : 0)) & 15) == 0;
   if (vec) {
-    int64_t q = g0 + threadIdx.x;
     const int64_t stride = blockDim.x;
-    // Two groups of four per iteration, and the next iteration's two groups
-    // are loaded before this one's atomics are issued (the loads are volatile
-    // asm, so they stay in this order): 64 bytes per thread stay in flight
-    // while the thread works through its shared-memory atomics.
-    int4 nb0 = make_int4(0, 0, 0, 0), nb1 = nb0;
-    float4 nv0 = make_float4(0, 0, 0, 0), nv1 = nv0;
-    if (q + stride < g1) {
+    int64_t q = g0 + threadIdx.x;
+    // Two groups of four per iteration (q and q + stride), and the next
+    // iteration's two groups are loaded before this one's atomics are issued
+    // (the loads are volatile asm, so they stay in this order): 64 bytes per
+    // thread stay in flight while the thread works through its shared-memory
+    // atomics. Every lane of a warp makes the same number of iterations (while
+    // the warp's first group is in the chunk); a lane past the chunk's end
+    // carries bin -1, which no CTA owns. So warps stay converged, which the
+    // aggregated form needs.
+    const int4 none = make_int4(-1, -1, -1, -1);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    int4 nb0 = none, nb1 = none;
+    float4 nv0 = zero, nv1 = zero;
+    if (q < g1) {
       nb0 = ld_nc_v4(idx + 4 * q);
-      nb1 = ld_nc_v4(idx + 4 * (q + stride));
-      if (ACC) {
-        nv0 = ld_nc_v4f(v + 4 * q);
-        nv1 = ld_nc_v4f(v + 4 * (q + stride));
-      }
+      if (ACC) nv0 = ld_nc_v4f(v + 4 * q);
     }
-    for (; q + stride < g1; q += 2 * stride) {
+    if (q + stride < g1) {
+      nb1 = ld_nc_v4(idx + 4 * (q + stride));
+      if (ACC) nv1 = ld_nc_v4f(v + 4 * (q + stride));
+    }
+    bool agg = false;
+    for (int64_t w = q - (threadIdx.x & 31), it = 0; w < g1; w += 2 * stride, q += 2 * stride, ++it) {
       const int4 b0 = nb0, b1 = nb1;
       const float4 v0 = nv0, v1 = nv1;
       const int64_t qn = q + 2 * stride;
-      if (qn + stride < g1) {
+      nb0 = none;
+      nb1 = none;
+      if (qn < g1) {
         nb0 = ld_nc_v4(idx + 4 * qn);
-        nb1 = ld_nc_v4(idx + 4 * (qn + stride));
-        if (ACC) {
-          nv0 = ld_nc_v4f(v + 4 * qn);
-          nv1 = ld_nc_v4f(v + 4 * (qn + stride));
-        }
+        if (ACC) nv0 = ld_nc_v4f(v + 4 * qn);
       }
-      scatter_one<ACC, HIST>(b0.x, v0.x, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.y, v0.y, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.z, v0.z, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.w, v0.w, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.x, v1.x, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.y, v1.y, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.z, v1.z, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b1.w, v1.w, rank, shift, acc_base, hist_base);
-    }
-    for (; q < g1; q += stride) {
-      int4 b0 = ld_nc_v4(idx + 4 * q);
-      float4 v0 = make_float4(0, 0, 0, 0);
-      if (ACC) v0 = ld_nc_v4f(v + 4 * q);
-      scatter_one<ACC, HIST>(b0.x, v0.x, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.y, v0.y, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.z, v0.z, rank, shift, acc_base, hist_base);
-      scatter_one<ACC, HIST>(b0.w, v0.w, rank, shift, acc_base, hist_base);
+      if (qn + stride < g1) {
+        nb1 = ld_nc_v4(idx + 4 * (qn + stride));
+        if (ACC) nv1 = ld_nc_v4f(v + 4 * (qn + stride));
+      }
+      const int bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      // every 16th iteration the warp re-measures how often its bins repeat
+      if ((it & 15) == 0) agg = repeats_often(bb, rank, shift);
+      if (agg) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) scatter_agg<ACC, HIST>(bb[k], vv[k], rank, shift, acc_base, hist_base);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) scatter_one<ACC, HIST>(bb[k], vv[k], rank, shift, acc_base, hist_base);
+      }
     }
     // The ragged tail (n not a multiple of four) belongs to the last cluster.
     if (cl == ncl - 1)

@@ -170,6 +170,7 @@ static int make_piece(const CV* poly, int n, int sub, int W, int H, Snap* sv, in
   return *bx0 <= *bx1 && *by0 <= *by1;
 }
 
+/* depth from the edge values: ((e0 z0 + e1 z1) + e2 z2) * (1 / S), S = e0 + e1 + e2 */
 static float piece_depth(const Snap* sv, int64_t sx, int64_t sy) {
   const int64_t e0 = edge(sv[1].X, sv[1].Y, sv[2].X, sv[2].Y, sx, sy);
   const int64_t e1 = edge(sv[2].X, sv[2].Y, sv[0].X, sv[0].Y, sx, sy);
@@ -178,9 +179,8 @@ static float piece_depth(const Snap* sv, int64_t sx, int64_t sy) {
       !inside(e1, owns_edge(sv[2].X, sv[2].Y, sv[0].X, sv[0].Y)) ||
       !inside(e2, owns_edge(sv[0].X, sv[0].Y, sv[1].X, sv[1].Y)))
     return -1.f;
-  const float S = (float)(e0 + e1 + e2);
-  const float l0 = (float)e0 / S, l1 = (float)e1 / S, l2 = (float)e2 / S;
-  const float d = (l0 * sv[0].z + l1 * sv[1].z + l2 * sv[2].z) + 0.f;
+  const float inv_s = 1.f / (float)edge(sv[0].X, sv[0].Y, sv[1].X, sv[1].Y, sv[2].X, sv[2].Y);
+  const float d = ((float)e0 * sv[0].z + (float)e1 * sv[1].z + (float)e2 * sv[2].z) * inv_s + 0.f;
   return (d >= 0.f && d < 1.f) ? d : -1.f;
 }
 static uint32_t fbits(float f) {
@@ -265,9 +265,7 @@ int64_t oracle_raster_instances(float* depth, uint32_t* out0, uint32_t* out1, ui
       const int64_t e0 = edge(sv[1].X, sv[1].Y, sv[2].X, sv[2].Y, sx, sy);
       const int64_t e1 = edge(sv[2].X, sv[2].Y, sv[0].X, sv[0].Y, sx, sy);
       const int64_t e2 = edge(sv[0].X, sv[0].Y, sv[1].X, sv[1].Y, sx, sy);
-      const float S = (float)(e0 + e1 + e2);
-      const float l0 = (float)e0 / S, l1 = (float)e1 / S, l2 = (float)e2 / S;
-      const float q0 = l0 * sv[0].iw, q1 = l1 * sv[1].iw, q2 = l2 * sv[2].iw;
+      const float q0 = (float)e0 * sv[0].iw, q1 = (float)e1 * sv[1].iw, q2 = (float)e2 * sv[2].iw;
       const float qs = q0 + q1 + q2;
       const float b0 = q0 / qs, b1 = q1 / qs, b2 = q2 / qs;
       const CV* v0 = &poly[vi[0]];

@@ -137,6 +137,42 @@ def test_scatter_unaligned_small_inputs_lose_no_element(dev, n, nbins):
     np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
 
 
+def skewed_indices(seed, n, nbins, hot=64, frac=0.9):
+    """Indices where `frac` of the elements fall in `hot` bins (spread over the
+    bin range) and the rest uniformly: the shape of additive splats, many
+    points on the same pixels (bench/two_scatters.jl:20-26)."""
+    rng = np.random.Generator(np.random.PCG64([seed, 9]))
+    hot_bins = rng.choice(nbins, hot, replace=False).astype(np.int32)
+    idx = rng.integers(0, nbins, n, dtype=np.int32)
+    pick = rng.uniform(size=n) < frac
+    idx[pick] = hot_bins[rng.integers(0, hot, int(pick.sum()))]
+    return idx
+
+
+@pytest.mark.parametrize("shape", ["skewed", "one bin", "sorted"])
+def test_scatter_repeated_bins_take_the_aggregated_form(dev, shape):
+    # Bins that repeat within a warp are summed in the warp first (one atomic
+    # per bin per warp); the result is the oracle's whichever form ran.
+    import torch
+    n, nbins = (1 << 20) + 4, 1 << 16
+    v = seeded_uniform(31, n, 0, 1, 0)
+    if shape == "skewed":
+        idx = skewed_indices(31, n, nbins)
+    elif shape == "one bin":
+        idx = np.full(n, 40000, np.int32)
+    else:
+        idx = np.sort(seeded_integers(31, n, nbins, 1))
+    acc = torch.zeros(nbins, device="cuda")
+    hist = torch.zeros(nbins, dtype=torch.int32, device="cuda")
+    args = (acc, hist, torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda(), nbins, 0)
+    ws = torch.empty(M.workspace_bytes(M.kernels.scatter_add, args, n), dtype=torch.uint8, device="cuda")
+    M.launch(M.kernels.scatter_add, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
+    torch.cuda.synchronize()
+    want_a, want_h = O.scatter_f64(v, idx, nbins)
+    assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h)
+    np.testing.assert_allclose(acc.cpu().numpy(), want_a, rtol=RTOL, atol=1e-5)
+
+
 @pytest.mark.parametrize("out_offset", [0, 1])  # 0: four bins a thread in the final sum; 1: one
 def test_scatter_accumulates_into_aligned_and_unaligned_tables(dev, out_offset):
     import torch

@@ -136,7 +136,9 @@ def _launch_raster(ppos, pnrm, visible, count, centers, sizes, colors, params, P
     outs = [torch.zeros(h * w, dtype=torch.int32, device="cuda") if (mode == 0 or (mode == 2 and k < 2)) else None
             for k in range(3)]
     opt = lambda a: None if a is None else _dev(a)  # noqa: E731
-    args = (depth, *outs, _dev(ppos), opt(pnrm), _dev(np.asarray(visible, np.uint32)),
+    vis = np.zeros(max(centers.shape[0], len(visible)), np.uint32)  # the cull's list has a slot per instance
+    vis[:len(visible)] = visible
+    args = (depth, *outs, _dev(ppos), opt(pnrm), _dev(vis),
             _dev(np.array([count], np.uint32)), _dev(centers), _dev(sizes), opt(colors), opt(params), _dev(P), off,
             mode, w, h, ppos.shape[0])
     n = centers.shape[0]
@@ -254,7 +256,7 @@ def test_showcase_frame_with_raster_passes_matches_oracle(dev, crystals):
     from mantle_cuda.workloads import build_showcase
     sc, centers, params = crystals
     w = build_showcase(dev, sc)
-    assert "gbuffer" in w.plan.names() and "shadow" in w.plan.names()
+    assert "gbuffer" in w.plan.names and "shadow" in w.plan.names
     M.run(w.plan)
     M.run(w.plan)
     dev.synchronize()
