@@ -211,16 +211,21 @@ def device_time_ms(stream_ptr: int, fn, steps: int) -> float:
 
 def device_time_flushed_ms(stream_ptr: int, fn, steps: int, local: int) -> float:
     """Sum of per-step CUDA-event durations, with the L2 flushed between
-    steps (a 256 MiB buffer written on the same stream, outside the event
-    pairs), so a step finds none of its inputs in the 126 MB L2."""
+    steps on the same stream, outside the event pairs: a 256 MiB buffer is
+    written, then a second one read, so a step finds none of its inputs in
+    the 126 MB L2 and no dirty line of the flush left to write back inside
+    its own timed region."""
     import torch
     s = torch.cuda.ExternalStream(stream_ptr)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
+    clean = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
+    sink = torch.zeros(1, dtype=torch.float32, device=f"cuda:{local}")
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     with torch.cuda.stream(s):
         for i in range(steps):
             flush.fill_(float(i))
+            torch.sum(clean, dim=0, keepdim=True, out=sink)
             ev[i][0].record(s)
             fn()
             ev[i][1].record(s)
@@ -440,7 +445,7 @@ def fft_config(ws: int, batch: int, n: int) -> dict:
     return {"workload": "batched 1-D complex FFT, forward then inverse", "transforms": batch, "length": n,
             "bytes_per_step": 2 * 2 * 8 * batch * n,
             "parallelism": f"{batch // ws} transforms per GPU on {ws} GPU(s), no collective",
-            "l2": "L2 flushed between steps (256 MiB written outside the timed events)"}
+            "l2": "L2 flushed between steps (256 MiB written, then 256 MiB read, outside the timed events)"}
 
 
 def gemm_config(ws: int, batch: int, M: int, N: int, K: int) -> dict:
@@ -453,7 +458,7 @@ def cnn_config(ws: int, total: int) -> dict:
     return {"workload": "CNN inference: 7x7/2 stem, 4 stages of two 3x3 convs (64-512), ReLU, GAP, FC 1000",
             "global_batch": total, "image": [3, 224, 224], "parallelism": f"batch split over {ws} GPUs"
             + (", NCCL all-gather of the logits every step" if ws > 1 else ""),
-            "l2": "L2 flushed between steps (256 MiB written outside the timed events)"}
+            "l2": "L2 flushed between steps (256 MiB written, then 256 MiB read, outside the timed events)"}
 
 
 # ── workloads ───────────────────────────────────────────────────────────────
@@ -504,19 +509,25 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
     for _ in range(3):
         flaunch()
     floor_ms = device_time_ms(stream, flaunch, kreps) / kreps
-    # The same call on repeated bins, the splat-like case: 90 % of the indices
-    # in 64 bins. Warps that see their bins repeat sum in the warp first.
+    # The same call on piled-up bins, the splat-like case: 90 % of the indices
+    # in 64 bins, and all in one bin, through both scatter families.
     rng = np.random.Generator(np.random.PCG64([4321, 9]))
     hot = torch.from_numpy(rng.choice(w.nbins, 64, replace=False).astype(np.int32)).to(f"cuda:{local}")
     gs = torch.Generator(device=f"cuda:{local}").manual_seed(4321)
     idx_skew = torch.randint(0, w.nbins, (w.n,), generator=gs, device=f"cuda:{local}", dtype=torch.int32)
     pick = torch.rand(w.n, generator=gs, device=f"cuda:{local}") < 0.9
     idx_skew[pick] = hot[torch.randint(0, 64, (int(pick.sum()),), generator=gs, device=f"cuda:{local}")]
-    sargs = (B["acc_a"], B["hist"], B["va"], idx_skew, w.nbins, 0)
-    slaunch = lambda: M.launch(M.kernels.scatter_add, sargs, w.n, stream=stream, workspace=scratch)  # noqa: E731
-    for _ in range(3):
-        slaunch()
-    skew_ms = device_time_ms(stream, slaunch, kreps) / kreps
+    idx_one = torch.full((w.n,), 40000, dtype=torch.int32, device=f"cuda:{local}")
+    pile = {}
+    for shape, ix in (("skewed", idx_skew), ("one_bin", idx_one)):
+        for fam in ("scatter_add", "scatter_add_dense"):
+            sargs = (B["acc_a"], B["hist"], B["va"], ix, w.nbins, 0)
+            kern = getattr(M.kernels, fam)
+            slaunch = lambda: M.launch(kern, sargs, w.n, stream=stream, workspace=scratch)  # noqa: E731
+            for _ in range(2):
+                slaunch()
+            reps = 5 if shape == "one_bin" else kreps
+            pile[f"{shape}_{fam}_ms"] = round(device_time_ms(stream, slaunch, reps) / reps, 4)
     roofline = {"bound": "hbm", "kernel": "scatter_add (scatter a: 2^24 values -> 2^16 bins + histogram)",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic_of("scatter_add"),
@@ -525,10 +536,10 @@ def bench_scatter(args, ws, rank, local, peaks, peak_kind):
                 "atomic_floor_ms": round(floor_ms, 4),
                 "frac_of_atomic_floor": round(floor_ms / k_ms, 4),
                 "atomic_floor": "the same call with 2^12 bins (all bins in one CTA's shared memory), measured here",
-                "skewed_ms": round(skew_ms, 4),
-                "skewed_gbs": round(algo_bytes / (skew_ms * 1e-3) / 1e9, 1),
-                "skewed": "the same call with 90 % of the indices in 64 of the 2^16 bins (warp-aggregated atomics)"}
-    del scratch, fws, idx_small, acc_small, hist_small, idx_skew
+                "piled_bins": dict(pile, note="the same call with 90 % of the indices in 64 of the 2^16 bins "
+                                              "(skewed) and with every index in one bin (one_bin), through "
+                                              "scatter_add and scatter_add_dense (warp-aggregated atomics)")}
+    del scratch, fws, idx_small, acc_small, hist_small, idx_skew, idx_one
 
     # End to end through the public API: each step the four input arrays go
     # from pinned host memory through Update, the graph replays, and the bins

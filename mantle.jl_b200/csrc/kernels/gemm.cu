@@ -40,6 +40,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "../mtl_internal.hpp"
@@ -52,7 +53,7 @@ constexpr uint32_t kAStage = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kBStage = kBK * kBN * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kAStage + kBStage;
 constexpr int kGemmThreads = 192;
-constexpr int kGroupM = 16;  // tile rows per raster group
+constexpr int kGroupM = 16;  // tile rows per raster group (MTL_GEMM_GROUP_M overrides it, for tuning)
 constexpr uint32_t kTmemCols = 512;
 // ring + barriers + alignment slack
 constexpr int kGemmSmem = kStages * (int)kStageBytes + 1024 + 1024;
@@ -66,15 +67,15 @@ constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, false, true);
 struct TileCoord {
   int b, m0, n0;
 };
-__device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tiles_n) {
+__device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tiles_n, int group_m) {
   const int64_t per = (int64_t)tiles_m * tiles_n;
   TileCoord c;
   c.b = (int)(t / per);
   int r = (int)(t % per);
-  const int group = r / (kGroupM * tiles_n);
-  const int first_m = group * kGroupM;
-  const int gsize = min(kGroupM, tiles_m - first_m);
-  const int in_group = r % (kGroupM * tiles_n);
+  const int group = r / (group_m * tiles_n);
+  const int first_m = group * group_m;
+  const int gsize = min(group_m, tiles_m - first_m);
+  const int in_group = r % (group_m * tiles_n);
   c.m0 = (first_m + in_group % gsize) * kBM;
   c.n0 = (in_group / gsize) * kBN;
   return c;
@@ -82,7 +83,7 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tile
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     float* __restrict__ C, int M, int N, int K, int batch, int stall_cta) {
+                     float* __restrict__ C, int M, int N, int K, int batch, int stall_cta, int group_m) {
   extern __shared__ unsigned char gsm_raw[];
   // 1024-byte alignment: the 128-byte swizzle repeats every 8 rows of 128 B.
   unsigned char* gsm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+        const TileCoord tc = tile_coord(t, tiles_m, tiles_n, group_m);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_gemm_timeouts)) goto producer_done;
           const uint32_t fb = smem_u32(&full[s]);
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int a = i & 1;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_gemm_timeouts)) break;
       tc_fence_after();
-      const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+      const TileCoord tc = tile_coord(t, tiles_m, tiles_n, group_m);
       const int row = tc.m0 + q * 32 + lane;
       float* crow = C + ((int64_t)tc.b * M + row) * (int64_t)N;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kBN);
@@ -271,6 +272,16 @@ mtl_status make_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uin
 static std::atomic<int> g_gemm_stalls{0};
 void gemm_inject_stall(int launches) { g_gemm_stalls.store(launches > 0 ? launches : 0); }
 
+// Tile rows per raster group: kGroupM, or MTL_GEMM_GROUP_M (1..1024) read once.
+static int group_m() {
+  static const int g = [] {
+    const char* e = std::getenv("MTL_GEMM_GROUP_M");
+    const int v = e ? std::atoi(e) : 0;
+    return v >= 1 && v <= 1024 ? v : kGroupM;
+  }();
+  return g;
+}
+
 // Host: the bounded waits' limit of this file's kernels on the current device.
 cudaError_t gemm_set_wait_limit(unsigned long long ns) { return set_wait_limit_this_file(ns); }
 
@@ -319,7 +330,7 @@ mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
       stall = 0;
       break;
     }
-  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall);
+  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall, group_m());
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
   return MTL_OK;

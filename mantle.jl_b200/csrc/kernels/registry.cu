@@ -55,6 +55,7 @@ mtl_status unpack_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status unpack_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status blur_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status blur_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
+mtl_status scatter_dense_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status raster_check(const LaunchArgs& la, const uint64_t* bytes);
 uint64_t raster_workspace(const LaunchArgs& la);
 mtl_status raster_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
@@ -269,6 +270,9 @@ static KernelDesc g_kernels[] = {
     {"clear_and_tally", "BB", false, 0b10, 0b11, check_counter, nullptr, run_clear_and_tally, nullptr},
     {"scatter_add", "bbbBii", false, 0b001100, 0b000011, scatter_check, scatter_workspace, scatter_run,
      nullptr},
+    // the same arguments, for inputs whose bins pile up (warp-aggregated atomics)
+    {"scatter_add_dense", "bbbBii", false, 0b001100, 0b000011, scatter_check, scatter_workspace,
+     scatter_dense_run, nullptr},
     // batched complex FFT: out, in, length, inverse; ndrange = number of transforms
     {"fft_c2c", "BBii", false, 0b10, 0b01, fft_check, nullptr, fft_run, nullptr},
     // batched bf16 GEMM, fp32 accumulate and output: C, A, B, M, N, K; ndrange = batch

@@ -149,24 +149,31 @@ def skewed_indices(seed, n, nbins, hot=64, frac=0.9):
     return idx
 
 
-@pytest.mark.parametrize("shape", ["skewed", "one bin", "sorted"])
-def test_scatter_repeated_bins_take_the_aggregated_form(dev, shape):
-    # Bins that repeat within a warp are summed in the warp first (one atomic
-    # per bin per warp); the result is the oracle's whichever form ran.
+@pytest.mark.parametrize("family", ["scatter_add", "scatter_add_dense"])
+@pytest.mark.parametrize("shape", ["uniform", "skewed", "one bin", "sorted", "eight bins"])
+def test_scatter_repeated_bins_both_families(dev, family, shape):
+    # scatter_add_dense: warps whose bins pile up sum in the warp first (one
+    # atomic per bin per warp), the others take the plain form; scatter_add is
+    # plain throughout. The result is the oracle's whichever form ran.
     import torch
     n, nbins = (1 << 20) + 4, 1 << 16
     v = seeded_uniform(31, n, 0, 1, 0)
-    if shape == "skewed":
+    if shape == "uniform":
+        idx = seeded_integers(31, n, nbins, 1)
+    elif shape == "skewed":
         idx = skewed_indices(31, n, nbins)
     elif shape == "one bin":
         idx = np.full(n, 40000, np.int32)
+    elif shape == "eight bins":
+        idx = (seeded_integers(31, n, 8, 1) * 8191).astype(np.int32)
     else:
         idx = np.sort(seeded_integers(31, n, nbins, 1))
+    kernel = getattr(M.kernels, family)
     acc = torch.zeros(nbins, device="cuda")
     hist = torch.zeros(nbins, dtype=torch.int32, device="cuda")
     args = (acc, hist, torch.from_numpy(v).cuda(), torch.from_numpy(idx).cuda(), nbins, 0)
-    ws = torch.empty(M.workspace_bytes(M.kernels.scatter_add, args, n), dtype=torch.uint8, device="cuda")
-    M.launch(M.kernels.scatter_add, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
+    ws = torch.empty(M.workspace_bytes(kernel, args, n), dtype=torch.uint8, device="cuda")
+    M.launch(kernel, args, n, stream=torch.cuda.current_stream().cuda_stream, workspace=ws)
     torch.cuda.synchronize()
     want_a, want_h = O.scatter_f64(v, idx, nbins)
     assert np.array_equal(hist.cpu().numpy().view(np.uint32), want_h)
