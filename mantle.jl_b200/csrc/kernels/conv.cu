@@ -2311,120 +2311,6 @@ mtl_status nhwc_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
 
 // gap_fc arguments: logits (B, f32), act (B, bf16 NHWC), w (B, f32,
 // [C][classes]), HW, C, classes (i); ndrange = images.
-// ── the fused form: pooling and FC in one launch ──
-// A cluster of kGfSplit CTAs takes kGfImg images. CTA z of the cluster pools
-// channels [z*C/8, (z+1)*C/8) of those images (16-byte loads, the pixels split
-// into up to eight interleaved groups added in group order), the eight pooled
-// slices meet over distributed shared memory, and then each CTA computes a
-// kGfImg x kGfCls tile of logits over all C channels: every thread 2 images x
-// 4 classes, one fmaf per channel in channel order, the weights streamed
-// through shared memory in kGfK-channel slices. Every sum has one owner and a
-// fixed order, so the result does not depend on timing. Used when C is a
-// multiple of 64 and at most 1024 and the activations are 16-byte aligned.
-constexpr int kGfImg = 16, kGfCls = 128, kGfK = 64, kGfSplit = 8;
-static size_t gf_smem(int c) { return ((size_t)kGfImg * c + (size_t)kGfImg * (c / kGfSplit) + kGfK * kGfCls) * 4; }
-
-__global__ void __cluster_dims__(1, kGfSplit, 1) __launch_bounds__(256)
-    gap_fc_cluster_kernel(const __nv_bfloat16* __restrict__ act, const float* __restrict__ w,
-                          float* __restrict__ logits, int nimg, int hw, int c, int classes, int vec) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) float gsm[];
-  const int cs = c / kGfSplit;                 // channels this CTA pools
-  float* means = gsm;                          // [kGfImg][c]; first the pooling's partial sums
-  float* pooled = gsm + kGfImg * c;            // [kGfImg][cs]
-  float* wch = pooled + kGfImg * cs;           // [kGfK][kGfCls]
-  const int z = (int)cluster.block_rank();
-  const int i0 = blockIdx.x * kGfImg, j0 = blockIdx.y * kGfCls, ch0 = z * cs;
-  pdl_wait();
-  pdl_trigger();
-  // 1. pool this CTA's channel slice of the kGfImg images
-  const int oct = cs / 8, items = kGfImg * oct;
-  const int G = max(1, min(8, 256 / items));
-  for (int idx = threadIdx.x; idx < G * items; idx += blockDim.x) {
-    const int g = idx / items, it = idx - g * items;
-    const int im = it / oct, o = it - im * oct;
-    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (i0 + im < nimg) {
-      const __nv_bfloat16* src = act + (int64_t)(i0 + im) * hw * c + ch0 + 8 * o;
-#pragma unroll 4
-      for (int p = g; p < hw; p += G) {
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)p * c));
-        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[e]));
-          sum[2 * e] += f.x;
-          sum[2 * e + 1] += f.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) means[(g * kGfImg + im) * cs + 8 * o + e] = sum[e];
-  }
-  __syncthreads();
-  const float inv = 1.f / (float)hw;
-  for (int idx = threadIdx.x; idx < kGfImg * cs; idx += blockDim.x) {
-    float t = 0.f;
-    for (int g = 0; g < G; ++g) t += means[g * kGfImg * cs + idx];
-    pooled[idx] = t * inv;
-  }
-  cluster.sync();
-  // 2. every CTA gathers the eight slices into its [image][channel] table
-  for (int idx = threadIdx.x; idx < kGfImg * c; idx += blockDim.x) {
-    const int im = idx / c, ch = idx - im * c;
-    const int q = ch / cs;
-    means[idx] = cluster.map_shared_rank(pooled, q)[im * cs + (ch - q * cs)];
-  }
-  cluster.sync();  // every remote read done: a CTA may leave or overwrite from here
-  // 3. the logits tile
-  const int ti = threadIdx.x / 32, tj = threadIdx.x % 32;
-  float acc[2][4] = {};
-  for (int k0 = 0; k0 < c; k0 += kGfK) {
-    for (int e = threadIdx.x; e < kGfK * kGfCls / 4; e += blockDim.x) {
-      const int kk = e / (kGfCls / 4), jj = 4 * (e % (kGfCls / 4));
-      const float* row = w + (int64_t)(k0 + kk) * classes + j0 + jj;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (vec) {
-        if (j0 + jj < classes) v = *reinterpret_cast<const float4*>(row);
-      } else {
-        if (j0 + jj + 0 < classes) v.x = row[0];
-        if (j0 + jj + 1 < classes) v.y = row[1];
-        if (j0 + jj + 2 < classes) v.z = row[2];
-        if (j0 + jj + 3 < classes) v.w = row[3];
-      }
-      *reinterpret_cast<float4*>(wch + kk * kGfCls + jj) = v;
-    }
-    __syncthreads();
-    const float* m0 = means + (2 * ti) * c + k0;
-    const float* m1 = m0 + c;
-#pragma unroll 8
-    for (int kk = 0; kk < kGfK; ++kk) {
-      const float a0 = m0[kk], a1 = m1[kk];
-      const float4 b = *reinterpret_cast<const float4*>(wch + kk * kGfCls + 4 * tj);
-      acc[0][0] = fmaf(a0, b.x, acc[0][0]);
-      acc[0][1] = fmaf(a0, b.y, acc[0][1]);
-      acc[0][2] = fmaf(a0, b.z, acc[0][2]);
-      acc[0][3] = fmaf(a0, b.w, acc[0][3]);
-      acc[1][0] = fmaf(a1, b.x, acc[1][0]);
-      acc[1][1] = fmaf(a1, b.y, acc[1][1]);
-      acc[1][2] = fmaf(a1, b.z, acc[1][2]);
-      acc[1][3] = fmaf(a1, b.w, acc[1][3]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int im = i0 + 2 * ti + r;
-    if (im >= nimg) continue;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int j = j0 + 4 * tj + q;
-      if (j < classes) logits[(int64_t)im * classes + j] = acc[r][q];
-    }
-  }
-}
-
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes) {
   const int64_t n = la.nd[0], hw = la.a[3].i32, c = la.a[4].i32, k = la.a[5].i32;
   if (la.ndim != 1 || n < 0 || hw <= 0 || c <= 0 || k <= 0) return fail(MTL_ERR_ARGUMENT, "gap_fc: bad sizes");
@@ -2448,18 +2334,6 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
   float* mean = reinterpret_cast<float*>(ws);
   cudaStream_t s = (cudaStream_t)stream;
   const auto* act = reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr);
-  if (c % 64 == 0 && c <= 1024 && (la.a[1].ptr & 15) == 0) {
-    const size_t smem = gf_smem(c);
-    cudaError_t e = cudaFuncSetAttribute(gap_fc_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
-    const int vec = classes % 4 == 0 && (la.a[2].ptr & 15) == 0;
-    const unsigned ty = (unsigned)((classes + kGfCls - 1) / kGfCls);
-    dim3 grid((unsigned)((n + kGfImg - 1) / kGfImg), (ty + kGfSplit - 1) / kGfSplit * kGfSplit);
-    gap_fc_cluster_kernel<<<grid, 256, smem, s>>>(act, reinterpret_cast<const float*>(la.a[2].ptr),
-                                                   reinterpret_cast<float*>(la.a[0].ptr), (int)n, hw, c, classes, vec);
-    e = cudaGetLastError();
-    return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
-  }
   const bool v4 = c % 8 == 0 && (la.a[1].ptr & 15) == 0;
   const int units = v4 ? c / 8 : c / 2;
   const int groups = std::max(1, std::min(kGapMaxGroups, 256 / units));
