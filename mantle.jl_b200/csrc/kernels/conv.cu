@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -1470,6 +1471,435 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * BN) : "memory");
 }
 
+// ── the 4-channel stride-2 stem with its weights in tensor memory (Cout = 64) ──
+// In conv_rows_kernel the MMA's A operand is 128 output pixels and B the 64
+// output channels: an M = 128, N = 64, K = 16 MMA reads 6 KiB of operands from
+// shared memory for 32 cycles of tensor work. Here the roles swap. A is the
+// weights, written once into tensor memory, and B is the overlapping windows
+// of one output row's pixels straight from the stage (N = Wo rounded up to 16,
+// the same 16-byte row stride trick), so an MMA reads only N x 32 bytes of
+// shared memory and does 1.75x the work. A's 128 rows are the 64 filters
+// twice: row 64*s + co holds filter co shifted down by s*stride input rows,
+// over K = (k + stride) input rows of 8 pixels x 4 channels, so one chain of
+// MMAs over those rows computes output rows oh and oh + 1 together. The
+// accumulator then holds channels in TMEM lanes and pixels in columns; the
+// epilogue reads it back in the mma fragment layout (.16x256b) and writes it
+// transposed with stmatrix, one pixel's 8 channels per 16-byte row.
+// Measured on B200 (batch 256, 224 x 224): 108-110 us against 143 us for
+// conv_rows_kernel. What bounds it is issuing the MMAs: a thread issues about
+// one tcgen05.mma per 75 cycles against 56 of tensor work at N = 112, so two
+// issuer warps take alternate row pairs. Roles: warp 0 loads (the weights,
+// then the stages), warps 1 and kPairIssuer2 issue, warps 2 .. kPairEpi + 1
+// write A into tensor memory and then drain the accumulators, the last two
+// warps convert NCHW rows as in conv_rows_kernel.
+constexpr int kPairEpi = 8;  // epilogue warps: kPairGroups per TMEM lane quarter, taking alternate 32-pixel chunks
+constexpr int kPairGroups = kPairEpi / 4;
+constexpr int kPairStg = 2;  // staging chunks of 32 channels x 32 pixels (2 KiB) per epilogue warp
+
+__host__ __device__ inline uint32_t pair_wbytes(const ConvShape& sh) {
+  return ((uint32_t)sh.k * sh.k * 4 * 64 * 2 + 1023) & ~1023u;
+}
+__host__ __device__ inline uint32_t pair_smem_bytes(const ConvShape& sh, int src_c) {
+  return 1024 + pair_wbytes(sh) + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + kPairEpi * kPairStg * 2048 +
+         2 * rows_raw_bytes(sh, src_c) + 256;
+}
+// warps: 0 loads, 1 and kPairIssuer2 issue the MMAs, 2 .. kPairEpi + 1 drain the accumulators, the
+// kPairConv after kPairIssuer2 convert (NCHW input)
+constexpr int kPairConv = 2;  // converter warps (NCHW input), taking alternate rows of a stage
+constexpr int kPairIssuer2 = 2 + kPairEpi;
+constexpr int kPairConv0 = kPairIssuer2 + 1;
+template <int SRC_C>
+constexpr int pair_threads() { return 32 * (kPairConv0 + (SRC_C ? kPairConv : 0)); }
+
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes, from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// tcgen05.mma with the A operand in tensor memory (row m in lane m, two bf16
+// of K per 32-bit column, the lower K index in the low half).
+__device__ __forceinline__ void tc_mma_ta(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_ta_acc(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, 1, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc)
+      : "memory");
+}
+
+// 16 TMEM lanes x 32 columns in the mma accumulator-fragment layout
+// (.16x256b, four 8-column blocks): block g's registers 4g .. 4g + 3 hold
+// (lane t/4, columns 8g + 2(t%4) and + 1) and (lane 8 + t/4, the same columns).
+__device__ __forceinline__ void tmem_ld16x256b_x4(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ uint32_t relu_pack_bf16(uint32_t a, uint32_t b, int relu) {
+  float x0 = __uint_as_float(a), x1 = __uint_as_float(b);
+  if (relu) {
+    x0 = fmaxf(x0, 0.f);
+    x1 = fmaxf(x1, 0.f);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// One 32-pixel chunk of this warp's 32 channels (TMEM lanes from tb, columns
+// = pixels): the two 16-lane halves come back in the fragment layout, so each
+// 8-channel x 8-pixel block is one stmatrix operand (thread t: channel t/4,
+// pixels 2(t%4) and + 1), and stmatrix .trans writes its columns — one pixel's
+// 8 channels, 16 bytes — as rows. The staging rows are 64 bytes (32 channels)
+// with the 64-byte swizzle (16-byte piece c of pixel row p at c ^ ((p >> 1) &
+// 3), which also keeps the eight rows of each block in distinct banks), stored
+// by one TMA box {32, 32, 1} at (c0, p0, orow).
+__device__ __forceinline__ void pair_chunk_store(uint32_t tb, int relu, unsigned char* buf, const CUtensorMap* tmO,
+                                                 int c0, int p0, int orow, int lane) {
+  uint32_t lo[16], hi[16];
+  tmem_ld16x256b_x4(tb, lo);                           // channels 0-15 of the warp
+  tmem_ld16x256b_x4(tb + ((uint32_t)16 << 16), hi);  // channels 16-31
+  tmem_wait_ld();
+  const int i = lane >> 3, r = lane & 7;  // this lane addresses row r of matrix i
+  const uint32_t rowaddr = smem_u32(buf) + (uint32_t)r * 64 + (uint32_t)((i ^ ((r >> 1) & 3)) << 4);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t m0 = relu_pack_bf16(lo[4 * g], lo[4 * g + 1], relu);
+    const uint32_t m1 = relu_pack_bf16(lo[4 * g + 2], lo[4 * g + 3], relu);
+    const uint32_t m2 = relu_pack_bf16(hi[4 * g], hi[4 * g + 1], relu);
+    const uint32_t m3 = relu_pack_bf16(hi[4 * g + 2], hi[4 * g + 3], relu);
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(rowaddr + g * 512),
+                 "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+                 : "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tmO, smem_u32(buf), c0, p0, orow);
+    bulk_commit();
+  }
+}
+
+template <int KT, int SRC_C>  // KT: the filter size when known at compile time, else 0
+__global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
+    conv_rows_pair_kernel(const __grid_constant__ CUtensorMap tmO, const __nv_bfloat16* __restrict__ in,
+                          const __nv_bfloat16* __restrict__ wgt, __nv_bfloat16* __restrict__ out, const ConvShape sh,
+                          int relu) {
+  constexpr int CIN = 4;
+  const int nmma = (sh.wo + 15) & ~15;
+  const uint32_t idesc = idesc_bf16_f32(128, nmma, false, false);
+  const int KR = sh.k + sh.stride;  // input rows under one pair of output rows
+  // TMEM: the two accumulators at columns 0 and 128 (measured: the second at
+  // column 112 instead makes the stem 5 % slower), A from column 256
+  constexpr uint32_t kAcol = 256;
+  extern __shared__ unsigned char psm_raw[];
+  unsigned char* wsm =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* astage = wsm + pair_wbytes(sh);
+  const int S = sh.halo_stages;
+  unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [kPairEpi warps][kPairStg][2 KiB]
+  unsigned char* raw = staging + kPairEpi * kPairStg * 2048;           // SRC_C: [2][raw bytes]
+  const uint32_t raw_bytes = SRC_C ? rows_raw_bytes(sh, SRC_C) : 0;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + 2 * raw_bytes);
+  uint64_t* full = bars;         // [S], S <= 4
+  uint64_t* empty = bars + 4;    // [S]
+  uint64_t* tfull = bars + 8;    // [2]
+  uint64_t* tempty = bars + 11;  // [2]
+  uint64_t* bfull = bars + 14;   // the weights in shared memory
+  uint64_t* afull = bars + 15;   // A in tensor memory
+  uint64_t* raw_full = bars + 16;   // [2]
+  uint64_t* raw_empty = bars + 18;  // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t first = blockIdx.x, step = gridDim.x;
+  const int groups = (sh.ho + kRowsG - 1) / kRowsG;
+  const int64_t units = (int64_t)sh.n * groups;
+  const uint32_t rowbytes = (uint32_t)sh.ws * CIN * 2;
+  const int hrows = sh.stride * (kRowsG - 1) + sh.k;  // input rows of a stage
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&full[i]), SRC_C ? kPairConv : 1);  // the converters, or the producer's load
+      mbar_init(smem_u32(&empty[i]), 2);  // both issuers
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), kPairEpi);
+    }
+    mbar_init(smem_u32(bfull), 1);
+    mbar_init(smem_u32(afull), kPairEpi);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&raw_full[b]), 1);
+      mbar_init(smem_u32(&raw_empty[b]), kPairConv);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the input, the weights (and the output's previous readers) are the last kernel's
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t wbytes = (uint32_t)sh.k * sh.k * CIN * 64 * 2;
+      mbar_expect_tx(smem_u32(bfull), wbytes);
+      bulk_load(smem_u32(wsm), wgt, wbytes, smem_u32(bfull));
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t u = first; u < units; u += step) {
+        const int img = (int)(u / groups);
+        const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+        const int r0 = oh0 * sh.stride - sh.pad;  // input row of stage row 0
+        const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
+        if (SRC_C) {
+          // the stage's rows of each channel plane into raw buffer s (s counts units here)
+          if (!wait_phase(smem_u32(&raw_empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+          const uint32_t fb = smem_u32(&raw_full[s]);
+          const uint32_t plane = (uint32_t)(hi - lo) * sh.w * 2;
+          mbar_expect_tx(fb, plane * SRC_C);
+          for (int c = 0; c < SRC_C; ++c)
+            bulk_load(smem_u32(raw + (size_t)s * raw_bytes + (size_t)c * hrows * sh.w * 2),
+                      in + (((int64_t)img * SRC_C + c) * sh.h + lo) * sh.w, plane, fb);
+          if (++s == 2) {
+            s = 0;
+            ph ^= 1;
+          }
+          continue;
+        }
+        if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+        const uint32_t fb = smem_u32(&full[s]);
+        const uint32_t bytes = (uint32_t)(hi - lo) * rowbytes;
+        mbar_expect_tx(fb, bytes);
+        bulk_load(smem_u32(astage + (size_t)s * sh.halo_stage_bytes + (size_t)(lo - r0) * rowbytes),
+                  in + ((int64_t)img * sh.h + lo) * sh.ws * CIN, bytes, fb);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1 || warp == kPairIssuer2) {
+    // two issuers take alternate row pairs, issuer j into accumulator j
+    // (issuing tcgen05.mma from one thread is the slower side here: about 75
+    // cycles an MMA against 56 of tensor work)
+    const int j = warp == 1 ? 0 : 1;
+    if (lane == 0 && wait_phase(smem_u32(afull), 0, abort, &g_conv_timeouts)) {
+      tc_fence_after();
+      int s = 0, i = 0;
+      uint32_t ph = 0;
+      const uint64_t bdesc = smem_desc_noswizzle(smem_u32(astage), 16, 128);
+      const uint32_t arow = rowbytes >> 4;
+      const uint32_t abase = tmem + kAcol;
+      bool ok = true;
+      for (int64_t u = first; u < units && ok; u += step) {
+        const int img = (int)(u / groups);
+        const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+        if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) break;
+        tc_fence_after();
+        const uint64_t bs = bdesc + (uint64_t)(((uint32_t)s * (uint32_t)sh.halo_stage_bytes) >> 4);
+        bool issued = false;
+        for (int t = 0; t < kRowsG && oh0 + t < sh.ho; t += 2, ++i) {
+          if ((i & 1) != j) continue;
+          const int a = j;
+          if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(a * 128);
+          const int ir0 = (oh0 + t) * sh.stride - sh.pad;  // input row of K row 0 (filter row 0 of row oh0 + t)
+          const int rlo = max(0, -ir0), rhi = min(KR, sh.h - ir0);  // K rows inside the image
+          const uint64_t bt = bs + (uint64_t)(((uint32_t)(sh.stride * t) * rowbytes) >> 4);
+          if (KT > 0 && rlo == 0 && rhi == KT + 2) {
+#pragma unroll
+            for (int r = 0; r < KT + 2; ++r)
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                if (r == 0 && q == 0)
+                  tc_mma_ta(d, abase, bt, idesc, 0);
+                else
+                  tc_mma_ta_acc(d, abase + (uint32_t)(16 * r + 8 * q), bt + r * arow + q * 2, idesc);
+              }
+          } else {
+            uint32_t acc = 0;
+            for (int r = rlo; r < rhi; ++r)
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                tc_mma_ta(d, abase + (uint32_t)(16 * r + 8 * q), bt + r * arow + q * 2, idesc, acc);
+                acc = 1;
+              }
+          }
+          tc_commit(smem_u32(&tfull[a]));
+          issued = true;
+        }
+        if (!ok) break;
+        // both issuers release the stage; one with no pair here (a short last
+        // stage) has nothing in flight on it
+        if (issued)
+          tc_commit(smem_u32(&empty[s]));
+        else
+          mbar_arrive(smem_u32(&empty[s]));
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else if (SRC_C && warp >= kPairConv0) {
+    // ── converters: raw channel-plane rows -> the stage's padded NHWC rows,
+    // converter i taking rows i, i + kPairConv, ... of a stage ──
+    const int half = warp - kPairConv0;
+    int s = 0, rb = 0;
+    uint32_t ph = 0, rph = 0;
+    for (int64_t u = first; u < units; u += step) {
+      const int img = (int)(u / groups);
+      const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+      const int r0 = oh0 * sh.stride - sh.pad;
+      const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
+      (void)img;
+      if (!wait_phase(smem_u32(&raw_full[rb]), rph, abort, &g_conv_timeouts)) break;
+      if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+      const unsigned char* src = raw + (size_t)rb * raw_bytes;
+      unsigned char* dst = astage + (size_t)s * sh.halo_stage_bytes + (size_t)(lo - r0) * rowbytes;
+      const int quads = sh.w / 4;
+      const size_t plane = (size_t)hrows * sh.w * 2;
+      for (int jr = half; jr < hi - lo; jr += kPairConv) {
+        const unsigned char* srow = src + (size_t)jr * sh.w * 2;
+        unsigned char* drow = dst + (size_t)jr * rowbytes;
+        for (int m = lane; m < quads; m += 32) {
+          uint2 pl[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            pl[c] = c < SRC_C ? *reinterpret_cast<const uint2*>(srow + c * plane + (size_t)m * 8) : make_uint2(0, 0);
+          uint2 px[4];
+          px[0] = make_uint2(__byte_perm(pl[0].x, pl[1].x, 0x5410), __byte_perm(pl[2].x, pl[3].x, 0x5410));
+          px[1] = make_uint2(__byte_perm(pl[0].x, pl[1].x, 0x7632), __byte_perm(pl[2].x, pl[3].x, 0x7632));
+          px[2] = make_uint2(__byte_perm(pl[0].y, pl[1].y, 0x5410), __byte_perm(pl[2].y, pl[3].y, 0x5410));
+          px[3] = make_uint2(__byte_perm(pl[0].y, pl[1].y, 0x7632), __byte_perm(pl[2].y, pl[3].y, 0x7632));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint2*>(drow + (size_t)(sh.wpad + 4 * m + i) * 8) = px[i];
+        }
+        if (lane < 2 * sh.wpad) {  // margins: stored pixels 0..wpad-1 and wpad+w..ws-1
+          const int x = lane < sh.wpad ? lane : sh.w + lane;
+          *reinterpret_cast<uint2*>(drow + (size_t)x * 8) = make_uint2(0, 0);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&full[s]));
+        mbar_arrive(smem_u32(&raw_empty[rb]));
+      }
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+      if (++rb == 2) {
+        rb = 0;
+        rph ^= 1;
+      }
+    }
+  } else if (warp >= 2 && warp < 2 + kPairEpi) {
+    // TMEM lanes 32q .. 32q + 31: A rows (and accumulator rows) 64 * srow + co;
+    // epilogue warp group h takes the 32-pixel chunks h, h + kPairGroups, ...
+    const int q = warp & 3, h = (warp - 2) / 4;
+    const int m = 32 * q + lane, srow = m >> 6, co = m & 63;
+    const uint32_t lanes = (uint32_t)(32 * q) << 16;
+    bool ok = wait_phase(smem_u32(bfull), 0, abort, &g_conv_timeouts);
+    if (ok) {
+      // A row m, K row r: column jc holds K elements 2jc and 2jc + 1 (pixel
+      // jc/2 of the window, channels 2(jc&1) and 2(jc&1) + 1) of filter row
+      // r - srow*stride; the two halves write alternate K rows
+      const uint16_t* wl = reinterpret_cast<const uint16_t*>(wsm);  // HWIO [k][k][4][64]
+      for (int r = h; r < KR; r += kPairGroups) {
+        const int fr = r - srow * sh.stride;
+        uint32_t pk[16];
+#pragma unroll
+        for (int jc = 0; jc < 16; ++jc) {
+          const int px = jc >> 1, ch = (jc & 1) * 2;
+          uint32_t v = 0;
+          if (fr >= 0 && fr < sh.k && px < sh.k) {
+            const int e = ((fr * sh.k + px) * CIN + ch) * 64 + co;
+            v = (uint32_t)wl[e] | ((uint32_t)wl[e + 64] << 16);
+          }
+          pk[jc] = v;
+        }
+        tmem_st16(tmem + lanes + kAcol + (uint32_t)(16 * r), pk);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(afull));
+    // ── epilogue: per pair of output rows, this warp's 32 channels of row srow ──
+    unsigned char* my_stage = staging + (warp - 2) * kPairStg * 2048;
+    int sb = 0, i = 0;
+    const int nch = (sh.wo + 31) / 32;  // 32-pixel chunks of a row (at most 4)
+    for (int64_t u = first; u < units && ok; u += step) {
+      const int img = (int)(u / groups);
+      const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
+      for (int t = 0; t < kRowsG && oh0 + t < sh.ho; t += 2, ++i) {
+        const int a = i & 1;
+        if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int oh = oh0 + t + srow;
+        if (oh < sh.ho && h < nch) {
+          const int orow = img * sh.ho + oh;
+          const uint32_t tb = tmem + lanes + (uint32_t)(a * 128);
+          for (int ck = h; ck < nch; ck += kPairGroups) {
+            unsigned char* buf = my_stage + (sb++ % kPairStg) * 2048;
+            if (lane == 0) bulk_wait_read<kPairStg - 1>();
+            __syncwarp();
+            pair_chunk_store(tb + 32 * ck, relu, buf, &tmO, 32 * (q & 1), 32 * ck, orow, lane);
+          }
+          if (sh.owp) {  // this row's margin pixels, this warp's channels (group 0 writes them)
+            if (h == 0) {
+              __nv_bfloat16* p = out + (int64_t)orow * sh.wso * 64 + co;
+              for (int e = 0; e < sh.owp; ++e) {
+                p[(int64_t)e * 64] = __float2bfloat16(0.f);
+                p[(int64_t)(sh.owp + sh.wo + e) * 64] = __float2bfloat16(0.f);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+}
+
 // ── NCHW -> NHWC, channels zero-padded to cpad, wpad zero columns each side ──
 __global__ void nchw_to_nhwc_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int c,
                                     int cpad, int h, int w, int wpad, int64_t n_stored) {
@@ -1596,16 +2026,24 @@ __global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restric
 
 // fc_kernel: a cluster of kFcSplit CTAs computes one 32-image x 256-class tile
 // of logits, CTA z of the cluster summing channels [z*kc, (z+1)*kc) (kc = C/8
-// rounded up to 4). Each thread keeps 4 images x 8 classes in registers over
-// 64-channel slices staged in shared memory; the partial tiles then meet over
-// distributed shared memory, CTA z adding images [4z, 4z+4) of the tile from
-// all eight partials in rank order (so the result does not depend on timing).
+// rounded up to 4, or to 8 with POOL). Each thread keeps 4 images x 8 classes
+// in registers over 64-channel slices staged in shared memory; the partial
+// tiles then meet over distributed shared memory, CTA z adding images [4z,
+// 4z+4) of the tile from all eight partials in rank order (so the result does
+// not depend on timing). POOL: the kernel pools its own slices from the
+// activations instead of reading gap_kernel's means — thread (image t/8,
+// channel octet t%8) adds its 8 channels over the HW pixels in pixel order
+// with 16-byte loads, the weight slice's loads issued first — so pooling and
+// FC are one launch and each image's means are computed by the CTAs that use
+// them (four class blocks each read the 12.8 MB of a batch-256 network once,
+// from L2).
 constexpr int kFcImg = 32, kFcCls = 256, kFcKc = 64, kFcSplit = 8;
 constexpr int kFcSmem = (kFcKc * kFcImg + kFcKc * kFcCls) * 4;  // 72 KiB; the partial tile reuses it
 
+template <bool POOL>
 __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
-    fc_kernel(const float* __restrict__ mean, const float* __restrict__ w, float* __restrict__ logits, int nimg,
-              int c, int classes, int vec) {
+    fc_kernel(const float* __restrict__ mean, const __nv_bfloat16* __restrict__ act, int hw,
+              const float* __restrict__ w, float* __restrict__ logits, int nimg, int c, int classes, int vec) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) float fsm[];
@@ -1614,14 +2052,43 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
   const int i0 = blockIdx.x * kFcImg, j0 = blockIdx.y * kFcCls;
   const int z = (int)cluster.block_rank();
   const int ig = threadIdx.x / 32, jg = threadIdx.x % 32;  // images 4ig..4ig+3; classes 4jg.., 128+4jg..
-  const int kc = (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
+  const int kc = POOL ? (((c + kFcSplit - 1) / kFcSplit) + 7) & ~7 : (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
   const int kbeg = min(c, z * kc), kend = min(c, kbeg + kc);
   float acc[4][8] = {};
   pdl_wait();
   pdl_trigger();
   for (int k0 = kbeg; k0 < kend; k0 += kFcKc) {
     const int kn = min(kFcKc, kend - k0);
-    if (vec) {  // kn, C and classes multiples of 4: whole float4s are in or out of range
+    if (POOL) {  // vec holds; kn, C multiples of 8
+#pragma unroll
+      for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
+        const int e = threadIdx.x + it * 256;
+        const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
+        const float4 v = kk < kn && j0 + jj < classes
+                             ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
+      }
+      const int ii = threadIdx.x >> 3, o = threadIdx.x & 7;
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (i0 + ii < nimg && 8 * o < kn) {
+        const __nv_bfloat16* src = act + (int64_t)(i0 + ii) * hw * c + k0 + 8 * o;
+#pragma unroll 7
+        for (int p = 0; p < hw; ++p) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)p * c));
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[e]));
+            s8[2 * e] += f.x;
+            s8[2 * e + 1] += f.y;
+          }
+        }
+      }
+      const float inv = 1.f / (float)hw;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sm[(8 * o + e) * kFcImg + ii] = s8[e] * inv;
+    } else if (vec) {  // kn, C and classes multiples of 4: whole float4s are in or out of range
       // fixed trip counts, fully unrolled: every load of the slice is in flight at once
 #pragma unroll
       for (int it = 0; it < kFcImg * kFcKc / 4 / 256; ++it) {
@@ -1871,17 +2338,20 @@ static mtl_status make_plane_maps(HaloMaps* maps, const void* in, const ConvShap
 }
 
 // The output as {Cout, Wo, N*Ho} (pixel stride Cout, row stride (Wo + 2*owp)
-// * Cout, starting after the left margin) for TMA stores of {64, 32, 1}.
-static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh) {
+// * Cout, starting after the left margin) for TMA stores of {64, 32, 1} from
+// 128-byte-swizzled staging, or (narrow) of {32, 32, 1} from 64-byte rows
+// with the 64-byte swizzle (conv_rows_pair_kernel).
+static mtl_status make_out_map(CUtensorMap* map, void* out, const ConvShape& sh, bool narrow = false) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return fail(MTL_ERR_CUDA, "conv2d: cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[3] = {(cuuint64_t)sh.cout, (cuuint64_t)sh.wo, (cuuint64_t)sh.n * sh.ho};
   cuuint64_t strides[2] = {(cuuint64_t)sh.cout * 2, (cuuint64_t)sh.wso * sh.cout * 2};
-  cuuint32_t box[3] = {64, 32, 1};
+  cuuint32_t box[3] = {narrow ? 32u : 64u, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   void* base = reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)sh.owp * sh.cout;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MTL_ERR_ARGUMENT, "conv2d: output tensor map rejected (CUresult %d)", (int)r);
   return MTL_OK;
 }
@@ -1898,6 +2368,20 @@ static cudaError_t launch_rows(const CUtensorMap& tw, const CUtensorMap& to, con
   grid = std::max(sh.nblk, grid - grid % sh.nblk);
   return launch_pdl(conv_rows_kernel<CIN, KT, SRC_C>, grid, rows_threads<SRC_C>(), smem, s, tw, to,
                     reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+}
+
+template <int KT, int SRC_C>
+static cudaError_t launch_pair(const CUtensorMap& to, const void* in, const void* w, void* out, const ConvShape& sh,
+                               int relu, int sm_count, cudaStream_t s) {
+  const uint32_t smem = pair_smem_bytes(sh, SRC_C);
+  cudaError_t e =
+      cudaFuncSetAttribute(conv_rows_pair_kernel<KT, SRC_C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t units = (int64_t)sh.n * ((sh.ho + kRowsG - 1) / kRowsG);
+  const int grid = (int)std::min<int64_t>(units, sm_count);
+  return launch_pdl(conv_rows_pair_kernel<KT, SRC_C>, grid, pair_threads<SRC_C>(), smem, s, to,
+                    reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<const __nv_bfloat16*>(w),
+                    reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
 }
 
 template <int BN, bool PH>
@@ -2038,6 +2522,31 @@ static bool rows_plan(ConvShape& sh, int src_c = 0) {
   return true;
 }
 
+// The plan of conv_rows_pair_kernel: the raw-row conditions with Cout = 64
+// (two output rows fill the 128 TMEM lanes) and pad < k (every output row
+// overlaps the image), its own shared-memory budget. MTL_CONV_STEM_PAIR=0
+// turns it off (conv_rows_kernel then runs these shapes).
+static bool pair_plan(ConvShape& sh, int src_c = 0) {
+  const char* env = std::getenv("MTL_CONV_STEM_PAIR");
+  if (env && env[0] == '0') return false;
+  if (sh.cin != 4 || sh.stride != 2 || sh.cout != 64 || sh.pad >= sh.k) return false;
+  if (sh.k > 8 || sh.wpad != sh.pad || sh.wo > 128 || sh.stride * (sh.wo - 1) + 8 > sh.ws) return false;
+  const int64_t rowbytes = (int64_t)sh.ws * sh.cin * 2;
+  if (rowbytes % 16) return false;
+  const int hrows = sh.stride * (kRowsG - 1) + sh.k;
+  // the last stage row's windows of up to 128 pixels: 127 * 16 + 16 * Cin bytes
+  const int64_t stage = (hrows * rowbytes + 127 * 16 + 16 * sh.cin + 1023) & ~int64_t(1023);
+  const int64_t avail = 232448 - 1024 - (int64_t)pair_wbytes(sh) - kPairEpi * kPairStg * 2048 - 256 -
+                        2 * (int64_t)rows_raw_bytes(sh, src_c);
+  const int stages = (int)std::min<int64_t>(4, avail / stage);
+  if (stages < 2) return false;
+  sh.kblocks = 0;
+  sh.halo_stages = stages;
+  sh.halo_stage_bytes = (int)stage;
+  sh.nblk = 1;
+  return true;
+}
+
 // Which A path a convolution takes (and, for the rectangle paths, its tile
 // shape in sh). Rectangles where they keep at least 85 % of the MMA rows busy
 // (wide outputs); flat 128-pixel im2col runs otherwise. The im2col paths need
@@ -2150,6 +2659,15 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   if (am == A_ROWS) {
     CUtensorMap to;
+    ConvShape ps = sh;
+    if (pair_plan(ps)) {
+      if (mtl_status st = make_out_map(&to, out, ps, true)) return st;
+      const void* w = reinterpret_cast<const void*>(la.a[2].ptr);
+      cudaError_t e = ps.k == 7 ? launch_pair<7, 0>(to, in, w, out, ps, relu, la.sm_count, s)
+                                : launch_pair<0, 0>(to, in, w, out, ps, relu, la.sm_count, s);
+      if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+      return MTL_OK;
+    }
     if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
     if (mtl_status st = make_out_map(&to, out, sh)) return st;
     cudaError_t e = sh.k == 7 ? launch_rows<4, 7, 0>(tw, to, in, out, sh, relu, la.sm_count, s)
@@ -2254,10 +2772,26 @@ mtl_status nchwconv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   void* out = reinterpret_cast<void*>(la.a[0].ptr);
   const void* in = reinterpret_cast<const void*>(la.a[1].ptr);
   CUtensorMap tw, to;
-  if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
-  if (mtl_status st = make_out_map(&to, out, sh)) return st;
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
+  ConvShape ps = sh;
+  if (pair_plan(ps, c)) {
+    if (mtl_status st = make_out_map(&to, out, ps, true)) return st;
+    const void* w = reinterpret_cast<const void*>(la.a[2].ptr);
+    if (c == 3)
+      e = ps.k == 7 ? launch_pair<7, 3>(to, in, w, out, ps, relu, la.sm_count, s)
+                    : launch_pair<0, 3>(to, in, w, out, ps, relu, la.sm_count, s);
+    else if (c == 4)
+      e = launch_pair<0, 4>(to, in, w, out, ps, relu, la.sm_count, s);
+    else if (c == 2)
+      e = launch_pair<0, 2>(to, in, w, out, ps, relu, la.sm_count, s);
+    else
+      e = launch_pair<0, 1>(to, in, w, out, ps, relu, la.sm_count, s);
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d_nchw: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
+  if (mtl_status st = make_window_weight_map(&tw, reinterpret_cast<const void*>(la.a[2].ptr), sh)) return st;
+  if (mtl_status st = make_out_map(&to, out, sh)) return st;
   if (c == 3)
     e = sh.k == 7 ? launch_rows<4, 7, 3>(tw, to, in, out, sh, relu, la.sm_count, s)
                   : launch_rows<4, 0, 3>(tw, to, in, out, sh, relu, la.sm_count, s);
@@ -2335,6 +2869,19 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
   cudaStream_t s = (cudaStream_t)stream;
   const auto* act = reinterpret_cast<const __nv_bfloat16*>(la.a[1].ptr);
   const bool v4 = c % 8 == 0 && (la.a[1].ptr & 15) == 0;
+  // float4 loads need C, classes and each CTA's channel range (a multiple of 4
+  // by construction) to keep rows 16-byte aligned
+  const int vec = c % 4 == 0 && classes % 4 == 0 && (la.a[2].ptr & 15) == 0;
+  dim3 grid((unsigned)((n + kFcImg - 1) / kFcImg), (unsigned)((classes + kFcCls - 1) / kFcCls), kFcSplit);
+  const float* w = reinterpret_cast<const float*>(la.a[2].ptr);
+  float* logits = reinterpret_cast<float*>(la.a[0].ptr);
+  const char* env = std::getenv("MTL_GAPFC_FUSED");  // "0": the two-kernel form
+  if (v4 && vec && !(env && env[0] == '0')) {  // pooling inside the FC kernel
+    cudaFuncSetAttribute(fc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
+    fc_kernel<true><<<grid, 256, kFcSmem, s>>>(nullptr, act, hw, w, logits, (int)n, c, classes, 1);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
+  }
   const int units = v4 ? c / 8 : c / 2;
   const int groups = std::max(1, std::min(kGapMaxGroups, 256 / units));
   const size_t gsm = (size_t)groups * c * 4;  // at most 8 x 1536 floats = 48 KiB
@@ -2342,13 +2889,8 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
     gap_kernel<4><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
   else
     gap_kernel<1><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
-  cudaFuncSetAttribute(fc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
-  // float4 loads need C, classes and each CTA's channel range (a multiple of 4
-  // by construction) to keep rows 16-byte aligned
-  const int vec = c % 4 == 0 && classes % 4 == 0 && (la.a[2].ptr & 15) == 0;
-  dim3 grid((unsigned)((n + kFcImg - 1) / kFcImg), (unsigned)((classes + kFcCls - 1) / kFcCls), kFcSplit);
-  fc_kernel<<<grid, 256, kFcSmem, s>>>(mean, reinterpret_cast<const float*>(la.a[2].ptr),
-                                       reinterpret_cast<float*>(la.a[0].ptr), (int)n, c, classes, vec);
+  cudaFuncSetAttribute(fc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
+  fc_kernel<false><<<grid, 256, kFcSmem, s>>>(mean, nullptr, hw, w, logits, (int)n, c, classes, vec);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
 }

@@ -120,8 +120,10 @@ def test_conv_matches_oracle(dev, n, h, w, cin, cout, k, s, relu):
     (4, 2, 40, 300, 64, 7, 2, 3, 3),     # 4-channel window rectangles 4 x 30: output rows wider than 128
     (4, 11, 6, 258, 64, 7, 2, 3, 3),     # 4-channel window, flat runs (3 x 129 outputs: no rectangle fills 85 %)
 ])
-def test_conv_with_stored_margin(dev, cin, n, h, w, cout, k, s, pad, wpad):
+@pytest.mark.parametrize("stem_pair", ["1", "0"])
+def test_conv_with_stored_margin(dev, monkeypatch, stem_pair, cin, n, h, w, cout, k, s, pad, wpad):
     import torch
+    monkeypatch.setenv("MTL_CONV_STEM_PAIR", stem_pair)
     rng = np.random.default_rng(11)
     x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
     x[..., 3:] = 0  # padded channels, as the network stores them
@@ -256,18 +258,25 @@ def test_conv_stride2_halo(dev, n, h, w, cin, cout, owp):
 
 
 # The stem straight from an NCHW input: each stage's channel-plane rows are
-# bulk-copied to shared memory and converted there to padded NHWC rows.
+# bulk-copied to shared memory and converted there to padded NHWC rows. With
+# 64 output channels the weights-in-tensor-memory kernel (two output rows per
+# MMA chain) runs, unless MTL_CONV_STEM_PAIR=0 selects the pixel-row kernel.
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,c,h,w,cout,owp", [
-    (2, 3, 224, 224, 64, 0),   # the network's stem
-    (3, 3, 61, 96, 128, 1),    # odd height (a partial last stage), two column blocks, output margins
-    (5, 1, 40, 48, 64, 0),     # one channel
-    (4, 4, 33, 64, 64, 0),     # four channels (no padding channel)
+@pytest.mark.parametrize("n,c,h,w,cout,owp,k,pad", [
+    (2, 3, 224, 224, 64, 0, 7, 3),   # the network's stem
+    (3, 3, 61, 96, 128, 1, 7, 3),    # odd height (a partial last stage), two column blocks, output margins
+    (3, 3, 61, 96, 64, 1, 7, 3),     # odd output height: the last row pair has one row; output margins
+    (2, 3, 30, 200, 64, 2, 7, 3),    # 100 output columns: the MMA's N (112) runs past the row
+    (5, 1, 40, 48, 64, 0, 7, 3),     # one channel
+    (4, 4, 33, 64, 64, 0, 7, 3),     # four channels (no padding channel)
+    (3, 3, 42, 64, 64, 1, 7, 2),     # even padding: the converter's aligned-word path
 ])
-def test_conv_nchw_matches_oracle(dev, n, c, h, w, cout, owp):
+@pytest.mark.parametrize("stem_pair", ["1", "0"])
+def test_conv_nchw_matches_oracle(dev, monkeypatch, stem_pair, n, c, h, w, cout, owp, k, pad):
     import torch
+    monkeypatch.setenv("MTL_CONV_STEM_PAIR", stem_pair)
     rng = np.random.default_rng(19)
-    k, s, pad = 7, 2, 3
+    s = 2
     x = _rand_bits(rng, (n, c, h, w), nonneg=True)
     wt = _rand_bits(rng, (k, k, 4, cout), scale=float(np.sqrt(2.0 / (k * k * c))))
     wt[:, :, c:] = 0
@@ -359,6 +368,7 @@ def test_cnn_full_batch_sampled_images(dev):
     (3, 5, 64, 10),       # fewer pixels than pixel groups; scalar FC loads
     (2, 3, 6, 12),        # 4-byte GAP loads (C not a multiple of 8)
     (4, 9, 1536, 8),      # the widest C: one pixel group, threads loop over the channel units
+    (5, 49, 96, 1000),    # pooled in the FC kernel with 16-channel slices: two CTAs of each cluster idle
 ])
 def test_gap_fc_matches_oracle(dev, n, hw, c, classes):
     import torch
