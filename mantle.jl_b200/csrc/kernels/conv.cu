@@ -2036,8 +2036,22 @@ __global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restric
 // with 16-byte loads, the weight slice's loads issued first — so pooling and
 // FC are one launch and each image's means are computed by the CTAs that use
 // them (four class blocks each read the 12.8 MB of a batch-256 network once,
-// from L2).
+// from L2). Measured on B200 in the batch-256 CNN the two forms take the same
+// step time within 0.5 %, so the two-kernel form stays the default and
+// MTL_GAPFC_FUSED=1 selects this one.
 constexpr int kFcImg = 32, kFcCls = 256, kFcKc = 64, kFcSplit = 8;
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// d = a * b + d on both 32-bit halves (sm_100 packed FP32)
+__device__ __forceinline__ void fma_f32x2(uint64_t& d, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
 constexpr int kFcSmem = (kFcKc * kFcImg + kFcKc * kFcCls) * 4;  // 72 KiB; the partial tile reuses it
 
 template <bool POOL>
@@ -2054,21 +2068,28 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
   const int ig = threadIdx.x / 32, jg = threadIdx.x % 32;  // images 4ig..4ig+3; classes 4jg.., 128+4jg..
   const int kc = POOL ? (((c + kFcSplit - 1) / kFcSplit) + 7) & ~7 : (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
   const int kbeg = min(c, z * kc), kend = min(c, kbeg + kc);
-  float acc[4][8] = {};
+  uint64_t acc2[4][4];  // images 4ig + r; classes (2q, 2q + 1) of the thread's eight
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc2[r][q] = 0;
+  auto load_w = [&](int k0, int kn) {
+#pragma unroll
+    for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
+      const int e = threadIdx.x + it * 256;
+      const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
+      const float4 v = kk < kn && j0 + jj < classes
+                           ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
+    }
+  };
   pdl_wait();
   pdl_trigger();
   for (int k0 = kbeg; k0 < kend; k0 += kFcKc) {
     const int kn = min(kFcKc, kend - k0);
     if (POOL) {  // vec holds; kn, C multiples of 8
-#pragma unroll
-      for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
-        const int e = threadIdx.x + it * 256;
-        const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
-        const float4 v = kk < kn && j0 + jj < classes
-                             ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
-      }
+      load_w(k0, kn);
       const int ii = threadIdx.x >> 3, o = threadIdx.x & 7;
       float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (i0 + ii < nimg && 8 * o < kn) {
@@ -2101,15 +2122,7 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
         sm[(kk + 2) * kFcImg + ii] = v.z;
         sm[(kk + 3) * kFcImg + ii] = v.w;
       }
-#pragma unroll
-      for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
-        const int e = threadIdx.x + it * 256;
-        const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
-        const float4 v = kk < kn && j0 + jj < classes
-                             ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
-      }
+      load_w(k0, kn);
     } else {
       for (int e = threadIdx.x; e < kFcImg * kFcKc; e += 256) {
         const int ii = e / kFcKc, kk = e % kFcKc;
@@ -2121,20 +2134,30 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
       }
     }
     __syncthreads();
+    // packed f32x2 FMAs (two classes an instruction; each half is an IEEE
+    // fma, so the sums are those of one fmaf per product in channel order)
 #pragma unroll 4
     for (int kk = 0; kk < kFcKc; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(sm + kk * kFcImg + 4 * ig);
       const float4 b0 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 4 * jg);
       const float4 b1 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 128 + 4 * jg);
       const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const uint64_t b2[4] = {pack_f32x2(b0.x, b0.y), pack_f32x2(b0.z, b0.w), pack_f32x2(b1.x, b1.y),
+                              pack_f32x2(b1.z, b1.w)};
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < 4; ++r) {
+        const uint64_t a2 = pack_f32x2(av[r], av[r]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[r][q] = fmaf(av[r], bv[q], acc[r][q]);
+        for (int q = 0; q < 4; ++q) fma_f32x2(acc2[r][q], a2, b2[q]);
+      }
     }
     __syncthreads();
   }
+  float acc[4][8];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack_f32x2(acc2[r][q], acc[r][2 * q], acc[r][2 * q + 1]);
   // the partial tile [image][class] into this CTA's shared memory
   float* part = fsm;
 #pragma unroll
@@ -2875,8 +2898,8 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
   dim3 grid((unsigned)((n + kFcImg - 1) / kFcImg), (unsigned)((classes + kFcCls - 1) / kFcCls), kFcSplit);
   const float* w = reinterpret_cast<const float*>(la.a[2].ptr);
   float* logits = reinterpret_cast<float*>(la.a[0].ptr);
-  const char* env = std::getenv("MTL_GAPFC_FUSED");  // "0": the two-kernel form
-  if (v4 && vec && !(env && env[0] == '0')) {  // pooling inside the FC kernel
+  const char* env = std::getenv("MTL_GAPFC_FUSED");  // "1": pooling inside the FC kernel
+  if (v4 && vec && env && env[0] == '1') {
     cudaFuncSetAttribute(fc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
     fc_kernel<true><<<grid, 256, kFcSmem, s>>>(nullptr, act, hw, w, logits, (int)n, c, classes, 1);
     cudaError_t e = cudaGetLastError();

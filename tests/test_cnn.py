@@ -370,8 +370,10 @@ def test_cnn_full_batch_sampled_images(dev):
     (4, 9, 1536, 8),      # the widest C: one pixel group, threads loop over the channel units
     (5, 49, 96, 1000),    # pooled in the FC kernel with 16-channel slices: two CTAs of each cluster idle
 ])
-def test_gap_fc_matches_oracle(dev, n, hw, c, classes):
+@pytest.mark.parametrize("fused", ["0", "1"])  # two kernels; pooling inside the FC kernel
+def test_gap_fc_matches_oracle(dev, monkeypatch, fused, n, hw, c, classes):
     import torch
+    monkeypatch.setenv("MTL_GAPFC_FUSED", fused)
     rng = np.random.default_rng(13)
     act = _rand_bits(rng, (n, hw, 1, c), nonneg=True)
     w = (rng.standard_normal((c, classes)) * np.sqrt(2.0 / c)).astype(np.float32)
