@@ -120,10 +120,14 @@ std::string source(const EwProgram& p) {
   k += "  const long long stride = (long long)gridDim.x * blockDim.x;\n";
   // Two groups per thread per iteration (g and g + stride): every load of
   // both is issued before any arithmetic, so twice the bytes are in flight.
+  // Loads and stores carry the streaming (evict-first) hint: each byte is
+  // touched once a replay (measured on B200, the eight-op chain at 2^22 over
+  // four copies in turn: 13.6 us a step against 14.0 with default caching;
+  // the hint on the stores alone 14.3, on the loads alone 13.9).
   auto group = [&](const std::string& gi, const std::string& tag) {
     std::string t;
     for (int i = 0; i < nin; ++i)
-      t += "      const float4 v" + tag + std::to_string(i) + " = __ldg(reinterpret_cast<const float4*>(in" +
+      t += "      const float4 v" + tag + std::to_string(i) + " = __ldcs(reinterpret_cast<const float4*>(in" +
            std::to_string(i) + ") + " + gi + ");\n";
     return t;
   };
@@ -137,8 +141,8 @@ std::string source(const EwProgram& p) {
       t += ");\n";
     }
     for (int j = 0; j < nout; ++j)
-      t += "      reinterpret_cast<float4*>(out" + std::to_string(j) + ")[" + gi + "] = w" + tag + std::to_string(j) +
-           ";\n";
+      t += "      __stcs(reinterpret_cast<float4*>(out" + std::to_string(j) + ") + " + gi + ", w" + tag + std::to_string(j) +
+           ");\n";
     return t;
   };
   k += "  long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
