@@ -1486,27 +1486,37 @@ __global__ void __launch_bounds__(rows_threads<SRC_C>(), 1)
 // epilogue reads it back in the mma fragment layout (.16x256b) and writes it
 // transposed with stmatrix, one pixel's 8 channels per 16-byte row.
 // Measured on B200 (batch 256, 224 x 224): 108-110 us against 143 us for
-// conv_rows_kernel. What bounds it is issuing the MMAs: a thread issues about
-// one tcgen05.mma per 75 cycles against 56 of tensor work at N = 112, so two
-// issuer warps take alternate row pairs. Roles: warp 0 loads (the weights,
+// conv_rows_kernel. A clock64 trace per role shows what bounds it: the MMAs
+// themselves, about 105 cycles each (a row pair's 18 complete ~1900 cycles
+// apart) against 56 of nominal tensor work at N = 112, with the two issuers
+// (one thread issues a tcgen05.mma about every 75 cycles) and the epilogue
+// keeping ahead of them. Roles: warp 0 loads (the weights,
 // then the stages), warps 1 and kPairIssuer2 issue, warps 2 .. kPairEpi + 1
 // write A into tensor memory and then drain the accumulators, the last two
 // warps convert NCHW rows as in conv_rows_kernel.
 constexpr int kPairEpi = 8;  // epilogue warps: kPairGroups per TMEM lane quarter, taking alternate 32-pixel chunks
 constexpr int kPairGroups = kPairEpi / 4;
 constexpr int kPairStg = 2;  // staging chunks of 32 channels x 32 pixels (2 KiB) per epilogue warp
+// Converter warps (NCHW input), taking every kPairConv-th row of a stage, and
+// raw-row buffers (each holds one stage's channel-plane rows from its bulk copy
+// until converted). Measured on B200 at batch 256: 2 or 4 converters and 2 or
+// 3 buffers, 108-110 us alike.
+constexpr int kPairConv = 2;
+constexpr int kPairRaw = 2;
 
 __host__ __device__ inline uint32_t pair_wbytes(const ConvShape& sh) {
   return ((uint32_t)sh.k * sh.k * 4 * 64 * 2 + 1023) & ~1023u;
 }
 __host__ __device__ inline uint32_t pair_smem_bytes(const ConvShape& sh, int src_c) {
   return 1024 + pair_wbytes(sh) + (uint32_t)(sh.halo_stages * sh.halo_stage_bytes) + kPairEpi * kPairStg * 2048 +
-         2 * rows_raw_bytes(sh, src_c) + 256;
+         kPairRaw * rows_raw_bytes(sh, src_c) + 256;
 }
 // warps: 0 loads, 1 and kPairIssuer2 issue the MMAs, 2 .. kPairEpi + 1 drain the accumulators, the
 // kPairConv after kPairIssuer2 convert (NCHW input)
-constexpr int kPairConv = 2;  // converter warps (NCHW input), taking alternate rows of a stage
 constexpr int kPairIssuer2 = 2 + kPairEpi;
+// TMEM accumulators in rotation (pair i into i % kPairAcc); 2 and 3 measured
+// alike (108.9 and 108.7-109.1 us), 2 leaves room for rows of 128 pixels
+constexpr int kPairAcc = 2;
 constexpr int kPairConv0 = kPairIssuer2 + 1;
 template <int SRC_C>
 constexpr int pair_threads() { return 32 * (kPairConv0 + (SRC_C ? kPairConv : 0)); }
@@ -1598,27 +1608,28 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
   const int nmma = (sh.wo + 15) & ~15;
   const uint32_t idesc = idesc_bf16_f32(128, nmma, false, false);
   const int KR = sh.k + sh.stride;  // input rows under one pair of output rows
-  // TMEM: the two accumulators at columns 0 and 128 (measured: the second at
-  // column 112 instead makes the stem 5 % slower), A from column 256
-  constexpr uint32_t kAcol = 256;
+  // TMEM: kPairAcc accumulators at columns 0, 128, ... (measured: one at
+  // column 112 instead of 128 makes the stem 5 % slower), A in the last
+  // 16*KR columns (its position does not matter)
+  const uint32_t kAcol = 512 - 16 * (uint32_t)KR;
   extern __shared__ unsigned char psm_raw[];
   unsigned char* wsm =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* astage = wsm + pair_wbytes(sh);
   const int S = sh.halo_stages;
   unsigned char* staging = astage + (size_t)S * sh.halo_stage_bytes;  // [kPairEpi warps][kPairStg][2 KiB]
-  unsigned char* raw = staging + kPairEpi * kPairStg * 2048;           // SRC_C: [2][raw bytes]
+  unsigned char* raw = staging + kPairEpi * kPairStg * 2048;           // SRC_C: [kPairRaw][raw bytes]
   const uint32_t raw_bytes = SRC_C ? rows_raw_bytes(sh, SRC_C) : 0;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + 2 * raw_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kPairRaw * raw_bytes);
   uint64_t* full = bars;         // [S], S <= 4
   uint64_t* empty = bars + 4;    // [S]
-  uint64_t* tfull = bars + 8;    // [2]
-  uint64_t* tempty = bars + 11;  // [2]
+  uint64_t* tfull = bars + 8;    // [kPairAcc]
+  uint64_t* tempty = bars + 11;  // [kPairAcc]
   uint64_t* bfull = bars + 14;   // the weights in shared memory
   uint64_t* afull = bars + 15;   // A in tensor memory
-  uint64_t* raw_full = bars + 16;   // [2]
-  uint64_t* raw_empty = bars + 18;  // [2]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* raw_full = bars + 16;   // [kPairRaw], kPairRaw <= 4
+  uint64_t* raw_empty = bars + 20;  // [kPairRaw]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -1633,13 +1644,13 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
       mbar_init(smem_u32(&full[i]), SRC_C ? kPairConv : 1);  // the converters, or the producer's load
       mbar_init(smem_u32(&empty[i]), 2);  // both issuers
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kPairAcc; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), kPairEpi);
     }
     mbar_init(smem_u32(bfull), 1);
     mbar_init(smem_u32(afull), kPairEpi);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kPairRaw; ++b) {
       mbar_init(smem_u32(&raw_full[b]), 1);
       mbar_init(smem_u32(&raw_empty[b]), kPairConv);
     }
@@ -1681,7 +1692,7 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
           for (int c = 0; c < SRC_C; ++c)
             bulk_load(smem_u32(raw + (size_t)s * raw_bytes + (size_t)c * hrows * sh.w * 2),
                       in + (((int64_t)img * SRC_C + c) * sh.h + lo) * sh.w, plane, fb);
-          if (++s == 2) {
+          if (++s == kPairRaw) {
             s = 0;
             ph ^= 1;
           }
@@ -1700,9 +1711,9 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
       }
     }
   } else if (warp == 1 || warp == kPairIssuer2) {
-    // two issuers take alternate row pairs, issuer j into accumulator j
-    // (issuing tcgen05.mma from one thread is the slower side here: about 75
-    // cycles an MMA against 56 of tensor work)
+    // two issuers take alternate row pairs (issuing tcgen05.mma from one
+    // thread is the slower side here: about 75 cycles an MMA against 56 of
+    // tensor work); pair i goes into accumulator i % kPairAcc
     const int j = warp == 1 ? 0 : 1;
     if (lane == 0 && wait_phase(smem_u32(afull), 0, abort, &g_conv_timeouts)) {
       tc_fence_after();
@@ -1721,8 +1732,8 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
         bool issued = false;
         for (int t = 0; t < kRowsG && oh0 + t < sh.ho; t += 2, ++i) {
           if ((i & 1) != j) continue;
-          const int a = j;
-          if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) {
+          const int a = i % kPairAcc;
+          if (!wait_phase(smem_u32(&tempty[a]), ((i / kPairAcc) & 1) ^ 1, abort, &g_conv_timeouts)) {
             ok = false;
             break;
           }
@@ -1815,7 +1826,7 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
         s = 0;
         ph ^= 1;
       }
-      if (++rb == 2) {
+      if (++rb == kPairRaw) {
         rb = 0;
         rph ^= 1;
       }
@@ -1860,8 +1871,8 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
       const int img = (int)(u / groups);
       const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
       for (int t = 0; t < kRowsG && oh0 + t < sh.ho; t += 2, ++i) {
-        const int a = i & 1;
-        if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) {
+        const int a = i % kPairAcc;
+        if (!wait_phase(smem_u32(&tfull[a]), (i / kPairAcc) & 1, abort, &g_conv_timeouts)) {
           ok = false;
           break;
         }
@@ -2554,13 +2565,15 @@ static bool pair_plan(ConvShape& sh, int src_c = 0) {
   if (env && env[0] == '0') return false;
   if (sh.cin != 4 || sh.stride != 2 || sh.cout != 64 || sh.pad >= sh.k) return false;
   if (sh.k > 8 || sh.wpad != sh.pad || sh.wo > 128 || sh.stride * (sh.wo - 1) + 8 > sh.ws) return false;
+  // TMEM: the accumulators (128 columns apart) and A (16 columns per K row) in 512 columns
+  if ((kPairAcc - 1) * 128 + ((sh.wo + 15) & ~15) + 16 * (sh.k + sh.stride) > 512) return false;
   const int64_t rowbytes = (int64_t)sh.ws * sh.cin * 2;
   if (rowbytes % 16) return false;
   const int hrows = sh.stride * (kRowsG - 1) + sh.k;
   // the last stage row's windows of up to 128 pixels: 127 * 16 + 16 * Cin bytes
   const int64_t stage = (hrows * rowbytes + 127 * 16 + 16 * sh.cin + 1023) & ~int64_t(1023);
   const int64_t avail = 232448 - 1024 - (int64_t)pair_wbytes(sh) - kPairEpi * kPairStg * 2048 - 256 -
-                        2 * (int64_t)rows_raw_bytes(sh, src_c);
+                        kPairRaw * (int64_t)rows_raw_bytes(sh, src_c);
   const int stages = (int)std::min<int64_t>(4, avail / stage);
   if (stages < 2) return false;
   sh.kblocks = 0;
