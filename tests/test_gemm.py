@@ -49,6 +49,8 @@ def test_bf16_rounding_is_nearest_even():
     (3, 200, 264, 72),      # ragged M, N and K
     (1, 1000, 1000, 1000),  # ragged everywhere, N and K multiples of 8 only
     (1, 64, 8, 8),          # smaller than a tile
+    (1, 384, 264, 136),     # a last row tile half past M, a last column tile mostly past N
+    (2, 512, 768, 512),     # several tiles a CTA
 ])
 def test_gemm_matches_oracle(dev, batch, m, n, k):
     w = build_gemm(dev, batch=batch, M=m, N=n, K=k, seed=5)
@@ -87,7 +89,7 @@ def test_gemm_full_size_sampled_rows(dev):
     M.run(w.plan)
     A, B = w.host_operands()
     C = w.C.array().reshape(w.batch, w.M, w.N)
-    for r0 in (0, 95, 4133, 8191):
+    for r0 in (0, 95, 130, 4133, 8191):
         want = O.gemm_bf16(A, B, w.M, w.N, w.K, w.batch, row0=r0, rows=1)
         check(C[:, r0:r0 + 1], want)
 
