@@ -361,6 +361,10 @@ static bool fusable(const mtl_graph* g, const Pass& p) {
   return true;
 }
 
+bool mtl_pass_compilable(const mtl_graph* g, int pid) {
+  return pid >= 0 && pid < (int)g->passes.size() && fusable(g, g->passes[pid]);
+}
+
 // The micro-op program of a run, with resource ids standing in for pointers:
 // it fails when the run exceeds what one fused kernel can hold.
 static bool program_fits(const mtl_graph* g, const std::vector<int>& run) {

@@ -163,6 +163,10 @@ mtl_status ew_build_program(const std::vector<EwMember>& ms, const std::vector<u
 mtl_status ew_launch_single(const KernelDesc* kd, const LaunchArgs& la, void* stream);
 // Whether a built program is within the limits of the fused kernel.
 bool ew_program_fits(const EwProgram& p);
+// Whether pass `pid` of a graph can be run as a compiled elementwise program:
+// one elementwise dispatch over a 1-D range whose arguments are whole declared
+// resources (the passes a fused run may hold).
+bool mtl_pass_compilable(const ::mtl_graph* g, int pid);
 // A program compiled to a straight-line kernel (kernels/ew_compile.cu): compile
 // (cached; outside stream capture) and launch.
 mtl_status ew_compile(const EwProgram& p, void** kernel);

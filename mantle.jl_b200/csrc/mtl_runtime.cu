@@ -257,6 +257,14 @@ static mtl_status capture_dispatch(mtl_plan* pl, const Dispatch& d, cudaGraph_t*
   return capture_graph(pl, dispatch_launcher(pl, d), out);
 }
 
+// Whether scheduled position p runs as one compiled elementwise program: a
+// fused run, or a single elementwise pass (compiled too: the interpreter
+// kernel moves ~1.1 TB/s, the compiled kernel of the same op ~5).
+static bool compiled_step(const mtl_plan* pl, int p) {
+  const auto& st = pl->a.steps[p];
+  return st.size() > 1 || (st.size() == 1 && mtl_pass_compilable(pl->g, st[0]));
+}
+
 // A fused run of elementwise passes (scheduled position p): one program, one
 // kernel. Transients the run keeps in registers are never stored.
 static mtl_status fused_launcher(mtl_plan* pl, int p, Launcher* out) {
@@ -309,7 +317,7 @@ static mtl_status direct_launcher(mtl_plan* pl, const ModeGraph& m, Launcher* ou
   *out = nullptr;
   const mtl_graph* g = pl->g;
   if (pl->a.order.size() != 1 || !g->updates.empty() || pl->o.profile || m.nkernels != 1) return MTL_OK;
-  if (pl->a.steps[0].size() > 1) return fused_launcher(pl, 0, out);
+  if (compiled_step(pl, 0)) return fused_launcher(pl, 0, out);
   const Pass& ps = g->passes[pl->a.order[0]];
   if (ps.kind == MTL_PASS_COMPUTE && ps.dispatches.size() == 1) *out = dispatch_launcher(pl, ps.dispatches[0]);
   return MTL_OK;
@@ -368,7 +376,7 @@ static mtl_status build_mode(mtl_plan* pl, int mode) {
       entry = {ev};
     }
     std::vector<cudaGraphNode_t> body;
-    if (a.steps[p].size() > 1) {
+    if (compiled_step(pl, p)) {
       cudaGraph_t child = nullptr;
       mtl_status st = capture_fused(pl, p, &child);
       if (st) return fail(st, "fused run from \"%s\": %s", ps.name.c_str(), std::string(mtl_last_error()).c_str());
@@ -873,7 +881,7 @@ mtl_status mtl_plan_set_arg(mtl_plan* pl, int32_t pass, int32_t dispatch, int32_
   if (!g->dev) return MTL_OK;
   if (mtl_status s = use_device(g->dev)) return s;
   const int pos = position_of(pl, pass);
-  const bool fused = pos >= 0 && pl->a.steps[pos].size() > 1;
+  const bool fused = pos >= 0 && compiled_step(pl, pos);
   for (auto& m : pl->modes) {
     if (!m.built || pos < 0) continue;
     cudaGraph_t child = nullptr;
