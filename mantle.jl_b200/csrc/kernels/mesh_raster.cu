@@ -341,22 +341,38 @@ __global__ void __launch_bounds__(256) raster_warp_kernel(Scratch s, int W) {
       bound = bk > bound ? bk : bound;
     }
     const bool narrow = bound < (int64_t)INT32_MAX;
-    for (int i = lane; i < area; i += 32) {
-      const int dx = i % bw, dy = i / bw;
-      int64_t ev[3];
-      if (narrow) {
-#pragma unroll
-        for (int k = 0; k < 3; ++k) ev[k] = (int32_t)E0[k] + (int32_t)A[k] * dx + (int32_t)B[k] * dy;
-      } else {
+    // i / bw as a multiply-high (exact for i < 4096 and any bw <= 4096: the
+    // error of the rounded-up reciprocal stays below 2^-20, the gap below the
+    // next integer is at least 1/bw)
+    const uint32_t mag = bw > 1 ? (uint32_t)((0x100000000ull + (uint32_t)bw - 1) / (uint32_t)bw) : 0u;
+    unsigned long long* vrow = s.vis + (int64_t)p.by0 * W + p.bx0;
+    if (narrow) {  // every edge value over the box fits 32 bits
+      const int32_t e0 = (int32_t)E0[0], e1 = (int32_t)E0[1], e2 = (int32_t)E0[2];
+      const int32_t a0 = (int32_t)A[0], a1 = (int32_t)A[1], a2 = (int32_t)A[2];
+      const int32_t b0 = (int32_t)B[0], b1 = (int32_t)B[1], b2 = (int32_t)B[2];
+      for (int i = lane; i < area; i += 32) {
+        const int dy = bw > 1 ? (int)__umulhi((uint32_t)i, mag) : i, dx = i - dy * bw;
+        const int32_t v0 = e0 + a0 * dx + b0 * dy, v1 = e1 + a1 * dx + b1 * dy, v2 = e2 + a2 * dx + b2 * dy;
+        if (v0 < bias[0] || v1 < bias[1] || v2 < bias[2]) continue;
+        const float d = depth_of((float)v0, (float)v1, (float)v2, p.z, inv_s);
+        if (d < 0.f) continue;
+        const unsigned long long k = key_of(d, p.prim);
+        unsigned long long* v = vrow + (int64_t)dy * W + dx;
+        if (k < *v) atomicMin(v, k);
+      }
+    } else {
+      for (int i = lane; i < area; i += 32) {
+        const int dy = bw > 1 ? (int)__umulhi((uint32_t)i, mag) : i, dx = i - dy * bw;
+        int64_t ev[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) ev[k] = E0[k] + A[k] * dx + B[k] * dy;
+        if (ev[0] < bias[0] || ev[1] < bias[1] || ev[2] < bias[2]) continue;
+        const float d = depth_of((float)ev[0], (float)ev[1], (float)ev[2], p.z, inv_s);
+        if (d < 0.f) continue;
+        const unsigned long long k = key_of(d, p.prim);
+        unsigned long long* v = vrow + (int64_t)dy * W + dx;
+        if (k < *v) atomicMin(v, k);
       }
-      if (ev[0] < bias[0] || ev[1] < bias[1] || ev[2] < bias[2]) continue;
-      const float d = depth_of((float)ev[0], (float)ev[1], (float)ev[2], p.z, inv_s);
-      if (d < 0.f) continue;
-      const unsigned long long k = key_of(d, p.prim);
-      unsigned long long* v = s.vis + (int64_t)(p.by0 + dy) * W + (p.bx0 + dx);
-      if (k < *v) atomicMin(v, k);
     }
   }
 }
