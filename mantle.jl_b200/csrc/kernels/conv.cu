@@ -1678,14 +1678,15 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
       bulk_load(smem_u32(wsm), wgt, wbytes, smem_u32(bfull));
       int s = 0;
       uint32_t ph = 0;
-      for (int64_t u = first; u < units; u += step) {
+      int64_t g = 0;  // loads issued (raw buffers with NCHW input, else stages)
+      for (int64_t u = first; u < units; u += step, ++g) {
         const int img = (int)(u / groups);
         const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
         const int r0 = oh0 * sh.stride - sh.pad;  // input row of stage row 0
         const int lo = max(r0, 0), hi = min(r0 + hrows, sh.h);
         if (SRC_C) {
           // the stage's rows of each channel plane into raw buffer s (s counts units here)
-          if (!wait_phase(smem_u32(&raw_empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;
+          if (!wait_phase(smem_u32(&raw_empty[s]), ph ^ 1, abort, &g_conv_timeouts)) break;  // (g not issued)
           const uint32_t fb = smem_u32(&raw_full[s]);
           const uint32_t plane = (uint32_t)(hi - lo) * sh.w * 2;
           mbar_expect_tx(fb, plane * SRC_C);
@@ -1709,6 +1710,13 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
           ph ^= 1;
         }
       }
+      // leaving on an abort: the loads in flight land before the CTA's shared
+      // memory is released (the last kPairRaw or S of them)
+      if (*abort) {
+        const int nb = SRC_C ? kPairRaw : S;
+        for (int64_t q = g > nb ? g - nb : 0; q < g; ++q)
+          drain_phase(smem_u32(SRC_C ? &raw_full[q % nb] : &full[q % nb]), (uint32_t)((q / nb) & 1));
+      }
     }
   } else if (warp == 1 || warp == kPairIssuer2) {
     // two issuers take alternate row pairs (issuing tcgen05.mma from one
@@ -1723,6 +1731,7 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
       const uint32_t arow = rowbytes >> 4;
       const uint32_t abase = tmem + kAcol;
       bool ok = true;
+      int last = -1;  // the last pair whose MMAs this thread committed
       for (int64_t u = first; u < units && ok; u += step) {
         const int img = (int)(u / groups);
         const int oh0 = (int)(u - (int64_t)img * groups) * kRowsG;
@@ -1763,6 +1772,7 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
           }
           tc_commit(smem_u32(&tfull[a]));
           issued = true;
+          last = i;
         }
         if (!ok) break;
         // both issuers release the stage; one with no pair here (a short last
@@ -1776,6 +1786,8 @@ __global__ void __launch_bounds__(pair_threads<SRC_C>(), 1)
           ph ^= 1;
         }
       }
+      // leaving on an abort: this thread's MMAs finish before the TMEM is freed
+      if (*abort && last >= 0) drain_phase(smem_u32(&tfull[last % kPairAcc]), (uint32_t)((last / kPairAcc) & 1));
     }
   } else if (SRC_C && warp >= kPairConv0) {
     // ── converters: raw channel-plane rows -> the stage's padded NHWC rows,
