@@ -20,6 +20,7 @@
 #include <nvrtc.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -145,6 +146,10 @@ std::string source(const EwProgram& p) {
            ");\n";
     return t;
   };
+  // programmatic dependent launch: wait for the previous grid's memory, then
+  // let the next kernel's CTAs take SMs as this grid's finish
+  k += "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+  k += "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
   k += "  long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n";
   k += "  for (; g + stride < groups; g += 2 * stride) {\n";
   k += "    {\n" + group("g", "a") + group("g + stride", "b") + apply("g", "a") + apply("g + stride", "b") +
@@ -239,8 +244,22 @@ mtl_status ew_launch_compiled(void* kernel, const EwProgram& p, void* stream) {
   // together; at 4 blocks an SM and 3-4 iterations a thread, 2^22-element
   // runs took 14.3 us instead of 13.8-14.0), capped at 16 blocks an SM
   const long long blocks = std::max<long long>(1, std::min<long long>((groups + 511) / 512, (long long)sms * 16));
-  cudaError_t e = cudaLaunchKernel((const void*)kernel, dim3((unsigned)blocks), dim3(256), args, 0,
-                                   (cudaStream_t)stream);
+  // launched with programmatic stream serialization (the kernel waits for the
+  // previous grid itself); MTL_NO_PDL=1 launches in plain stream order
+  static const bool no_pdl = [] {
+    const char* v = std::getenv("MTL_NO_PDL");
+    return v && v[0] == '1';
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = no_pdl ? 0 : 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)kernel, args);
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "compiled fused run: %s", cudaGetErrorString(e));
   return MTL_OK;
 }
