@@ -466,6 +466,21 @@ def test_set_arg_reaches_the_next_run(dev):
     M.run(plan2)
     np.testing.assert_allclose(d.array(), a_h * 4 + b_h, rtol=1e-6, atol=1e-7)
 
+    # the same two passes unfused: two compiled kernels, one graph node each;
+    # the scalar is compiled into the first kernel, so set_arg replaces that
+    # node's kernel in both barrier modes' graphs
+    plan3 = M.Plan(g2)
+    for barriers in ("derived", "backend"):
+        d.update(np.zeros(n, np.float32))
+        M.run(plan3, barriers=barriers)
+        assert plan3.nkernels(barriers) == 2
+        np.testing.assert_allclose(d.array(), a_h * 4 + b_h, rtol=1e-6, atol=1e-7)
+    plan3.set_arg(q, 0, 2, -3.0)
+    for barriers in ("derived", "backend"):
+        d.update(np.zeros(n, np.float32))
+        M.run(plan3, barriers=barriers)
+        np.testing.assert_allclose(d.array(), a_h * -3 + b_h, rtol=1e-6, atol=1e-7)
+
 
 def test_disjoint_slices_both_land(dev):
     """test/test_window.jl:391-420: two writes into disjoint halves of one buffer
