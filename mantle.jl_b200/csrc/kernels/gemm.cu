@@ -48,15 +48,29 @@
 
 namespace mtl {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr uint32_t kAStage = kBM * kBK * 2;  // 16 KiB
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr uint32_t kAStage = kBM * kBK * 2;  // 16 KiB: one 128-row run of A
 constexpr uint32_t kBStage = kBK * kBN * 2;  // 32 KiB
-constexpr uint32_t kStageBytes = kAStage + kBStage;
 constexpr int kGemmThreads = 192;
 constexpr int kGroupM = 16;  // tile rows per raster group (MTL_GEMM_GROUP_M overrides it, for tuning)
 constexpr uint32_t kTmemCols = 512;
-// ring + barriers + alignment slack
-constexpr int kGemmSmem = kStages * (int)kStageBytes + 1024 + 1024;
+
+// RUNS 128-row runs of A per tile, sharing each k-block's B. One run: 4
+// stages of 48 KiB and two accumulators, so a tile's epilogue overlaps the
+// next tile's main loop. Two runs (256 x 256 tiles): 3 stages of 64 KiB, the
+// two runs' accumulators filling the 512 TMEM columns, so the epilogue runs
+// between tiles, but each k-block moves 64 KiB for eight MMAs instead of 48
+// KiB for four: a third fewer operand bytes per MAC from L2 and shared
+// memory.
+template <int RUNS>
+struct GemmCfg {
+  static constexpr int kStages = RUNS == 1 ? 4 : 3;
+  static constexpr uint32_t kStageBytes = RUNS * kAStage + kBStage;
+  static constexpr int kAcc = RUNS == 1 ? 2 : 1;  // accumulator sets of RUNS x 256 columns
+  static constexpr int kTileM = kBM * RUNS;
+  // ring + barriers + alignment slack
+  static constexpr int kSmem = kStages * (int)kStageBytes + 1024 + 1024;
+};
 
 __device__ int g_gemm_timeouts;
 
@@ -67,6 +81,7 @@ constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, false, true);
 struct TileCoord {
   int b, m0, n0;
 };
+template <int RUNS>
 __device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tiles_n, int group_m) {
   const int64_t per = (int64_t)tiles_m * tiles_n;
   TileCoord c;
@@ -76,14 +91,18 @@ __device__ __forceinline__ TileCoord tile_coord(int64_t t, int tiles_m, int tile
   const int first_m = group * group_m;
   const int gsize = min(group_m, tiles_m - first_m);
   const int in_group = r % (group_m * tiles_n);
-  c.m0 = (first_m + in_group % gsize) * kBM;
+  c.m0 = (first_m + in_group % gsize) * GemmCfg<RUNS>::kTileM;
   c.n0 = (in_group / gsize) * kBN;
   return c;
 }
 
+template <int RUNS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      float* __restrict__ C, int M, int N, int K, int batch, int stall_cta, int group_m) {
+  using Cfg = GemmCfg<RUNS>;
+  constexpr int kStages = Cfg::kStages, kAcc = Cfg::kAcc;
+  constexpr uint32_t kStageBytes = Cfg::kStageBytes;
   extern __shared__ unsigned char gsm_raw[];
   // 1024-byte alignment: the 128-byte swizzle repeats every 8 rows of 128 B.
   unsigned char* gsm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -91,13 +110,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + kStages * kStageBytes);
   uint64_t* full = bars;                   // [kStages]
   uint64_t* empty = bars + kStages;        // [kStages]
-  uint64_t* tfull = bars + 2 * kStages;    // [2]
-  uint64_t* tempty = bars + 2 * kStages + 2;  // [2]
+  uint64_t* tfull = bars + 2 * kStages;    // [kAcc]
+  uint64_t* tempty = bars + 2 * kStages + 2;  // [kAcc]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
+  const int tiles_m = (M + Cfg::kTileM - 1) / Cfg::kTileM, tiles_n = (N + kBN - 1) / kBN;
   const int64_t ntiles = (int64_t)tiles_m * tiles_n * batch;
   const int kblocks = (K + kBK - 1) / kBK;
 
@@ -106,7 +125,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAcc; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 4);
     }
@@ -131,17 +150,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const TileCoord tc = tile_coord(t, tiles_m, tiles_n, group_m);
+        const TileCoord tc = tile_coord<RUNS>(t, tiles_m, tiles_n, group_m);
+        // runs and B chunks that start past M or N feed only outputs that are
+        // never stored: they are not loaded (a box wholly outside the tensor)
+        const int runs = min(RUNS, (M - tc.m0 + kBM - 1) / kBM);
+        const int nchunks = min(kBN / 64, (N - tc.n0 + 63) / 64);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_gemm_timeouts)) goto producer_done;
           const uint32_t fb = smem_u32(&full[s]);
-          // B chunks that start past N feed only output columns that are never
-          // stored: they are not loaded (a box wholly outside the tensor).
-          const int nchunks = min(kBN / 64, (N - tc.n0 + 63) / 64);
-          mbar_expect_tx(fb, kAStage + (uint32_t)nchunks * (kBK * 128));
+          mbar_expect_tx(fb, (uint32_t)runs * kAStage + (uint32_t)nchunks * (kBK * 128));
           const uint32_t a_dst = smem_u32(ring + s * kStageBytes);
-          const uint32_t b_dst = a_dst + kAStage;
-          tma_load_3d(a_dst, &tmA, kb * kBK, tc.m0, tc.b, fb);
+          const uint32_t b_dst = a_dst + RUNS * kAStage;
+          for (int r = 0; r < runs; ++r) tma_load_3d(a_dst + r * kAStage, &tmA, kb * kBK, tc.m0 + r * kBM, tc.b, fb);
           for (int c = 0; c < nchunks; ++c) tma_load_3d(b_dst + c * (kBK * 128), &tmB, tc.n0 + c * 64, kb * kBK, tc.b, fb);
           if (++s == kStages) {
             s = 0;
@@ -158,8 +178,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t ph = 0;
       int i = 0;
       for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-        const int a = i & 1;
-        if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_gemm_timeouts)) break;
+        const int a = i % kAcc;
+        if (!wait_phase(smem_u32(&tempty[a]), ((i / kAcc) & 1) ^ 1, abort, &g_gemm_timeouts)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * kBN);
         bool ok = true;
@@ -170,19 +190,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(ring + s * kStageBytes);
-          const uint32_t b_addr = a_addr + kAStage;
+          const uint32_t b_addr = a_addr + RUNS * kAStage;
           // A: K-major, rows of 128 B, 8-row groups 1024 B apart (SBO); a K=16
           // slice is 32 B further along the swizzled row.
           // B: N-major, 64-column chunks kBK*128 B apart (LBO), 8-row K groups
           // 1024 B apart (SBO); a K=16 slice is 16 rows = 2048 B further.
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = smem_desc(b_addr + kk * 2048, kBK * 128, 1024);
-            if (kk == 0)
-              tc_mma(d, ad, bd, kIdesc, kb != 0);
-            else
-              tc_mma_acc(d, ad, bd, kIdesc);
+#pragma unroll
+            for (int r = 0; r < RUNS; ++r) {
+              // run r's accumulator: the second 256 columns (two runs)
+              const uint64_t ad = smem_desc(a_addr + r * kAStage + kk * 32, 16, 1024);
+              if (kk == 0)
+                tc_mma(d + (uint32_t)(r * kBN), ad, bd, kIdesc, kb != 0);
+              else
+                tc_mma_acc(d + (uint32_t)(r * kBN), ad, bd, kIdesc);
+            }
           }
           tc_commit(smem_u32(&empty[s]));
           if (++s == kStages) {
@@ -199,29 +223,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     int i = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-      const int a = i & 1;
-      if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_gemm_timeouts)) break;
+      const int a = i % kAcc;
+      if (!wait_phase(smem_u32(&tfull[a]), (i / kAcc) & 1, abort, &g_gemm_timeouts)) break;
       tc_fence_after();
-      const TileCoord tc = tile_coord(t, tiles_m, tiles_n, group_m);
-      const int row = tc.m0 + q * 32 + lane;
-      float* crow = C + ((int64_t)tc.b * M + row) * (int64_t)N;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kBN);
+      const TileCoord tc = tile_coord<RUNS>(t, tiles_m, tiles_n, group_m);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        const int col = tc.n0 + c * 32;
-        if (row < M) {
-          if (col + 32 <= N) {
-            float4* dst = reinterpret_cast<float4*>(crow + col);
+      for (int run = 0; run < RUNS; ++run) {
+        const int row = tc.m0 + run * kBM + q * 32 + lane;
+        float* crow = C + ((int64_t)tc.b * M + row) * (int64_t)N;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((a + run) * kBN);
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          const int col = tc.n0 + c * 32;
+          if (row < M) {
+            if (col + 32 <= N) {
+              float4* dst = reinterpret_cast<float4*>(crow + col);
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-          } else {
+              for (int v = 0; v < 8; ++v)
+                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            } else {
 #pragma unroll
-            for (int v = 0; v < 32; ++v)
-              if (col + v < N) crow[col + v] = __uint_as_float(r[v]);
+              for (int v = 0; v < 32; ++v)
+                if (col + v < N) crow[col + v] = __uint_as_float(r[v]);
+            }
           }
         }
       }
@@ -282,6 +309,16 @@ static int group_m() {
   return g;
 }
 
+// 128-row runs of A per tile: two (256 x 256 tiles) where M has more than
+// one run, unless MTL_GEMM_RUNS=1 (read once).
+static int gemm_runs(int M) {
+  static const bool one = [] {
+    const char* e = std::getenv("MTL_GEMM_RUNS");
+    return e && e[0] == '1';
+  }();
+  return one || M <= kBM ? 1 : 2;
+}
+
 // Host: the bounded waits' limit of this file's kernels on the current device.
 cudaError_t gemm_set_wait_limit(unsigned long long ns) { return set_wait_limit_this_file(ns); }
 
@@ -320,9 +357,9 @@ mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   CUtensorMap ta, tb;
   if (mtl_status st = make_bf16_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, kBM)) return st;
   if (mtl_status st = make_bf16_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, kBK)) return st;
-  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-  if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
-  const int64_t tiles = (int64_t)((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * batch;
+  const int runs = gemm_runs(M);
+  const int tile_m = kBM * runs;
+  const int64_t tiles = (int64_t)((M + tile_m - 1) / tile_m) * ((N + kBN - 1) / kBN) * batch;
   const int grid = (int)std::min<int64_t>(tiles, la.sm_count);
   int stall = -1;
   for (int left = g_gemm_stalls.load(); left > 0;)
@@ -330,8 +367,19 @@ mtl_status gemm_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
       stall = 0;
       break;
     }
-  gemm_bf16_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall, group_m());
-  e = cudaGetLastError();
+  cudaError_t e;
+  if (runs == 2) {
+    e = cudaFuncSetAttribute(gemm_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<2>::kSmem);
+    if (e == cudaSuccess)
+      gemm_bf16_kernel<2><<<grid, kGemmThreads, GemmCfg<2>::kSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall,
+                                                                        group_m());
+  } else {
+    e = cudaFuncSetAttribute(gemm_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<1>::kSmem);
+    if (e == cudaSuccess)
+      gemm_bf16_kernel<1><<<grid, kGemmThreads, GemmCfg<1>::kSmem, s>>>(ta, tb, C, M, N, K, (int)batch, stall,
+                                                                        group_m());
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "gemm: %s", cudaGetErrorString(e));
   return MTL_OK;
 }
