@@ -53,6 +53,7 @@ def test_bf16_rounding_is_nearest_even():
     (1, 64, 8, 8),          # smaller than a tile
     (1, 384, 264, 136),     # a last row tile half past M, a last column tile mostly past N
     (2, 512, 768, 512),     # several tiles a CTA
+    (40, 96, 2048, 128),    # M within one run: 128 x 256 tiles, several a CTA (both accumulators)
 ])
 def test_gemm_matches_oracle(dev, batch, m, n, k):
     w = build_gemm(dev, batch=batch, M=m, N=n, K=k, seed=5)
