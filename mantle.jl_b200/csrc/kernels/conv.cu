@@ -160,7 +160,7 @@ template <int BN, int AM>
 __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kCtasPerSm)
     conv_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                      const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, const ConvShape sh,
-                     int relu) {
+                     int relu, float* __restrict__ part, int ks) {
   using Cfg = ConvCfg<BN, AM>;
   extern __shared__ unsigned char csm_raw[];
   unsigned char* ring =
@@ -177,7 +177,15 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int tiles_m = is_rect(AM) ? sh.n * sh.tiles_x * sh.tiles_y : (int)((sh.mtot + 127) / 128);
   const int tiles_n = sh.cout / BN;
-  const int64_t ntiles = (int64_t)tiles_m * tiles_n;
+  // Work item w: K part w % ks of tile w / ks, K blocks [kb0, kb1) (ks = 1:
+  // the whole tile; the gather mode always runs whole tiles).
+  const int64_t nitems = (int64_t)tiles_m * tiles_n * ks;
+  auto item = [&](int64_t w, int64_t& t, int& kb0, int& kb1) {
+    t = w / ks;
+    const int r = (int)(w - t * ks);
+    kb0 = (int)((int64_t)sh.kblocks * r / ks);
+    kb1 = (int)((int64_t)sh.kblocks * (r + 1) / ks);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kConvStages; ++s) {
@@ -233,8 +241,10 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
       uint32_t ph = 0;
       int64_t loads = 0;
       const int cblocks = sh.cin / 64;
-      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        int m0, n0, img, oh, ow;
+      for (int64_t w = blockIdx.x; w < nitems; w += gridDim.x) {
+        int64_t t;
+        int m0, n0, img, oh, ow, kb0, kb1;
+        item(w, t, kb0, kb1);
         coord(t, m0, n0);
         if (is_rect(AM)) {
           rect_of(m0, img, oh, ow);
@@ -245,8 +255,8 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
           ow = rem - (rem / sh.wo) * sh.wo;
         }
         const int bw = ow * sh.stride - sh.pad + sh.wpad, bh = oh * sh.stride - sh.pad;
-        int tap = 0, cb = 0;
-        for (int kb = 0; kb < sh.kblocks; ++kb) {
+        int tap = kb0 / cblocks, cb = kb0 - (kb0 / cblocks) * cblocks;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_phase(smem_u32(&empty[s]), ph ^ 1, abort, &g_conv_timeouts)) goto w_done;
           const uint32_t fb = smem_u32(&full[s]);
           // rectangles land th*tw rows (the rest of the 128-row tile is unused)
@@ -330,13 +340,16 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
                           : (AM == A_WINDOW4 || AM == A_WINDOW4_RECT) ? smem_desc(ring0, 16, 512, 4)
                                                                        : smem_desc(ring0, 16, 1024);
       const uint64_t b0 = smem_desc(ring0 + kConvA, 64 * 128, 1024);
-      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      for (int64_t w = blockIdx.x; w < nitems; w += gridDim.x, ++i) {
+        int64_t t;
+        int kb0, kb1;
+        item(w, t, kb0, kb1);
         const int a = i & 1;
         if (!wait_phase(smem_u32(&tempty[a]), ((i >> 1) & 1) ^ 1, abort, &g_conv_timeouts)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * BN);
         bool ok = true;
-        for (int kb = 0; kb < sh.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_phase(smem_u32(&full[s]), ph, abort, &g_conv_timeouts)) {
             ok = false;
             break;
@@ -349,7 +362,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
                                 : (AM == A_WINDOW4 || AM == A_WINDOW4_RECT) ? (kk >> 1) * 512 + (kk & 1) * 2
                                                                              : kk * 2;
             if (kk == 0)
-              tc_mma(d, a0 + so + ao, b0 + so, Cfg::kIdesc, kb != 0);
+              tc_mma(d, a0 + so + ao, b0 + so, Cfg::kIdesc, kb != kb0);
             else
               tc_mma_acc(d, a0 + so + ao, b0 + so + kk * 128, Cfg::kIdesc);
           }
@@ -370,7 +383,10 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
     // ── epilogue: ReLU, bf16, NHWC rows ──
     const int q = warp & 3;
     int i = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    for (int64_t w = blockIdx.x; w < nitems; w += gridDim.x, ++i) {
+      int64_t t;
+      int kb0, kb1;
+      item(w, t, kb0, kb1);
       const int a = i & 1;
       if (!wait_phase(smem_u32(&tfull[a]), (i >> 1) & 1, abort, &g_conv_timeouts)) break;
       tc_fence_after();
@@ -394,6 +410,29 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
           y = rem / sh.wo;
           x = rem - y * sh.wo;
         }
+      }
+      if (ks > 1) {
+        // this K part's fp32 sums, unrounded, into its plane (row = output
+        // pixel, in image order); the reduction kernel stores the layer
+        float* prow = part + (w - t * ks) * sh.mtot * sh.cout +
+                      (is_rect(AM) ? ((int64_t)img * sh.ho + y) * sh.wo + x : m) * sh.cout + n0;
+        const uint32_t pbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(pbase + c * 32, r);
+          if (mok) {
+            float4* dst = reinterpret_cast<float4*>(prow + c * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[a]));
+        continue;
       }
       if (is_rect(AM) || sh.owp) m = ((int64_t)img * sh.ho + y) * sh.wso + sh.owp + x;  // stored output pixel
       // the first and last pixel of an output row also zero the row's margins
@@ -429,7 +468,7 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
     uint32_t ph = 0;
     int s_sig = 0;  // next stage to signal
     bool alive = true;
-    for (int64_t t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+    for (int64_t t = blockIdx.x; t < nitems && alive; t += gridDim.x) {  // ks = 1: items are tiles
       int m0, n0;
       coord(t, m0, n0);
       const int64_t m = (int64_t)m0 + g;
@@ -489,6 +528,57 @@ __global__ void __launch_bounds__(ConvCfg<BN, AM>::kThreads, ConvCfg<BN, AM>::kC
   tc_fence_after();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols) : "memory");
+}
+
+// The second kernel of a layer split over K: output pixel m, channels
+// c8..c8+7 = the sum of the ks parts' fp32 planes, added in part order, then
+// ReLU and bf16 rounding as in the epilogues; stored at the pixel's stored
+// position (rows with owp zero margin columns get them written at their ends).
+__global__ void __launch_bounds__(256) conv_splitk_reduce_kernel(const float* __restrict__ part,
+                                                                 __nv_bfloat16* __restrict__ out, const ConvShape sh,
+                                                                 int relu, int ks) {
+  const int g8 = sh.cout / 8;
+  const int64_t groups = sh.mtot * g8, plane = sh.mtot * sh.cout;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = g / g8;
+    const int c8 = (int)(g - m * g8) * 8;
+    const float4* p = reinterpret_cast<const float4*>(part + m * sh.cout + c8);
+    float4 a = __ldcs(p), b = __ldcs(p + 1);
+    for (int r = 1; r < ks; ++r) {
+      const float4* q = reinterpret_cast<const float4*>(part + r * plane + m * sh.cout + c8);
+      const float4 u = __ldcs(q), v = __ldcs(q + 1);
+      a.x += u.x, a.y += u.y, a.z += u.z, a.w += u.w;
+      b.x += v.x, b.y += v.y, b.z += v.z, b.w += v.w;
+    }
+    const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float x0 = f[2 * e], x1 = f[2 * e + 1];
+      if (relu) {
+        x0 = fmaxf(x0, 0.f);
+        x1 = fmaxf(x1, 0.f);
+      }
+      __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+      pk[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    int64_t ms = m;
+    int lmargin = 0, rmargin = 0;
+    if (sh.owp) {
+      const int img = (int)(m / ((int64_t)sh.ho * sh.wo));
+      const int rem = (int)(m - (int64_t)img * sh.ho * sh.wo);
+      const int y = rem / sh.wo, x = rem - (rem / sh.wo) * sh.wo;
+      ms = ((int64_t)img * sh.ho + y) * sh.wso + sh.owp + x;
+      lmargin = x == 0;
+      rmargin = x == sh.wo - 1;
+    }
+    __nv_bfloat16* o = out + ms * sh.cout + c8;
+    *reinterpret_cast<uint4*>(o) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    for (int e = 1; e <= sh.owp; ++e) {
+      if (lmargin) *reinterpret_cast<uint4*>(o - (int64_t)e * sh.cout) = make_uint4(0, 0, 0, 0);
+      if (rmargin) *reinterpret_cast<uint4*>(o + (int64_t)e * sh.cout) = make_uint4(0, 0, 0, 0);
+    }
+  }
 }
 
 // ── two M tiles per CTA over flat im2col runs (A_IM2COL, Cout % 256 == 0) ──
@@ -2346,16 +2436,54 @@ static mtl_status make_window_weight_map(CUtensorMap* map, const void* w, const 
 
 template <int BN, int AM>
 static cudaError_t launch_conv(const CUtensorMap& tw, const CUtensorMap& ta, const void* in, void* out,
-                               const ConvShape& sh, int relu, int sm_count, cudaStream_t s) {
+                               const ConvShape& sh, int relu, int sm_count, cudaStream_t s, float* part = nullptr,
+                               int ks = 1) {
   using Cfg = ConvCfg<BN, AM>;
   cudaError_t e =
       cudaFuncSetAttribute(conv_bf16_kernel<BN, AM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   if (e != cudaSuccess) return e;
+  if (AM == A_GATHER) ks = 1;
   const int64_t mtiles = is_rect(AM) ? (int64_t)sh.n * sh.tiles_x * sh.tiles_y : (sh.mtot + 127) / 128;
-  const int64_t tiles = mtiles * (sh.cout / BN);
-  const int grid = (int)std::min<int64_t>(tiles, (int64_t)sm_count * Cfg::kCtasPerSm);
-  return launch_pdl(conv_bf16_kernel<BN, AM>, grid, Cfg::kThreads, Cfg::kSmem, s, tw, ta,
-                    reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu);
+  const int64_t items = mtiles * (sh.cout / BN) * ks;
+  const int grid = (int)std::min<int64_t>(items, (int64_t)sm_count * Cfg::kCtasPerSm);
+  e = launch_pdl(conv_bf16_kernel<BN, AM>, grid, Cfg::kThreads, Cfg::kSmem, s, tw, ta,
+                 reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), sh, relu, part,
+                 ks);
+  if (e != cudaSuccess || ks == 1) return e;
+  const int64_t groups = sh.mtot * (sh.cout / 8);
+  const int rgrid = (int)std::min<int64_t>((groups + 255) / 256, (int64_t)sm_count * 8);
+  conv_splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(part, reinterpret_cast<__nv_bfloat16*>(out), sh, relu, ks);
+  return cudaGetLastError();
+}
+
+// K parts per tile for a one-run layer with fewer tiles than SMs (1: no
+// split): the largest count, up to 8, that leaves every part at least 4 K
+// blocks and keeps the work items to one round over the SMs. Taken when
+// it is at least three parts and saves more than 28 K blocks a tile: the
+// parts' fp32 planes and the reduction launch cost about 10 us, which only the
+// deep layers win back (measured at batch 32: 7x7x512 layers 38 -> 24 us and
+// 26 -> 22 us with five parts; a 14x14x256 layer with three parts 20 -> 23
+// us; at batch 64 two parts made the 7x7x512 layers slower). Small batches,
+// such as one GPU's share of a batch split over eight, leave most SMs idle on
+// those layers without it. MTL_CONV_SPLITK=0 keeps every layer whole.
+static int conv_split(const ConvShape& sh, int bn, bool rect, int sm_count) {
+  static const bool off = [] {
+    const char* v = std::getenv("MTL_CONV_SPLITK");
+    return v && v[0] == '0';
+  }();
+  const int64_t mtiles = rect ? (int64_t)sh.n * sh.tiles_x * sh.tiles_y : (sh.mtot + 127) / 128;
+  const int64_t tiles = mtiles * (sh.cout / bn);
+  if (off || tiles >= sm_count) return 1;
+  auto cost = [&](int ks) { return (double)((tiles * ks + sm_count - 1) / sm_count) / ks; };
+  int best = 1;
+  for (int ks = 2; ks <= 8 && sh.kblocks / ks >= 4 && tiles * ks <= sm_count; ++ks)  // one round of items
+    if (cost(ks) < cost(best)) best = ks;
+  const double saved = sh.kblocks * (1.0 - cost(best) / cost(1));
+  return best >= 3 && saved > 28.0 ? best : 1;
+}
+
+static uint64_t split_bytes(const ConvShape& sh, int ks) {
+  return ks > 1 ? (uint64_t)ks * (uint64_t)sh.mtot * (uint64_t)sh.cout * 4 : 0;
 }
 
 // The four parity planes of a plain NHWC input for the stride-2 halo path:
@@ -2465,10 +2593,11 @@ static cudaError_t launch_m2(const CUtensorMap& tw, const CUtensorMap& ta, void*
 
 template <int AM>
 static cudaError_t launch_conv_bn(int bn, const CUtensorMap& tw, const CUtensorMap& ta, const void* in, void* out,
-                                  const ConvShape& sh, int relu, int sm_count, cudaStream_t s) {
-  return bn == 256   ? launch_conv<256, AM>(tw, ta, in, out, sh, relu, sm_count, s)
-         : bn == 128 ? launch_conv<128, AM>(tw, ta, in, out, sh, relu, sm_count, s)
-                     : launch_conv<64, AM>(tw, ta, in, out, sh, relu, sm_count, s);
+                                  const ConvShape& sh, int relu, int sm_count, cudaStream_t s, float* part = nullptr,
+                                  int ks = 1) {
+  return bn == 256   ? launch_conv<256, AM>(tw, ta, in, out, sh, relu, sm_count, s, part, ks)
+         : bn == 128 ? launch_conv<128, AM>(tw, ta, in, out, sh, relu, sm_count, s, part, ks)
+                     : launch_conv<64, AM>(tw, ta, in, out, sh, relu, sm_count, s, part, ks);
 }
 
 // The rectangle th x tw (th * tw <= 128 output pixels) that wastes the fewest
@@ -2674,7 +2803,20 @@ static mtl_status make_rect_map(CUtensorMap* map, const void* in, const ConvShap
   return MTL_OK;
 }
 
-mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
+// Scratch of a conv2d_bf16 launch: the K parts' fp32 planes when a one-run
+// layer (flat im2col runs or rectangles) has fewer tiles than SMs and splits
+// its K blocks (conv_split); none otherwise. A launch given less runs whole.
+uint64_t conv_workspace(const LaunchArgs& la) {
+  ConvShape sh = conv_shape(la);
+  if (sh.mtot == 0 || sh.mtot > (int64_t)1 << 31) return 0;
+  const int BN = sh.cout % 256 == 0 ? 256 : sh.cout % 128 == 0 ? 128 : 64;
+  const int am = conv_amode(sh);
+  if (am != A_IM2COL && am != A_RECT) return 0;
+  if (am == A_IM2COL && BN == 256 && m2_pays(sh, la.sm_count)) return 0;
+  return split_bytes(sh, conv_split(sh, BN, am == A_RECT, la.sm_count));
+}
+
+mtl_status conv_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream) {
   ConvShape sh = conv_shape(la);
   if (sh.mtot == 0) return MTL_OK;
   if (sh.mtot > (int64_t)1 << 31) return fail(MTL_ERR_UNSUPPORTED, "conv2d: more than 2^31 output pixels");
@@ -2744,6 +2886,21 @@ mtl_status conv_run(const LaunchArgs& la, void*, uint64_t, void* stream) {
   }
   if (am == A_IM2COL && BN == 256 && m2_pays(sh, la.sm_count)) {
     cudaError_t e = launch_m2(tw, ta, out, sh, relu, la.sm_count, s);
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
+  // a one-run layer with fewer tiles than SMs splits its K blocks when given
+  // the scratch for the parts (conv_workspace)
+  int ks = am == A_IM2COL || am == A_RECT ? conv_split(sh, BN, am == A_RECT, la.sm_count) : 1;
+  if (!ws || ws_bytes < split_bytes(sh, ks) || (reinterpret_cast<uintptr_t>(ws) & 15)) ks = 1;
+  float* part = reinterpret_cast<float*>(ws);
+  if (am == A_IM2COL && ks > 1) {
+    cudaError_t e = launch_conv_bn<A_IM2COL>(BN, tw, ta, in, out, sh, relu, la.sm_count, s, part, ks);
+    if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
+    return MTL_OK;
+  }
+  if (am == A_RECT && ks > 1) {
+    cudaError_t e = launch_conv_bn<A_RECT>(BN, tw, ta, in, out, sh, relu, la.sm_count, s, part, ks);
     if (e != cudaSuccess) return fail(MTL_ERR_CUDA, "conv2d: %s", cudaGetErrorString(e));
     return MTL_OK;
   }

@@ -43,6 +43,7 @@ mtl_status nhwc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* str
 mtl_status gapfc_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 uint64_t gapfc_workspace(const LaunchArgs& la);
+uint64_t conv_workspace(const LaunchArgs& la);
 mtl_status advect_check(const LaunchArgs& la, const uint64_t* bytes);
 mtl_status advect_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* stream);
 mtl_status clear_check(const LaunchArgs& la, const uint64_t* bytes);
@@ -279,7 +280,7 @@ static KernelDesc g_kernels[] = {
     {"gemm_bf16", "BBBiii", false, 0b110, 0b001, gemm_check, nullptr, gemm_run, nullptr},
     // NHWC bf16 convolution (implicit GEMM): out, in, w (HWIO), H, W, Cin, Cout,
     // k, stride, pad, relu, in_wpad, out_wpad; ndrange = images
-    {"conv2d_bf16", "BBBiiiiiiiiii", false, 0b110, 0b001, conv_check, nullptr, conv_run, nullptr},
+    {"conv2d_bf16", "BBBiiiiiiiiii", false, 0b110, 0b001, conv_check, conv_workspace, conv_run, nullptr},
     // the first convolution straight from an NCHW input (C <= 4, stride 2):
     // out, in, w (HWIO, 4 input channels), H, W, C, Cout, k, stride, pad,
     // relu, out_wpad; ndrange = images

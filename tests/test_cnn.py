@@ -180,6 +180,43 @@ def test_conv_margins_and_halo(dev, n, h, w, cin, cout, k, s, pad, wpad, owp):
     assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
 
 
+# A one-run layer with fewer tiles than SMs (a small batch, such as one GPU's
+# share of a batch split over eight) splits each tile's K blocks into parts:
+# fp32 planes in the launch's scratch, added in part order by a second
+# kernel. The same layer given the scratch (split) and not (whole), both
+# against the oracle, margins included.
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,h,w,cin,cout,s,owp", [
+    (8, 7, 7, 512, 512, 1, 0),     # flat im2col runs: 8 tiles, 72 K blocks
+    (8, 14, 14, 256, 512, 2, 1),   # flat runs, stride 2, margins out
+    (6, 14, 14, 256, 256, 1, 1),   # rectangles, margins out
+    (3, 28, 28, 256, 256, 2, 0),   # stride 2, 14 x 14 outputs
+])
+def test_conv_split_k(dev, n, h, w, cin, cout, s, owp):
+    import torch
+    rng = np.random.default_rng(29)
+    k, pad = 3, 1
+    x = _rand_bits(rng, (n, h, w, cin), nonneg=True)
+    wt = _rand_bits(rng, (k, k, cin, cout), scale=float(np.sqrt(2.0 / (k * k * cin))))
+    ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+    xt = torch.from_numpy(x.view(np.int16)).cuda()
+    wtt = torch.from_numpy(wt.view(np.int16)).cuda()
+    ref, _ = O.conv_bf16(x, wt, s, pad, relu=True)
+    st = torch.cuda.current_stream().cuda_stream
+    plane = n * ho * wo * cout * 4
+    for split in (True, False):
+        out = torch.full((n, ho, wo + 2 * owp, cout), -1, dtype=torch.int16, device="cuda")
+        args = (out, xt, wtt, h, w, cin, cout, k, s, pad, 1, 0, owp)
+        need = M.workspace_bytes(M.kernels.conv2d_bf16, args, n)
+        assert need >= 2 * plane and need % plane == 0, need
+        ws = torch.full((need // 4,), float("nan"), dtype=torch.float32, device="cuda") if split else None
+        M.launch(M.kernels.conv2d_bf16, args, n, stream=st, workspace=ws)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy().view(np.uint16)
+        close_layer(got[:, :, owp:owp + wo], ref)
+        assert not got[:, :, :owp].any() and not got[:, :, owp + wo:].any()
+
+
 # Stride-2 halo: a 3x3 stride-2 conv (padding 1) over plain NHWC rows reads
 # the input as four parity planes (tensor maps with pixel and row stride 2).
 # A tile is T output rows; per plane one load brings the frame of plane rows
@@ -345,6 +382,21 @@ def test_cnn_small_batch_matches_oracle(dev):
     assert np.corrcoef(got.ravel(), want.ravel())[0, 1] > 0.9999
     # the activations are transients: the placer aliases them
     assert M.peakbytes(w.plan) < M.naivebytes(w.plan)
+
+
+@pytest.mark.gpu
+def test_cnn_one_gpus_share_of_eight_matches_oracle(dev):
+    # Batch 32, one GPU's share of the batch-256 network on eight: the late
+    # layers split their K blocks; images at both ends and inside, against the
+    # oracle.
+    w = build_cnn(dev, batch=32)
+    M.run(w.plan)
+    x, ws, fc = w.host_params()
+    got = w.logits.array().reshape(32, CNN_CLASSES)
+    images = [0, 13, 31]
+    want = O.cnn_forward(x[images], ws, fc, CNN_LAYERS, STEM_CPAD)
+    for j, i in enumerate(images):
+        assert np.abs(got[i] - want[j]).max() <= 1e-2 * np.abs(want[j]).max(), f"image {i}"
 
 
 @pytest.mark.gpu
