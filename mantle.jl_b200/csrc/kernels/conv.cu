@@ -2092,16 +2092,19 @@ __global__ void nchw_to_nhwc_vec_kernel(const __nv_bfloat16* __restrict__ in, __
 // (below).
 constexpr int kGapMaxGroups = 8;
 
+// blockIdx.y: a slice of cw = c / gridDim.y channels (one slice for large
+// batches; several when the images alone leave SMs idle).
 template <int V>
 __global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restrict__ act, float* __restrict__ mean,
                                                   int hw, int c) {
-  extern __shared__ float part[];  // [G][c]
+  extern __shared__ float part[];  // [G][cw]
   const int img = blockIdx.x;
+  const int cw = c / (int)gridDim.y, c0 = (int)blockIdx.y * cw;
   pdl_wait();
   pdl_trigger();
-  const int units = c / (2 * V);
+  const int units = cw / (2 * V);
   const int G = max(1, min(kGapMaxGroups, (int)blockDim.x / units));
-  const __nv_bfloat16* a = act + (int64_t)img * hw * c;
+  const __nv_bfloat16* a = act + (int64_t)img * hw * c + c0;
   for (int idx = threadIdx.x; idx < G * units; idx += blockDim.x) {
     const int g = idx / units, u = idx - (idx / units) * units;
     float sum[2 * V];
@@ -2126,14 +2129,14 @@ __global__ void __launch_bounds__(256) gap_kernel(const __nv_bfloat16* __restric
       }
     }
 #pragma unroll
-    for (int e = 0; e < 2 * V; ++e) part[g * c + u * 2 * V + e] = sum[e];
+    for (int e = 0; e < 2 * V; ++e) part[g * cw + u * 2 * V + e] = sum[e];
   }
   __syncthreads();
   const float inv = 1.f / (float)hw;
-  for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+  for (int ch = threadIdx.x; ch < cw; ch += blockDim.x) {
     float t = 0.f;
-    for (int g = 0; g < G; ++g) t += part[g * c + ch];
-    mean[(int64_t)img * c + ch] = t * inv;
+    for (int g = 0; g < G; ++g) t += part[g * cw + ch];
+    mean[(int64_t)img * c + c0 + ch] = t * inv;
   }
 }
 
@@ -2167,34 +2170,39 @@ __device__ __forceinline__ void fma_f32x2(uint64_t& d, uint64_t a, uint64_t b) {
 }
 constexpr int kFcSmem = (kFcKc * kFcImg + kFcKc * kFcCls) * 4;  // 72 KiB; the partial tile reuses it
 
-template <bool POOL>
+// CLS: classes per tile, 256 (the thread's eight classes 4jg.., 128+4jg..) or
+// 64 for small batches (the thread's two classes 2jg, 2jg + 1: four times the
+// CTAs over the same work). Each logit is summed in the same order either way.
+template <bool POOL, int CLS = kFcCls>
 __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
     fc_kernel(const float* __restrict__ mean, const __nv_bfloat16* __restrict__ act, int hw,
               const float* __restrict__ w, float* __restrict__ logits, int nimg, int c, int classes, int vec) {
+  static_assert(CLS == 256 || (CLS == 64 && !POOL), "class tiles of 256, or 64 without pooling");
+  constexpr int NQ = CLS / 64;  // class pairs a thread
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) float fsm[];
   float* sm = fsm;                   // [k][image]
   float* sw = fsm + kFcKc * kFcImg;  // [k][class]
-  const int i0 = blockIdx.x * kFcImg, j0 = blockIdx.y * kFcCls;
+  const int i0 = blockIdx.x * kFcImg, j0 = blockIdx.y * CLS;
   const int z = (int)cluster.block_rank();
-  const int ig = threadIdx.x / 32, jg = threadIdx.x % 32;  // images 4ig..4ig+3; classes 4jg.., 128+4jg..
+  const int ig = threadIdx.x / 32, jg = threadIdx.x % 32;  // images 4ig..4ig+3; classes as above
   const int kc = POOL ? (((c + kFcSplit - 1) / kFcSplit) + 7) & ~7 : (((c + kFcSplit - 1) / kFcSplit) + 3) & ~3;
   const int kbeg = min(c, z * kc), kend = min(c, kbeg + kc);
-  uint64_t acc2[4][4];  // images 4ig + r; classes (2q, 2q + 1) of the thread's eight
+  uint64_t acc2[4][NQ];  // images 4ig + r; class pairs of the thread
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc2[r][q] = 0;
+    for (int q = 0; q < NQ; ++q) acc2[r][q] = 0;
   auto load_w = [&](int k0, int kn) {
 #pragma unroll
-    for (int it = 0; it < kFcKc * kFcCls / 4 / 256; ++it) {
+    for (int it = 0; it < kFcKc * CLS / 4 / 256; ++it) {
       const int e = threadIdx.x + it * 256;
-      const int kk = e / (kFcCls / 4), jj = 4 * (e % (kFcCls / 4));
+      const int kk = e / (CLS / 4), jj = 4 * (e % (CLS / 4));
       const float4 v = kk < kn && j0 + jj < classes
                            ? *reinterpret_cast<const float4*>(w + (int64_t)(k0 + kk) * classes + j0 + jj)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(sw + kk * kFcCls + jj) = v;
+      *reinterpret_cast<float4*>(sw + kk * CLS + jj) = v;
     }
   };
   pdl_wait();
@@ -2241,9 +2249,9 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
         const int ii = e / kFcKc, kk = e % kFcKc;
         sm[kk * kFcImg + ii] = i0 + ii < nimg && kk < kn ? mean[(int64_t)(i0 + ii) * c + k0 + kk] : 0.f;
       }
-      for (int e = threadIdx.x; e < kFcKc * kFcCls; e += 256) {
-        const int kk = e / kFcCls, jj = e % kFcCls;
-        sw[kk * kFcCls + jj] = kk < kn && j0 + jj < classes ? w[(int64_t)(k0 + kk) * classes + j0 + jj] : 0.f;
+      for (int e = threadIdx.x; e < kFcKc * CLS; e += 256) {
+        const int kk = e / CLS, jj = e % CLS;
+        sw[kk * CLS + jj] = kk < kn && j0 + jj < classes ? w[(int64_t)(k0 + kk) * classes + j0 + jj] : 0.f;
       }
     }
     __syncthreads();
@@ -2252,47 +2260,60 @@ __global__ void __cluster_dims__(1, 1, kFcSplit) __launch_bounds__(256)
 #pragma unroll 4
     for (int kk = 0; kk < kFcKc; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(sm + kk * kFcImg + 4 * ig);
-      const float4 b0 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 4 * jg);
-      const float4 b1 = *reinterpret_cast<const float4*>(sw + kk * kFcCls + 128 + 4 * jg);
+      uint64_t b2[NQ];
+      if constexpr (CLS == 256) {
+        const float4 b0 = *reinterpret_cast<const float4*>(sw + kk * CLS + 4 * jg);
+        const float4 b1 = *reinterpret_cast<const float4*>(sw + kk * CLS + 128 + 4 * jg);
+        b2[0] = pack_f32x2(b0.x, b0.y);
+        b2[1] = pack_f32x2(b0.z, b0.w);
+        b2[2] = pack_f32x2(b1.x, b1.y);
+        b2[3] = pack_f32x2(b1.z, b1.w);
+      } else {
+        const float2 b = *reinterpret_cast<const float2*>(sw + kk * CLS + 2 * jg);
+        b2[0] = pack_f32x2(b.x, b.y);
+      }
       const float av[4] = {a.x, a.y, a.z, a.w};
-      const uint64_t b2[4] = {pack_f32x2(b0.x, b0.y), pack_f32x2(b0.z, b0.w), pack_f32x2(b1.x, b1.y),
-                              pack_f32x2(b1.z, b1.w)};
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const uint64_t a2 = pack_f32x2(av[r], av[r]);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) fma_f32x2(acc2[r][q], a2, b2[q]);
+        for (int q = 0; q < NQ; ++q) fma_f32x2(acc2[r][q], a2, b2[q]);
       }
     }
     __syncthreads();
   }
-  float acc[4][8];
+  float acc[4][2 * NQ];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) unpack_f32x2(acc2[r][q], acc[r][2 * q], acc[r][2 * q + 1]);
+    for (int q = 0; q < NQ; ++q) unpack_f32x2(acc2[r][q], acc[r][2 * q], acc[r][2 * q + 1]);
   // the partial tile [image][class] into this CTA's shared memory
   float* part = fsm;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    float* row = part + (4 * ig + r) * kFcCls;
-    *reinterpret_cast<float4*>(row + 4 * jg) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-    *reinterpret_cast<float4*>(row + 128 + 4 * jg) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+    float* row = part + (4 * ig + r) * CLS;
+    if constexpr (CLS == 256) {
+      *reinterpret_cast<float4*>(row + 4 * jg) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      *reinterpret_cast<float4*>(row + 128 + 4 * jg) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+    } else {
+      *reinterpret_cast<float2*>(row + 2 * jg) = make_float2(acc[r][0], acc[r][1]);
+    }
   }
   cluster.sync();
-  // all 32 remote loads of a thread in flight before the in-order sums
-  float pv[4][kFcSplit];
+  // all of a thread's remote loads in flight before the in-order sums
+  constexpr int kOut = 4 * CLS / 256;  // outputs a thread: CTA z adds images [4z, 4z + 4) of the tile
+  float pv[kOut][kFcSplit];
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {
+  for (int it = 0; it < kOut; ++it) {
     const int e = threadIdx.x + it * 256;
-    const int ii = 4 * z + e / kFcCls, jj = e % kFcCls;
+    const int ii = 4 * z + e / CLS, jj = e % CLS;
 #pragma unroll
-    for (int rk = 0; rk < kFcSplit; ++rk) pv[it][rk] = cluster.map_shared_rank(part, rk)[ii * kFcCls + jj];
+    for (int rk = 0; rk < kFcSplit; ++rk) pv[it][rk] = cluster.map_shared_rank(part, rk)[ii * CLS + jj];
   }
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {
+  for (int it = 0; it < kOut; ++it) {
     const int e = threadIdx.x + it * 256;
-    const int ii = 4 * z + e / kFcCls, jj = e % kFcCls;
+    const int ii = 4 * z + e / CLS, jj = e % CLS;
     float sum = 0.f;
 #pragma unroll
     for (int rk = 0; rk < kFcSplit; ++rk) sum += pv[it][rk];
@@ -3087,15 +3108,34 @@ mtl_status gapfc_run(const LaunchArgs& la, void* ws, uint64_t ws_bytes, void* st
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
   }
-  const int units = v4 ? c / 8 : c / 2;
+  // channel slices per image while the images alone fill under two CTAs an
+  // SM (each slice a whole number of units and at least 64 channels); batch
+  // sizes that fill the SMs keep one slice
+  const int unit = v4 ? 8 : 2;
+  int slices = 1;
+  while (slices < 8 && n * slices * 2 <= 2 * (int64_t)la.sm_count && c % (2 * slices * unit) == 0 &&
+         c / (2 * slices) >= 64)
+    slices *= 2;
+  const int cw = c / slices;
+  const int units = cw / unit;
   const int groups = std::max(1, std::min(kGapMaxGroups, 256 / units));
-  const size_t gsm = (size_t)groups * c * 4;  // at most 8 x 1536 floats = 48 KiB
+  const size_t gsm = (size_t)groups * cw * 4;  // at most 8 x 1536 floats = 48 KiB
+  const dim3 ggrid((unsigned)n, (unsigned)slices);
   if (v4)
-    gap_kernel<4><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
+    gap_kernel<4><<<ggrid, 256, gsm, s>>>(act, mean, hw, c);
   else
-    gap_kernel<1><<<(unsigned)n, 256, gsm, s>>>(act, mean, hw, c);
-  cudaFuncSetAttribute(fc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
-  fc_kernel<false><<<grid, 256, kFcSmem, s>>>(mean, nullptr, hw, w, logits, (int)n, c, classes, vec);
+    gap_kernel<1><<<ggrid, 256, gsm, s>>>(act, mean, hw, c);
+  // a batch whose 32-image x 256-class clusters fill under the SMs takes
+  // 64-class tiles: four times the CTAs, each a quarter of the work
+  if ((int64_t)grid.x * grid.y * kFcSplit < la.sm_count) {
+    constexpr int kSmall = (kFcKc * kFcImg + kFcKc * 64) * 4;
+    const dim3 g64(grid.x, (unsigned)((classes + 63) / 64), kFcSplit);
+    cudaFuncSetAttribute(fc_kernel<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall);
+    fc_kernel<false, 64><<<g64, 256, kSmall, s>>>(mean, nullptr, hw, w, logits, (int)n, c, classes, vec);
+  } else {
+    cudaFuncSetAttribute(fc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFcSmem);
+    fc_kernel<false><<<grid, 256, kFcSmem, s>>>(mean, nullptr, hw, w, logits, (int)n, c, classes, vec);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MTL_OK : fail(MTL_ERR_CUDA, "gap_fc: %s", cudaGetErrorString(e));
 }
